@@ -1,0 +1,346 @@
+#!/usr/bin/env python
+"""Batch-1 greedy decode throughput of the Qwen3-1.7B-shape int8 model on B200 (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one decode token: one replay of the CUDA graph that holds the native decode step (141 kernels for
+28 layers). Workload = BASELINE config 2: random-init weights (seed 0), int8 per-row weights with bf16 scales,
+a 32-token uniform prompt, then 256 greedy tokens; the timed loop replays that 256-token window (position reset
+to 32 every 256 steps), so contexts run 33..288 as in the config. The 1.72 GB of weights streamed per token are
+far larger than L2 (126 MB), so no flush is needed between steps.
+
+Printed JSON line (rank 0):
+  value        decode tok/s over all ranks, device-timed (CUDA events around the K replays, max over ranks)
+  e2e          the same metric through GraphGreedyDecoder.generate with a pinned host prompt: H2D prompt copy,
+               per-token D2H token reads, (n - 1) / (total - ttft) as research/realmodel/bench_int8.py
+  step_roofline  algorithmic bytes per token (weights + scales + norms + embedding row + KV at each step's
+               context) / step time, against the measured HBM copy bandwidth
+  roofline     the dominant kernel (gemv_i8_tma_kernel): the step's 113 GEMV launches replayed alone as one
+               PDL-chained graph, algorithmic bytes / time; traffic from the committed ncu summary
+  cpu_baseline the reference's CPU path (oracle/torch_ref.py) on this host's cores, bounded sample
+With N > 1 every rank runs an independent replica (no collective on the data path; scaling "weak").
+"""
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = 'batch-1 decode tok/s and % of HBM roofline, Qwen3-1.7B-shape int8, 1 B200'
+PROMPT_LEN, NEW_TOKENS = 32, 256
+FALLBACK_PEAKS = {'hbm_gbs': 6650.0}
+PROFILE_SUMMARY = ROOT / 'profiles' / 'gemv_i8_tma_kernel_qwen3_1p7b.md'
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=2048)
+    ap.add_argument('--warmup', type=int, default=16)
+    ap.add_argument('--impl', choices=['ours', 'reference'], default='ours')
+    ap.add_argument('--no-e2e', action='store_true')
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-pdl', action='store_true')
+    ap.add_argument('--cpu-sample', type=int, default=3, help='timed CPU decode tokens (after one warm-up token)')
+    a = ap.parse_args()
+    if a.warmup < 3:
+        ap.error('--warmup must be >= 3')
+    return a
+
+
+def dist_setup():
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=torch.device('cuda', local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device='cuda')
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def measured_peaks():
+    p = ROOT / 'MEASURED_PEAKS.json'
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, 'measured'
+    return FALLBACK_PEAKS, 'fallback'
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms while the timed region runs."""
+    Q = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
+         'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,'
+         'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self):
+        self.proc = None
+        self.out = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.Q}', '--format=csv,noheader,nounits',
+                                          '-lms', '100'], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self, gpu_index):
+        if self.proc is None:
+            return None
+        time.sleep(0.05)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], None, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(',')]
+            if len(f) < 9 or f[0] != str(gpu_index):
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == 'active':
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': smax, 'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+def profile_traffic():
+    """dram bytes read+write per launch of the dominant kernel, from the committed ncu summary (or None)."""
+    if not PROFILE_SUMMARY.exists():
+        return None
+    m = re.search(r'traffic_bytes_per_step_gemv\s*[:=]\s*([0-9.eE+]+)', PROFILE_SUMMARY.read_text())
+    return float(m.group(1)) if m else None
+
+
+def build(device, pdl):
+    from efficientgpt_b200.configs import qwen3_1p7b_config, random_model
+    from efficientgpt_b200.fast_decode import GraphGreedyDecoder
+    from efficientgpt_b200.int8_linear import quantize_model
+    model = random_model(qwen3_1p7b_config(), device, seed=0)
+    quantize_model(model, scale_dtype=torch.bfloat16)
+    torch.cuda.empty_cache()
+    dec = GraphGreedyDecoder(model, max_cache_len=PROMPT_LEN + NEW_TOKENS, pdl=pdl)
+    prompt = torch.randint(0, model.config.vocab_size, (1, PROMPT_LEN), generator=torch.Generator().manual_seed(0))
+    return model, dec, prompt
+
+
+def gemv_chain_graph(eng):
+    """A graph with only the step's GEMV launches (same shapes, weights and buffers, PDL-chained)."""
+    from efficientgpt_b200 import _lib as L, ops
+    H, I = eng.hidden, eng.inter
+    x_h = eng.h.view(1, H)
+    qkv = eng.qkv.view(1, -1)
+    attn = eng.attn.view(1, -1)
+    act = eng.act.view(1, I)
+
+    def chain():
+        for lay in eng.layers:
+            ops.gemv_i8(x_h, lay['w_qkv'], lay['s_qkv'], out=qkv, norm_w=lay['ln_in'], eps=eng.eps, pdl=True)
+            ops.gemv_i8(attn, lay['w_o'], lay['s_o'], epilogue=L.EPI_RESIDUAL, residual=x_h, pdl=True)
+            ops.gemv_i8(x_h, lay['w_gu'], lay['s_gu'], out=act, epilogue=L.EPI_SILU_MUL, norm_w=lay['ln_post'],
+                        eps=eng.eps, pdl=True)
+            ops.gemv_i8(act, lay['w_down'], lay['s_down'], epilogue=L.EPI_RESIDUAL, residual=x_h, pdl=True)
+        ops.lm_head_argmax(eng.h, eng.w_lm, eng.s_lm, eng.lm_ws, norm_w=eng.final_norm, eps=eng.eps, token=eng.token,
+                           pdl=True)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            chain()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        chain()
+    nbytes = 0
+    for lay in eng.layers:
+        for w, s_ in (('w_qkv', 's_qkv'), ('w_o', 's_o'), ('w_gu', 's_gu'), ('w_down', 's_down')):
+            n, k = lay[w].shape
+            nbytes += n * k + n * lay[s_].element_size() + 2 * k + 2 * n
+        nbytes += 2 * lay['ln_in'].numel() + 2 * lay['ln_post'].numel() + 2 * H + 2 * H  # norm weights, residual rw
+    nbytes += eng.w_lm.numel() + eng.s_lm.numel() * eng.s_lm.element_size() + 2 * H * 2
+    return g, nbytes, 4 * len(eng.layers) + 1
+
+
+def time_replays(graph, k, reset=None):
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for i in range(k):
+        if reset is not None and i and i % NEW_TOKENS == 0:
+            reset()
+        graph.replay()
+    e1.record(st)
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def cpu_baseline(dec, n_tokens):
+    """The reference's CPU decode path (oracle/torch_ref.py) on this host: 1 warm-up + n_tokens timed steps at
+    the contexts right after the 32-token prompt (KV of the prompt copied from the GPU prefill)."""
+    from oracle.torch_ref import TorchCpuQwen3
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    eng = dec.engine
+    cpu = TorchCpuQwen3(eng, PROMPT_LEN + n_tokens + 2)
+    cpu.k[:, 0, :, :PROMPT_LEN] = eng.kv[:, 0, :, :PROMPT_LEN].cpu()
+    cpu.v[:, 0, :, :PROMPT_LEN] = eng.kv[:, 1, :, :PROMPT_LEN].cpu()
+    tok = int(eng.token)
+    tok = cpu.step(tok, PROMPT_LEN)
+    t0 = time.perf_counter()
+    for i in range(n_tokens):
+        tok = cpu.step(tok, PROMPT_LEN + 1 + i)
+    dt = time.perf_counter() - t0
+    return {'value': n_tokens / dt, 'unit': 'tok/s', 'cores': threads, 'kind': 'port',
+            'sample': f'{n_tokens} decode tokens (after 1 warm-up token) of the same Qwen3-1.7B-shape int8 model at '
+                      f'context {PROMPT_LEN + 2}..{PROMPT_LEN + 1 + n_tokens}, torch CPU ops, '
+                      f'bf16((x.float() @ q.float().T) * s) per linear'}
+
+
+def run_reference(a, world, rank):
+    if rank != 0:
+        return
+    _, dec, _ = build('cuda', pdl=True)
+    dec.engine.prefill(torch.randint(0, dec.engine.vocab, (1, PROMPT_LEN),
+                                     generator=torch.Generator().manual_seed(0)).cuda())
+    n = max(1, min(a.steps, a.cpu_sample))
+    cb = cpu_baseline(dec, n)
+    line = {'impl': 'reference', 'metric': METRIC, 'value': cb['value'], 'unit': 'tok/s', 'n_gpus': a.gpus,
+            'steps': n, 'warmup': 1, 'ms_per_step': 1e3 / cb['value'], 'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': None, 'dtype': 'int8-weight/bf16', 'data': 'synthetic',
+            'config': {'workload': 'qwen3_1.7b int8 decode, BASELINE config 2 (CPU port of the reference path)',
+                       'prompt': PROMPT_LEN, 'new_tokens': NEW_TOKENS, 'scale_dtype': 'bf16'},
+            'cpu_baseline': cb, 'e2e': {'value': cb['value'], 'unit': 'tok/s', 'h2d_bytes_per_step': 0,
+                                        'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse()
+    world, rank, local = dist_setup()
+    if a.impl == 'reference':
+        run_reference(a, world, rank)
+        return
+    model, dec, prompt = build('cuda', pdl=not a.no_pdl)
+    eng = dec.engine
+    dec._capture()
+    eng.prefill(prompt.cuda())
+
+    def reset():
+        eng.position.fill_(PROMPT_LEN)
+
+    # warm-up, then the timed region: K replays of the graph (one token each)
+    time_replays(dec.graph, a.warmup)
+    reset()
+    barrier(world)
+    torch.cuda.synchronize()
+    sampler = ClockSampler()
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+    ms = time_replays(dec.graph, a.steps, reset)
+    clocks = sampler.stop(local) if rank == 0 else None
+    ms = max_over_ranks(ms, world)
+    barrier(world)
+    tok_s = a.steps / (ms / 1e3) * world
+
+    # algorithmic bytes per token over the timed window
+    ctxs = [PROMPT_LEN + 1 + (i % NEW_TOKENS) for i in range(a.steps)]
+    kv_mean = statistics.fmean(eng.kv_bytes_per_token(c) for c in ctxs)
+    bytes_tok = eng.weight_bytes() + kv_mean
+    peaks, peak_src = measured_peaks()
+    hbm = float(peaks['hbm_gbs'])
+    step_gbs = bytes_tok / (ms / 1e3 / a.steps) / 1e9
+
+    # dominant kernel: the GEMV chain alone
+    g, gemv_bytes, gemv_launches = gemv_chain_graph(eng)
+    reps = 64
+    time_replays(g, 4)
+    gms = time_replays(g, reps) / reps
+    gemv_gbs = gemv_bytes / (gms / 1e3) / 1e9
+    traffic = profile_traffic()
+
+    e2e = None
+    if not a.no_e2e:
+        reset()
+        host_prompt = prompt.pin_memory()
+        vals = []
+        for _ in range(3):
+            out, st = dec.generate(host_prompt, NEW_TOKENS)
+            vals.append((st['tokens'] - 1) / (st['total_s'] - st['ttft_s']))
+        e2e = {'value': statistics.median(vals) * world, 'unit': 'tok/s', 'h2d_bytes_per_step': PROMPT_LEN * 8 / NEW_TOKENS,
+               'd2h_bytes_per_step': 8, 'ttft_ms': round(st['ttft_s'] * 1e3, 3),
+               'api': 'efficientgpt_b200.GraphGreedyDecoder.generate (pinned host prompt, 256 new tokens)'}
+
+    cb = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cb = cpu_baseline(dec, a.cpu_sample)
+
+    if rank == 0:
+        line = {
+            'metric': METRIC, 'value': round(tok_s, 2), 'unit': 'tok/s', 'n_gpus': world, 'steps': a.steps,
+            'warmup': a.warmup, 'ms_per_step': round(ms / a.steps, 5), 'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': None, 'dtype': 'int8-weight/bf16', 'data': 'synthetic',
+            'config': {'workload': 'qwen3_1.7b int8 decode, BASELINE config 2', 'prompt': PROMPT_LEN,
+                       'new_tokens': NEW_TOKENS, 'scale_dtype': 'bf16', 'init': 'HF random init N(0,0.02), seed 0',
+                       'parallelism': f'replicas{world}' if world > 1 else 'single',
+                       'l2': 'no flush: 1.72 GB of weights streamed per step, larger than L2',
+                       'pdl': not a.no_pdl},
+            'tok_s_per_gpu': round(tok_s / world, 2),
+            'step_roofline': {'bound': 'hbm', 'bytes_per_token': round(bytes_tok), 'achieved': round(step_gbs, 1),
+                              'peak': hbm, 'unit': 'GB/s', 'frac': round(step_gbs / hbm, 4), 'peak_source': peak_src},
+            'roofline': {'bound': 'hbm', 'kernel': 'gemv_i8_tma_kernel', 'achieved': round(gemv_gbs, 1), 'peak': hbm,
+                         'unit': 'GB/s', 'frac': round(gemv_gbs / hbm, 4), 'traffic': traffic,
+                         'launches_per_step': gemv_launches, 'bytes_per_step': gemv_bytes,
+                         'avg_launch_us': round(gms * 1e3 / gemv_launches, 3), 'peak_source': peak_src},
+            'e2e': e2e,
+            'cpu_baseline': cb,
+            'gpu_launches': a.steps * (5 * eng.n_layers + 1),
+            'clocks': clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        del g
+        dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    sys.path.insert(0, str(ROOT))
+    main()

@@ -1,0 +1,22 @@
+"""efficientgpt_b200: batch-1 int8 decode engine for NVIDIA B200 (sm_100a).
+
+Drop-in for the research/realmodel path of BagelsFun/efficientgpt: `int8_linear` (op, Int8Linear, quantize_model),
+`fast_decode.GraphGreedyDecoder`, with the arithmetic in hand-written CUDA (libegpt_b200.so, C-ABI in
+include/egpt_b200.h). Submodules import lazily so the package imports without a GPU.
+"""
+from . import _lib  # noqa: F401
+
+__version__ = '0.1.0'
+
+
+def __getattr__(name):
+    if name in ('quantize_weight', 'Int8Linear', 'quantize_model', 'int8_linear', 'int8_matmul'):
+        from . import int8_linear as m
+        return getattr(m, name)
+    if name == 'GraphGreedyDecoder':
+        from .fast_decode import GraphGreedyDecoder
+        return GraphGreedyDecoder
+    if name == 'Qwen3Engine':
+        from .engine import Qwen3Engine
+        return Qwen3Engine
+    raise AttributeError(name)

@@ -1,0 +1,6 @@
+// Single translation unit of libegpt_b200.so: the kernels share one device error word
+// (egpt::g_device_error), which a unity build lets every kernel reach without relocatable device code.
+#include "capi.cu"
+#include "elementwise.cu"
+#include "gemv_i8.cu"
+#include "attention.cu"

@@ -1,0 +1,104 @@
+"""Weight-only int8 linear layers for Hugging Face decoder models, on B200 CUDA kernels.
+
+Drop-in for BagelsFun/efficientgpt research/realmodel/int8_linear.py: same names, arguments, buffers
+(`qweight` int8 [N, K], `scale` [N]), errors and custom op `efficientgpt::int8_linear`. What changed is below
+the op: the arithmetic runs in libegpt_b200.so (hand-written sm_100a CUDA, see csrc/gemv_i8.cu) instead of
+Triton (decode) and cuBLAS (prefill).
+
+  quantize_weight   int8_linear.py:106-117  per-row s = max|w|/127 (>= 1e-12), q = round(w/s) in [-127, 127];
+                    bit-identical, computed by egpt_quantize_rows on the GPU. scale_dtype=torch.bfloat16 stores
+                    bf16(s) (BASELINE configs 2 and 5), q is computed from the fp32 s as in the reference.
+  int8_matmul       int8_linear.py:67-85    <= 16 rows: bf16(s * (x @ q.T)), fp32 accumulation
+  int8_linear (op)  int8_linear.py:88-103   bf16 only; > 16 rows reproduces the reference's prefill rounding,
+                    bf16(bf16(x @ q.T) * s), with the same kernel run over 16-row blocks (no cuBLAS)
+  Int8Linear        int8_linear.py:120-134
+  quantize_model    int8_linear.py:137-157  every nn.Linear incl. lm_head; a tied lm_head becomes an int8 copy
+
+There is no CPU path: CPU tensors raise ValueError.
+"""
+import torch
+from torch import nn
+
+from . import _lib as L
+from . import ops
+
+MAX_DECODE_ROWS = 16
+
+
+def int8_matmul(x2, w, s):
+    """x2 bf16 [M <= 16, K] contiguous rows; w int8 [N, K]; s fp32/bf16 [N] -> bf16 [M, N]."""
+    m, k = x2.shape
+    if m > MAX_DECODE_ROWS:  # the kernel holds at most 16 rows of x
+        raise ValueError(f'int8_matmul handles at most {MAX_DECODE_ROWS} rows, got {m}')
+    return ops.gemv_i8(x2, w, s)
+
+
+@torch.library.custom_op('efficientgpt::int8_linear', mutates_args=())
+def int8_linear(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+    k = x.shape[-1]
+    x2 = x.reshape(-1, k)
+    if x2.dtype != torch.bfloat16:
+        raise ValueError('int8_linear expects bf16 activations')
+    if x2.shape[0] == 0:
+        return x.new_empty(*x.shape[:-1], w.shape[0])
+    if x2.shape[0] <= MAX_DECODE_ROWS:
+        y = int8_matmul(x2.contiguous(), w, s)
+    else:  # the reference's prefill branch: bf16 GEMM output, then the scale in fp32
+        y = ops.gemv_i8_rows(x2.contiguous(), w, s, double_round=True)
+    return y.reshape(*x.shape[:-1], w.shape[0])
+
+
+@int8_linear.register_fake
+def _(x, w, s):
+    return x.new_empty(*x.shape[:-1], w.shape[0])
+
+
+def quantize_weight(weight, scale_dtype=torch.float32):
+    """Per-output-channel symmetric int8: returns (q int8 [N, K], s [N]) with weight ~= q * s[:, None]."""
+    if scale_dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError('scale_dtype must be torch.float32 or torch.bfloat16')
+    w = weight.detach()
+    if w.dtype not in (torch.float32, torch.bfloat16):
+        w = w.float()
+    return ops.quantize_rows(w, scale_dtype)
+
+
+class Int8Linear(nn.Module):
+    def __init__(self, linear, scale_dtype=torch.float32):
+        super().__init__()
+        q, s = quantize_weight(linear.weight, scale_dtype)
+        self.in_features, self.out_features = linear.in_features, linear.out_features
+        self.register_buffer('qweight', q)
+        self.register_buffer('scale', s)
+        self.bias = None if linear.bias is None else nn.Parameter(linear.bias.detach().clone(), requires_grad=False)
+
+    def forward(self, x):
+        y = int8_linear(x, self.qweight, self.scale)
+        return y if self.bias is None else y + self.bias
+
+    def extra_repr(self):
+        return f'in={self.in_features}, out={self.out_features}, int8 per-channel'
+
+
+@torch.no_grad()
+def quantize_model(model, include_lm_head=True, scale_dtype=torch.float32):
+    """Replace every nn.Linear in the decoder layers (and the lm_head) by Int8Linear, in place. Returns the count.
+    Embeddings and norms stay bf16. A tied lm_head becomes an untied int8 copy (the embedding keeps its weight)."""
+    names = [n for n, m in model.named_modules() if isinstance(m, nn.Linear) and (include_lm_head or n != 'lm_head')]
+    count = 0
+    for full in names:
+        parent_name, _, child_name = full.rpartition('.')
+        parent = model.get_submodule(parent_name) if parent_name else model
+        child = getattr(parent, child_name)
+        setattr(parent, child_name, Int8Linear(child, scale_dtype))
+        del child
+        count += 1
+        if count % 16 == 0:
+            torch.cuda.empty_cache()
+    if hasattr(model, 'config') and include_lm_head:
+        model.config.tie_word_embeddings = False
+    torch.cuda.empty_cache()
+    return count
+
+
+__all__ = ['MAX_DECODE_ROWS', 'int8_matmul', 'int8_linear', 'quantize_weight', 'Int8Linear', 'quantize_model', 'L']

@@ -1,0 +1,189 @@
+/*
+ * efficientgpt-b200: C-ABI of the batch-1 int8 decode engine for NVIDIA B200 (sm_100a).
+ *
+ * Every entry point takes raw device pointers, sizes and a cudaStream_t passed as `void *` (NULL = the
+ * legacy default stream), launches stream-ordered work and returns an int status (EGPT_OK = 0). Nothing
+ * here allocates device memory: callers own weights, activations, KV cache and workspaces, so every call
+ * can be captured in a CUDA graph. On a non-zero status egpt_last_error() returns a message for the
+ * calling thread.
+ *
+ * The "replaces" line above each function names the reference symbol (BagelsFun/efficientgpt, paths
+ * relative to that project) whose behaviour the entry point provides.
+ */
+#ifndef EGPT_B200_H
+#define EGPT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define EGPT_API __attribute__((visibility("default")))
+#else
+#define EGPT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------------------------- */
+#define EGPT_OK 0
+#define EGPT_ERR_SHAPE 1     /* a size is out of range or inconsistent                                    */
+#define EGPT_ERR_DTYPE 2     /* unsupported dtype combination                                             */
+#define EGPT_ERR_ALIGN 3     /* a pointer or leading dimension breaks the 16-byte rule of the fast path   */
+#define EGPT_ERR_LAUNCH 4    /* the CUDA launch failed (message from the runtime in egpt_last_error)      */
+#define EGPT_ERR_TIMEOUT 5   /* a device-side wait gave up (reported by egpt_device_error)                */
+#define EGPT_ERR_ARG 6       /* null pointer or bad flag                                                  */
+#define EGPT_ERR_WORKSPACE 7 /* workspace too small                                                       */
+
+/* ---- dtypes ---------------------------------------------------------------------------------------- */
+#define EGPT_F32 0
+#define EGPT_BF16 1
+
+/* ---- GEMV epilogues -------------------------------------------------------------------------------- */
+#define EGPT_EPI_NONE 0     /* y = round(acc * s[n]) (+ bias[n])                                          */
+#define EGPT_EPI_RESIDUAL 1 /* y = round(residual[n] + round(acc * s[n]))   (in place when out==residual) */
+#define EGPT_EPI_SILU_MUL 2 /* w = cat(gate, up) [2I, K]: y[i] = round(round(silu(g_i)) * u_i), I outputs  */
+#define EGPT_EPI_GELU 3     /* fp32 only: y = gelu_erf(acc * s[n] + bias[n])                              */
+
+/* ---- flags ----------------------------------------------------------------------------------------- */
+#define EGPT_FLAG_DOUBLE_ROUND 1u /* round acc to bf16 before the scale (the reference's >16-row branch)  */
+#define EGPT_FLAG_RMSNORM 2u      /* prologue: x <- RMSNorm(x) * norm_w (bf16 rounding as HF Qwen3)        */
+#define EGPT_FLAG_PDL 4u          /* launch with programmatic dependent launch                            */
+#define EGPT_FLAG_EMBED 8u        /* prologue: x <- embed[*token] and residual <- the same row            */
+#define EGPT_FLAG_ADVANCE 16u     /* lm_head argmax: also *position += 1                                  */
+#define EGPT_FLAG_APPEND 32u      /* attention: q/k-RMSNorm + RoPE + KV append of this step's row in-kernel */
+#define EGPT_FLAG_NO_TMA 64u      /* GEMV: force the plain-load kernel (any K)                            */
+
+/* ---- library ---------------------------------------------------------------------------------------- */
+EGPT_API const char *egpt_version(void);
+EGPT_API const char *egpt_last_error(void);
+/* Reads (and with clear != 0 resets) the device error word that kernels set when a bounded wait gives up.
+ * Synchronises the device. Returns the code (EGPT_OK when no kernel reported a problem). */
+EGPT_API int egpt_device_error(int clear);
+/* Number of SMs of the current device (used to size grids and workspaces). */
+EGPT_API int egpt_num_sms(void);
+
+/* ---- quantiser --------------------------------------------------------------------------------------
+ * replaces: research/realmodel/int8_linear.py:106-117 quantize_weight
+ * s[n] = max(max_k |w[n,k]| / 127, 1e-12) (fp32, stored as scale_dtype); q = clamp(rint(w / s), -127, 127).
+ * w is fp32 or bf16 [n, k] row-major with leading dimension k. Bit-identical to the reference formula. */
+EGPT_API int egpt_quantize_rows(int8_t *q, void *scale, int scale_dtype, const void *w, int w_dtype, int64_t n, int64_t k,
+                       void *stream);
+
+/* ---- int8 weight-only GEMV / small GEMM ------------------------------------------------------------
+ * replaces: research/realmodel/int8_linear.py:26-85 (_dot16, _part, _reduce, int8_matmul) and the
+ *           op efficientgpt::int8_linear (int8_linear.py:88-98) for M <= 16 rows
+ * out[m, n] = epilogue(s[n] * sum_k x[m, k] * q[n, k]) with fp32 accumulation; x/out/residual/bias have
+ * dtype x_dtype (bf16 for the Qwen path, fp32 for the nanoGPT path), s has scale_dtype.
+ * Leading dimensions: x ldx, out/residual ldo (elements). EGPT_EPI_SILU_MUL writes n/2 outputs per row.
+ * token (int64, device) is read with EGPT_FLAG_EMBED, in which case x points at the embedding table
+ * [vocab, K], ldx is vocab (the token is bounds-checked against it) and residual receives the selected row. */
+EGPT_API int egpt_gemv_i8(void *out, const void *x, int x_dtype, int64_t m, int64_t ldx, int64_t ldo, const int8_t *w,
+                 const void *scale, int scale_dtype, int64_t n, int64_t k, const void *bias, void *residual,
+                 int epilogue, const void *norm_w, float eps, const int64_t *token, unsigned flags, void *stream);
+
+/* ---- lm_head + greedy argmax ------------------------------------------------------------------------
+ * replaces: transformers Qwen3ForCausalLM lm_head (modeling_qwen3.py:503-505) on the int8 op, followed by
+ *           research/realmodel/fast_decode.py:48 (argmax(-1), first index on ties) and :49 (position += 1)
+ * token[0] = argmax_n bf16(s[n] * sum_k xn[k] q[n, k]) where xn = RMSNorm(x)*norm_w if EGPT_FLAG_RMSNORM.
+ * logits (bf16 [n], nullable) receives the rounded logits. ws must hold egpt_lm_head_ws_bytes(n) bytes,
+ * zero-filled once before first use (the kernel leaves its counter at zero). */
+EGPT_API size_t egpt_lm_head_ws_bytes(int64_t n);
+EGPT_API int egpt_lm_head_argmax(int64_t *token, int64_t *position, void *logits, const void *x, const int8_t *w,
+                        const void *scale, int scale_dtype, int64_t n, int64_t k, const void *norm_w, float eps,
+                        void *ws, size_t ws_bytes, unsigned flags, void *stream);
+
+/* ---- norms and embedding ----------------------------------------------------------------------------
+ * replaces: transformers Qwen3RMSNorm.forward (modeling_qwen3.py:59-64): y = w * bf16(x * rsqrt(mean(x^2)+eps))
+ * x, w, y bf16; rows of length dim. */
+EGPT_API int egpt_rmsnorm(void *out, const void *x, const void *w, int64_t rows, int64_t dim, float eps, void *stream);
+/* nanoGPT LayerNorm (model.py:18-27), fp32: y = (x - mean) / sqrt(var + eps) * w + b (b nullable). */
+EGPT_API int egpt_layernorm_f32(float *out, const float *x, const float *w, const float *b, int64_t rows, int64_t dim,
+                       float eps, void *stream);
+/* Embedding rows: out[i] = table[ids[i]] (+ pos_table[pos0 + i] when pos_table is non-null, fp32 only).
+ * dtype bf16 or fp32; ids int64 on the device. */
+EGPT_API int egpt_embed(void *out, const int64_t *ids, int64_t rows, const void *table, const void *pos_table,
+               int64_t pos0, int64_t vocab, int64_t dim, int dtype, void *stream);
+
+/* ---- attention --------------------------------------------------------------------------------------
+ * replaces: transformers Qwen3Attention.forward core (modeling_qwen3.py:258-291: q/k RMSNorm, RoPE,
+ *           StaticLayer.update index_copy, SDPA with GQA and the causal mask over the static cache) and the
+ *           split-K decode attention design of research/phase5/decode_attention.py:22-71
+ *
+ * egpt_qk_norm_rope_kv_append: for rows i < m at position pos0 + i (pos0 = *position):
+ *   q_out[i] = RoPE(RMSNorm(q_i) * q_norm_w), K[pos0+i] = RoPE(RMSNorm(k_i) * k_norm_w), V[pos0+i] = v_i.
+ *   qkv rows are [nq*d | nkv*d | nkv*d] bf16 with leading dimension ldqkv. Caches are [nkv][cap][d] bf16.
+ *   rope_cos / rope_sin are bf16 [cap][d/2] (the HF table, cos[i] == cos[i + d/2]).
+ *   q_norm_w / k_norm_w may be NULL (no q/k norm: nanoGPT-style attention), rope_cos NULL = no RoPE.
+ * egpt_attn_decode: out[i, h] = softmax(scale * q_i,h . K[0..L_i)) V[0..L_i), L_i = pos0 + i + 1, GQA head
+ *   h uses kv head h / (nq / nkv). With EGPT_FLAG_APPEND (m must be 1) the norm/RoPE/append above is done
+ *   in-kernel from the raw qkv row, else q comes from q (ldq) already rotated.
+ *   Work is split over up to max_split key ranges per kv head; ws must hold
+ *   egpt_attn_ws_bytes(m, nq, nkv, d, max_split) bytes, zero-filled once before first use.
+ *   dtype: bf16 (Qwen) or fp32 (nanoGPT, no norm/RoPE). */
+EGPT_API int egpt_qk_norm_rope_kv_append(void *q_out, const void *qkv, int64_t ldqkv, void *k_cache, void *v_cache,
+                                int64_t cap, const int64_t *position, int64_t m, int nq, int nkv, int d,
+                                const void *q_norm_w, const void *k_norm_w, float eps, const void *rope_cos,
+                                const void *rope_sin, int dtype, void *stream);
+EGPT_API size_t egpt_attn_ws_bytes(int64_t m, int nq, int nkv, int d, int max_split);
+EGPT_API int egpt_attn_decode(void *out, int64_t ldo, const void *q, int64_t ldq, void *k_cache, void *v_cache, int64_t cap,
+                     const int64_t *position, int64_t m, int nq, int nkv, int d, const void *q_norm_w,
+                     const void *k_norm_w, float eps, const void *rope_cos, const void *rope_sin, float scale,
+                     int max_split, void *ws, size_t ws_bytes, int dtype, unsigned flags, void *stream);
+
+/* ---- argmax over rows of bf16/fp32 logits -----------------------------------------------------------
+ * replaces: logits[:, -1].argmax(-1) (research/realmodel/fast_decode.py:48,84): first index on ties. */
+EGPT_API int egpt_argmax_rows(int64_t *out, const void *logits, int64_t rows, int64_t n, int64_t ld, int dtype, void *stream);
+
+/* ---- whole decode step (Qwen3 family) ---------------------------------------------------------------
+ * replaces: research/realmodel/fast_decode.py:45-49 GraphGreedyDecoder._step (HF Qwen3 forward with
+ *           StaticCache + argmax + position += 1), captured into one CUDA graph by the caller.
+ * Launches 5 kernels per layer + the lm_head/argmax kernel. Reads *token and *position on the device,
+ * writes the next token to *token and increments *position. */
+typedef struct egpt_qwen3_layer {
+  const int8_t *w_qkv;  /* [(nq + 2 nkv) d, hidden]: q_proj, k_proj, v_proj rows concatenated          */
+  const void *s_qkv;    /* scales for w_qkv                                                             */
+  const int8_t *w_o;    /* [hidden, nq d]                                                               */
+  const void *s_o;
+  const int8_t *w_gu;   /* [2 inter, hidden]: gate_proj rows then up_proj rows                          */
+  const void *s_gu;
+  const int8_t *w_down; /* [hidden, inter]                                                              */
+  const void *s_down;
+  const void *ln_in;    /* input_layernorm.weight, bf16 [hidden]                                        */
+  const void *ln_post;  /* post_attention_layernorm.weight, bf16 [hidden]                               */
+  const void *q_norm;   /* self_attn.q_norm.weight, bf16 [d]                                            */
+  const void *k_norm;   /* self_attn.k_norm.weight, bf16 [d]                                            */
+  void *k_cache;        /* bf16 [nkv][cap][d]                                                           */
+  void *v_cache;        /* bf16 [nkv][cap][d]                                                           */
+} egpt_qwen3_layer;
+
+typedef struct egpt_qwen3_plan {
+  int32_t n_layers, hidden, n_q_heads, n_kv_heads, head_dim, intermediate;
+  int64_t vocab, cap;
+  float eps, attn_scale;
+  int32_t scale_dtype;          /* EGPT_F32 or EGPT_BF16                                                  */
+  uint32_t flags;               /* EGPT_FLAG_PDL to chain the step's kernels with PDL                    */
+  int32_t attn_max_split;
+  const egpt_qwen3_layer *layers; /* host array of n_layers entries                                      */
+  const void *embed;            /* bf16 [vocab, hidden]                                                   */
+  const void *final_norm;       /* bf16 [hidden]                                                          */
+  const int8_t *w_lm;           /* [vocab, hidden]                                                        */
+  const void *s_lm;
+  const void *rope_cos, *rope_sin; /* bf16 [cap][d/2]                                                     */
+  int64_t *token, *position;    /* device int64 [1] each                                                  */
+  void *h, *qkv, *attn, *act;   /* bf16 activations: [hidden], [(nq+2nkv) d], [nq d], [inter]             */
+  void *logits;                 /* nullable bf16 [vocab]                                                  */
+  void *attn_ws;
+  size_t attn_ws_bytes;
+  void *lm_ws;
+  size_t lm_ws_bytes;
+} egpt_qwen3_plan;
+
+EGPT_API int egpt_decode_step(const egpt_qwen3_plan *plan, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EGPT_B200_H */

@@ -1,0 +1,63 @@
+"""Restatement of the reference's int8 weight-only linear in numpy (test infrastructure; see oracle/__init__.py).
+
+Reference: BagelsFun/efficientgpt research/realmodel/int8_linear.py.
+"""
+import numpy as np
+
+from .bf16 import round_bf16
+
+MAX_DECODE_ROWS = 16  # int8_linear.py:18
+
+
+def quantize_weight(w):
+    """int8_linear.py:106-117 quantize_weight: per-row s = max(max|w| / 127, 1e-12) in fp32,
+    q = clamp(round_half_even(w / s), -127, 127) as int8. (The 8192-row chunking there is elementwise per row.)"""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    s = np.maximum(np.abs(w).max(axis=1) / np.float32(127.0), np.float32(1e-12)).astype(np.float32)
+    with np.errstate(invalid='ignore'):
+        q = np.clip(np.rint(w / s[:, None]), -127, 127).astype(np.int8)
+    return q, s
+
+
+def int8_matmul(x, q, s):
+    """int8_linear.py:26-38,67-78 (_dot16 via int8_matmul, <= 16 rows): bf16(s * (x @ q.T)), fp32 accumulation.
+    x float32 array holding bf16 values [M, K]; q int8 [N, K]; s float32 [N] (bf16 scales passed as their values)."""
+    x = np.asarray(x, dtype=np.float32)
+    if x.shape[0] > MAX_DECODE_ROWS:
+        raise ValueError(f'int8_matmul handles at most {MAX_DECODE_ROWS} rows, got {x.shape[0]}')
+    acc = x @ q.astype(np.float32).T
+    return round_bf16(acc * np.asarray(s, dtype=np.float32)[None, :])
+
+
+def int8_linear_prefill(x, q, s):
+    """int8_linear.py:96-97 (> 16 rows): bf16(bf16(x @ bf16(q).T) * s)."""
+    acc = np.asarray(x, dtype=np.float32) @ q.astype(np.float32).T
+    return round_bf16(round_bf16(acc) * np.asarray(s, dtype=np.float32)[None, :])
+
+
+def int8_linear(x, q, s):
+    """int8_linear.py:88-98: the op, dispatching on the row count."""
+    x2 = np.asarray(x, dtype=np.float32).reshape(-1, x.shape[-1])
+    y = int8_matmul(x2, q, s) if x2.shape[0] <= MAX_DECODE_ROWS else int8_linear_prefill(x2, q, s)
+    return y.reshape(*x.shape[:-1], q.shape[0])
+
+
+def int8_truth(x, q, s):
+    """fp64 ground truth of x @ (q * s).T (research/kernelagent/tasks.py:150-158, chunking irrelevant in numpy)."""
+    return np.asarray(x, np.float64) @ (q.astype(np.float64) * np.asarray(s, np.float64)[:, None]).T
+
+
+def gemv_inputs(n, k, seed, m=1, edge=None):
+    """Seeded GEMV sweep inputs (BASELINE config 3 and research/kernelagent/tasks.py:132-147):
+    x ~ N(0,1) bf16 [m, k] (x30 for edge='large'), q uniform in [-127, 127] (+-127 for edge='extreme_w'),
+    s ~ U(0.001, 0.02) rounded to bf16. Returns (x float32 holding bf16 values, q int8, s float32 holding bf16)."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    if edge == 'large':
+        x = x * np.float32(30.0)
+    x = round_bf16(x)
+    q = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+    if edge == 'extreme_w':
+        q = np.where(q >= 0, 127, -127).astype(np.int8)
+    s = round_bf16(rng.uniform(0.001, 0.02, size=n).astype(np.float32))
+    return x, q, s

@@ -1,0 +1,36 @@
+"""Token-parity rule for greedy decoding with bf16 logits (test infrastructure; see oracle/__init__.py).
+
+The reference accepts a divergence between two greedy decoders only at a near-tie of the reference logits
+(BagelsFun/efficientgpt research/phase5/benchmark_review.py:54-67: first divergence, top-1/top-2 margin < 1e-2).
+That rule was written for fp32 logits. The int8 path's logits are bf16 (modeling_qwen3.py:503-505 has no
+upcast), whose spacing near |logit| = 4 is 0.03125, so exact ties (margin 0) and one-ulp margins are common
+and any change of fp32 summation order can flip them. The rule used here: identical tokens up to the first
+divergence, and that divergence must sit where the reference's margin is within two bf16 ulps of its top-1
+logit (or below 1e-2). Steps after a legitimate divergence are not compared (the contexts differ).
+"""
+import math
+
+
+def bf16_ulp(v):
+    """Spacing of bf16 values at |v| (normal range)."""
+    a = abs(float(v))
+    if a == 0.0 or not math.isfinite(a):
+        return 0.0
+    return 2.0 ** (math.floor(math.log2(a)) - 7)
+
+
+def near_tie_threshold(top):
+    return max(1e-2, 2.0 * bf16_ulp(top))
+
+
+def near_tie_match(ref_tokens, ref_margins, ref_tops, got_tokens):
+    """Returns (ok, first_divergence_index_or_None, detail)."""
+    n = min(len(ref_tokens), len(got_tokens))
+    if len(got_tokens) != len(ref_tokens):
+        return False, None, f'length {len(got_tokens)} != {len(ref_tokens)}'
+    for i in range(n):
+        if ref_tokens[i] != got_tokens[i]:
+            thr = near_tie_threshold(ref_tops[i])
+            ok = ref_margins[i] <= thr
+            return ok, i, f'step {i}: ref margin {ref_margins[i]:.5g}, near-tie threshold {thr:.5g}'
+    return True, None, 'identical'

@@ -1,0 +1,155 @@
+"""GPU parity of the decode attention kernels (egpt_attn_decode, egpt_qk_norm_rope_kv_append)
+against fp64 truth, the reference's masked-SDPA error rule (research/phase5/test_graph_gpu.py:202-261) and the
+oracle's norm/RoPE restatement."""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import attn_ref
+from oracle.bf16 import from_torch
+from oracle.qwen3_ref import apply_rope, rmsnorm
+
+pytestmark = pytest.mark.gpu
+
+NQ, NKV, D = 16, 8, 128
+SCALE = D ** -0.5
+
+
+def _ops():
+    from efficientgpt_b200 import _lib as L, ops
+    return L, ops
+
+
+def _inputs(L, cap, seed, cuda, dtype=torch.bfloat16):
+    g = torch.Generator(device='cuda').manual_seed(seed)
+    q = torch.randn(1, NQ * D, device=cuda, generator=g).to(dtype)
+    k = torch.randn(NKV, cap, D, device=cuda, generator=g).to(dtype)
+    v = torch.randn(NKV, cap, D, device=cuda, generator=g).to(dtype)
+    return q, k, v
+
+
+def _sdpa_err(q, k, v, length):
+    qq = q.view(1, NQ, 1, D)
+    kk = k[:, :length].repeat_interleave(NQ // NKV, 0)[None]
+    vv = v[:, :length].repeat_interleave(NQ // NKV, 0)[None]
+    ref = F.scaled_dot_product_attention(qq.double(), kk.double(), vv.double(), scale=SCALE)
+    out = F.scaled_dot_product_attention(qq, kk, vv, scale=SCALE)
+    return float((out.double() - ref).abs().max())
+
+
+@pytest.mark.parametrize('length', [512, 2048, 8192, 32768])
+@pytest.mark.parametrize('max_split', [1, 19, 64])
+def test_decode_attention_vs_fp64(cuda, length, max_split):
+    L, ops = _ops()
+    q, k, v = _inputs(L, length, length, cuda)
+    pos = torch.tensor([length - 1], device=cuda)
+    out = ops.attn_decode(q, k, v, pos, NQ, NKV, D, scale=SCALE, max_split=max_split)
+    truth = attn_ref.decode_attention_truth(from_torch(q).reshape(NQ, D), from_torch(k), from_torch(v), length, SCALE)
+    err = float(np.abs(from_torch(out).reshape(NQ, D) - truth).max())
+    assert err <= 2e-3, (length, max_split, err)
+    assert err <= max(2 * _sdpa_err(q, k, v, length), 1e-3), (length, max_split, err)
+
+
+def test_split_count_does_not_change_much(cuda):
+    L, ops = _ops()
+    q, k, v = _inputs(L, 4096, 1, cuda)
+    pos = torch.tensor([3000], device=cuda)
+    outs = [ops.attn_decode(q, k, v, pos, NQ, NKV, D, scale=SCALE, max_split=ms).float() for ms in (1, 2, 7, 24, 64)]
+    for o in outs[1:]:
+        torch.testing.assert_close(o, outs[0], atol=4e-3, rtol=1e-2)
+
+
+def test_never_reads_past_position(cuda):
+    L, ops = _ops()
+    q, k, v = _inputs(L, 300, 2, cuda)
+    for p in (0, 17, 127, 128, 250, 299):
+        pos = torch.tensor([p], device=cuda)
+        clean = ops.attn_decode(q, k, v, pos, NQ, NKV, D, scale=SCALE, max_split=8)
+        kp, vp = k.clone(), v.clone()
+        kp[:, p + 1:] = float('nan')
+        vp[:, p + 1:] = float('nan')
+        assert torch.equal(clean, ops.attn_decode(q, kp, vp, pos, NQ, NKV, D, scale=SCALE, max_split=8)), p
+
+
+def test_multi_row_causal_matches_rowwise(cuda):
+    """Prefill rows: row i attends to [0, pos0 + i]; equals one decode call per row."""
+    L, ops = _ops()
+    cap, m = 96, 9
+    g = torch.Generator(device='cuda').manual_seed(4)
+    q = torch.randn(m, NQ * D, device=cuda, generator=g).to(torch.bfloat16)
+    k = torch.randn(NKV, cap, D, device=cuda, generator=g).to(torch.bfloat16)
+    v = torch.randn(NKV, cap, D, device=cuda, generator=g).to(torch.bfloat16)
+    pos0 = torch.tensor([40], device=cuda)
+    out = ops.attn_decode(q, k, v, pos0, NQ, NKV, D, scale=SCALE, max_split=4)
+    for i in range(m):
+        one = ops.attn_decode(q[i:i + 1].contiguous(), k, v, pos0 + i, NQ, NKV, D, scale=SCALE, max_split=4)
+        assert torch.equal(out[i:i + 1], one), i
+
+
+def _norm_rope_setup(cuda, cap=64):
+    g = torch.Generator(device='cuda').manual_seed(5)
+    qkv = torch.randn(3, (NQ + 2 * NKV) * D, device=cuda, generator=g).to(torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(D, device=cuda, generator=g)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(D, device=cuda, generator=g)).to(torch.bfloat16)
+    inv = (1.0 / (1e6 ** (torch.arange(0, D, 2, device=cuda).float() / D))).to(torch.bfloat16).float()
+    fr = torch.arange(cap, device=cuda).float()[:, None] * inv[None]
+    cos, sin = fr.cos().to(torch.bfloat16).contiguous(), fr.sin().to(torch.bfloat16).contiguous()
+    return qkv, qn, kn, cos, sin
+
+
+def test_qk_norm_rope_append_vs_oracle(cuda):
+    L, ops = _ops()
+    cap = 64
+    qkv, qn, kn, cos, sin = _norm_rope_setup(cuda, cap)
+    kc = torch.zeros(NKV, cap, D, device=cuda, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    pos0 = torch.tensor([10], device=cuda)
+    q = ops.qk_norm_rope_kv_append(qkv, kc, vc, pos0, NQ, NKV, D, q_norm_w=qn, k_norm_w=kn, eps=1e-6, rope_cos=cos,
+                                   rope_sin=sin)
+    x = from_torch(qkv)
+    c = np.concatenate([from_torch(cos)] * 2, -1)[10:13][:, None, :]
+    s = np.concatenate([from_torch(sin)] * 2, -1)[10:13][:, None, :]
+    q_ref = apply_rope(rmsnorm(x[:, :NQ * D].reshape(3, NQ, D), from_torch(qn), 1e-6), c, s).reshape(3, NQ * D)
+    k_ref = apply_rope(rmsnorm(x[:, NQ * D:(NQ + NKV) * D].reshape(3, NKV, D), from_torch(kn), 1e-6), c, s)
+    v_ref = x[:, (NQ + NKV) * D:].reshape(3, NKV, D)
+    # rsqrtf vs 1/sqrt: rare one-ulp differences
+    assert (from_torch(q) != q_ref).mean() < 0.01
+    np.testing.assert_allclose(from_torch(q), q_ref, rtol=2 ** -7, atol=1e-6)
+    np.testing.assert_allclose(from_torch(kc)[:, 10:13].transpose(1, 0, 2), k_ref, rtol=2 ** -7, atol=1e-6)
+    np.testing.assert_array_equal(from_torch(vc)[:, 10:13].transpose(1, 0, 2), v_ref)
+    assert float(kc[:, :10].abs().sum()) == 0 and float(kc[:, 13:].abs().sum()) == 0
+
+
+def test_fused_append_equals_separate_kernels(cuda):
+    L, ops = _ops()
+    cap = 200
+    qkv, qn, kn, cos, sin = _norm_rope_setup(cuda, cap)
+    g = torch.Generator(device='cuda').manual_seed(9)
+    k0 = torch.randn(NKV, cap, D, device=cuda, generator=g).to(torch.bfloat16)
+    v0 = torch.randn(NKV, cap, D, device=cuda, generator=g).to(torch.bfloat16)
+    for p, ms in ((0, 4), (130, 4), (130, 1), (199, 19)):
+        pos = torch.tensor([p], device=cuda)
+        ka, va = k0.clone(), v0.clone()
+        fused = ops.attn_decode(qkv[:1].contiguous(), ka, va, pos, NQ, NKV, D, scale=SCALE, max_split=ms, append=True,
+                                q_norm_w=qn, k_norm_w=kn, eps=1e-6, rope_cos=cos, rope_sin=sin)
+        kb, vb = k0.clone(), v0.clone()
+        q = ops.qk_norm_rope_kv_append(qkv[:1].contiguous(), kb, vb, pos, NQ, NKV, D, q_norm_w=qn, k_norm_w=kn,
+                                       eps=1e-6, rope_cos=cos, rope_sin=sin)
+        sep = ops.attn_decode(q, kb, vb, pos, NQ, NKV, D, scale=SCALE, max_split=ms)
+        assert torch.equal(ka, kb) and torch.equal(va, vb), p
+        assert torch.equal(fused, sep), (p, ms)
+
+
+def test_fp32_mha_path(cuda):
+    """nanoGPT attention: fp32 caches, 6 heads of 64, no norm / RoPE."""
+    L, ops = _ops()
+    g = torch.Generator(device='cuda').manual_seed(6)
+    cap, nh, d = 256, 6, 64
+    q = torch.randn(1, nh * d, device=cuda, generator=g)
+    k = torch.randn(nh, cap, d, device=cuda, generator=g)
+    v = torch.randn(nh, cap, d, device=cuda, generator=g)
+    pos = torch.tensor([200], device=cuda)
+    out = ops.attn_decode(q, k, v, pos, nh, nh, d, scale=d ** -0.5, max_split=8)
+    truth = attn_ref.decode_attention_truth(from_torch(q).reshape(nh, d), from_torch(k), from_torch(v), 201, d ** -0.5)
+    assert np.abs(from_torch(out).reshape(nh, d) - truth).max() < 1e-5

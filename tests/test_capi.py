@@ -1,0 +1,67 @@
+"""CPU tests of the C-ABI boundary: the library loads, exports every function the header declares, and
+rejects bad arguments with the documented status before touching a GPU. No kernel is launched here."""
+import ctypes
+
+import pytest
+import torch
+
+from efficientgpt_b200 import _lib as L
+
+
+def test_library_exports_every_header_function():
+    lib = L.load()
+    names = L.header_functions()
+    assert len(names) >= 16
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in L.SIGNATURES, f'{n} has no ctypes signature'
+    assert set(L.SIGNATURES) == set(names)
+
+
+def test_version_and_error_strings():
+    lib = L.load()
+    assert b'sm_100a' in lib.egpt_version()
+    assert lib.egpt_last_error() is not None
+
+
+def test_workspace_size_queries():
+    lib = L.load()
+    assert lib.egpt_lm_head_ws_bytes(151936) >= 1024 * 8
+    a = lib.egpt_attn_ws_bytes(1, 16, 8, 128, 19)
+    assert a >= 16 * 19 * 130 * 4 + 8 * 4
+    assert lib.egpt_attn_ws_bytes(4, 16, 8, 128, 19) > a
+
+
+def test_argument_validation_without_launch():
+    lib = L.load()
+    null = None
+    rc = lib.egpt_gemv_i8(null, null, L.EGPT_BF16, 1, 16, 16, null, null, L.EGPT_F32, 16, 16, null, null, 0, null,
+                          0.0, null, 0, null)
+    assert rc == L.EGPT_ERR_ARG
+    assert 'null' in L.last_error()
+    dummy = ctypes.c_void_p(16)
+    rc = lib.egpt_gemv_i8(dummy, dummy, L.EGPT_BF16, 17, 16, 16, dummy, dummy, L.EGPT_F32, 16, 16, null, null, 0, null,
+                          0.0, null, 0, null)
+    assert rc == L.EGPT_ERR_SHAPE
+    rc = lib.egpt_gemv_i8(dummy, dummy, 7, 1, 16, 16, dummy, dummy, L.EGPT_F32, 16, 16, null, null, 0, null, 0.0, null,
+                          0, null)
+    assert rc == L.EGPT_ERR_DTYPE
+    rc = lib.egpt_attn_decode(dummy, 64, dummy, 64, dummy, dummy, 8, dummy, 1, 6, 4, 32, null, null, 0.0, null, null,
+                              1.0, 4, null, 0, L.EGPT_BF16, 0, null)
+    assert rc == L.EGPT_ERR_SHAPE  # 6 q heads over 4 kv heads
+    rc = lib.egpt_lm_head_argmax(dummy, null, null, dummy, dummy, dummy, L.EGPT_F32, 100, 64, null, 0.0, dummy, 8, 0,
+                                 null)
+    assert rc == L.EGPT_ERR_WORKSPACE
+    with pytest.raises(ValueError, match='workspace'):
+        L.check(rc, 'lm_head_argmax')
+
+
+def test_ops_reject_cpu_tensors():
+    from efficientgpt_b200 import ops
+    from efficientgpt_b200.int8_linear import int8_linear, quantize_weight
+    with pytest.raises(ValueError, match='CUDA'):
+        ops.gemv_i8(torch.zeros(1, 32, dtype=torch.bfloat16), torch.zeros(8, 32, dtype=torch.int8), torch.ones(8))
+    with pytest.raises(ValueError, match='CUDA'):
+        quantize_weight(torch.randn(4, 4))
+    with pytest.raises(ValueError, match='bf16'):
+        int8_linear(torch.zeros(2, 32), torch.zeros(8, 32, dtype=torch.int8), torch.ones(8))

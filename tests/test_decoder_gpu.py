@@ -1,0 +1,147 @@
+"""GPU parity of the whole decode path (egpt_decode_step in a CUDA graph behind GraphGreedyDecoder) against the
+reference's greedy tokens (golden fixtures) and the oracle. Mirrors research/realmodel/test_fast_decode.py."""
+import numpy as np
+import pytest
+import torch
+
+import golden_inputs as gi
+from oracle import parity
+from oracle.bf16 import from_bits, from_torch
+from oracle.qwen3_ref import Qwen3Ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _tiny(scale_dtype=torch.float32, quantize=True):
+    from efficientgpt_b200.int8_linear import quantize_model
+    model = gi.build_model(gi.tiny_config())
+    cpu_hash = gi.state_hash(model)
+    model = model.cuda()
+    if quantize:
+        quantize_model(model, scale_dtype=scale_dtype)
+    return model, cpu_hash
+
+
+@pytest.mark.parametrize('scale_dtype', [torch.float32, torch.bfloat16])
+def test_tokens_match_reference_golden(cuda, golden, scale_dtype):
+    from efficientgpt_b200.fast_decode import GraphGreedyDecoder
+    model, h = _tiny(scale_dtype)
+    assert h == golden['tiny_qwen3']['state_sha256'], 'HF random init changed: golden tokens do not apply'
+    key = 'fp32' if scale_dtype == torch.float32 else 'bf16'
+    dec = GraphGreedyDecoder(model, max_cache_len=128)
+    exact = 0
+    for p, x in gi.tiny_prompts().items():
+        run = golden['tiny_qwen3']['runs'][key][str(p)]
+        got, st = dec.generate(x.cuda(), 40)
+        assert st['tokens'] == 40
+        assert len(set(got)) > 8, 'degenerate model output would make equality trivial'
+        ok, first, detail = parity.near_tie_match(run['tokens'], run['margins'], run['tops'], got)
+        assert ok, (key, p, detail)
+        exact += first is None
+    assert exact >= 1
+
+
+def test_quantized_weights_equal_oracle(cuda):
+    model, _ = _tiny()
+    ref_model = gi.build_model(gi.tiny_config())
+    ref = Qwen3Ref.from_hf(ref_model, 128, 'fp32')
+    blk = model.model.layers[1].mlp.down_proj
+    q, s = ref.layers[1]['down']
+    np.testing.assert_array_equal(blk.qweight.cpu().numpy(), q)
+    np.testing.assert_array_equal(blk.scale.cpu().numpy(), s)
+
+
+@pytest.mark.parametrize('scale_dtype', ['fp32', 'bf16'])
+def test_logits_match_reference_and_oracle(cuda, scale_dtype):
+    """Prefill logits vs the reference's golden logits, then 12 teacher-forced decode steps vs the oracle
+    (bf16 logits within 1e-2 abs / 1e-2 rel)."""
+    from conftest import ROOT
+    from efficientgpt_b200.engine import Qwen3Engine
+    sd = torch.float32 if scale_dtype == 'fp32' else torch.bfloat16
+    model, _ = _tiny(sd)
+    eng = Qwen3Engine(model, 128, keep_logits=True)
+    x = gi.tiny_prompts()[5]
+    eng.prefill(x.cuda())
+    z = np.load(ROOT / 'tests' / 'golden' / 'tiny_qwen3.npz')
+    np.testing.assert_allclose(from_torch(eng.logits), from_bits(z[f'logits_p5_{scale_dtype}']), atol=1e-2, rtol=1e-2)
+    ref = Qwen3Ref.from_hf(gi.build_model(gi.tiny_config()), 128, scale_dtype)
+    lg = ref.forward(x[0].tolist(), 0)
+    np.testing.assert_allclose(from_torch(eng.logits), lg, atol=1e-2, rtol=1e-2)
+    pos = 5
+    for i in range(12):
+        tok = int(np.argmax(lg))
+        eng.token.fill_(tok)
+        eng.step()
+        lg = ref.forward([tok], pos)
+        pos += 1
+        assert int(eng.position) == pos
+        np.testing.assert_allclose(from_torch(eng.logits), lg, atol=1e-2, rtol=1e-2, err_msg=f'step {i}')
+        if int(eng.token) != int(np.argmax(lg)):  # only at a near-tie of the oracle's own logits
+            top = np.sort(lg)[-2:]
+            assert top[1] - top[0] <= parity.near_tie_threshold(top[1]), i
+
+
+def test_graph_replay_equals_eager_steps(cuda):
+    from efficientgpt_b200.engine import Qwen3Engine
+    model, _ = _tiny()
+    eng = Qwen3Engine(model, 128)
+    x = gi.tiny_prompts()[37].cuda()
+    eng.prefill(x)
+    eager = []
+    for _ in range(20):
+        eager.append(int(eng.token))
+        eng.step()
+    from efficientgpt_b200.fast_decode import GraphGreedyDecoder
+    dec = GraphGreedyDecoder(model, max_cache_len=128)
+    got, _ = dec.generate(x, 20)
+    assert got == eager
+
+
+def test_eos_stops_exactly_and_never_leaks_lookahead_tokens(cuda):
+    """research/realmodel/test_fast_decode.py:42-56."""
+    from efficientgpt_b200.fast_decode import GraphGreedyDecoder
+    model, _ = _tiny()
+    dec = GraphGreedyDecoder(model, max_cache_len=128, lookahead=8)
+    x = torch.randint(0, 512, (1, 7), generator=torch.Generator().manual_seed(2)).cuda()
+    full, _ = dec.generate(x, 60)
+    k = max(i for i in range(len(full)) if full[i] not in full[:i])
+    assert k > 10, 'EOS must fall well past the first lookahead window'
+    streamed = []
+    got, st = dec.generate(x, 60, eos_ids={full[k]}, on_token=streamed.append)
+    assert got == full[:k + 1]
+    assert streamed == got
+    again, _ = dec.generate(x, 60)
+    assert again == full
+
+
+def test_guards(cuda):
+    """research/realmodel/test_fast_decode.py:58-70."""
+    from efficientgpt_b200.fast_decode import GraphGreedyDecoder
+    model, _ = _tiny()
+    dec = GraphGreedyDecoder(model, max_cache_len=32)
+    with pytest.raises(ValueError):
+        dec.generate(torch.zeros((1, 20), dtype=torch.long, device='cuda'), 20)
+    with pytest.raises(ValueError):
+        dec.generate(torch.zeros((2, 4), dtype=torch.long, device='cuda'), 4)
+    with pytest.raises(ValueError):
+        dec.generate(torch.zeros((1, 4), dtype=torch.long, device='cuda'), 0)
+    out, st = dec.generate(torch.zeros((1, 4), dtype=torch.long, device='cuda'), 3)
+    assert (len(out), st['tokens']) == (3, 3)
+    assert 'capture_s' in st
+    with pytest.raises(ValueError):  # unquantised models are refused (no silent bf16 fallback)
+        GraphGreedyDecoder(_tiny(quantize=False)[0], max_cache_len=32)
+
+
+def test_qwen3_1p7b_shape_matches_reference_golden(cuda, golden):
+    """BASELINE config 2 at full size: the reference's 16 greedy tokens (CPU, bf16 scales) vs the native path."""
+    from efficientgpt_b200.fast_decode import GraphGreedyDecoder
+    from efficientgpt_b200.int8_linear import quantize_model
+    g = golden['qwen3_1p7b']
+    model = gi.build_model(gi.qwen3_1p7b_config())
+    assert gi.state_hash(model) == g['state_sha256'], 'HF random init changed: golden tokens do not apply'
+    model = model.cuda()
+    quantize_model(model, scale_dtype=torch.bfloat16)
+    dec = GraphGreedyDecoder(model, max_cache_len=64)
+    got, st = dec.generate(gi.big_prompt().cuda(), 16)
+    ok, first, detail = parity.near_tie_match(g['tokens'], g['margins'], g['tops'], got)
+    assert ok, detail
