@@ -9,6 +9,9 @@ namespace egpt {
 constexpr int kRowThreads = 256;
 
 // s[n] = max(absmax(w[n]) / 127, 1e-12); q = clamp(rint(w / s), -127, 127)   (reference quantize_weight)
+// The reference quantises on the GPU, where PyTorch evaluates `tensor / 127.0` (a CPU scalar divisor) as
+// tensor * fl32(1 / 127); that product is reproduced here, so q and s are bit-identical to the reference's.
+// `w / s` (tensor / tensor) is a true IEEE division in PyTorch and here.
 __global__ void __launch_bounds__(kRowThreads) quantize_rows_kernel(int8_t *q, void *scale, int scale_bf16,
                                                                      const void *w, int w_bf16, int64_t k) {
   __shared__ float red[32];
@@ -28,7 +31,7 @@ __global__ void __launch_bounds__(kRowThreads) quantize_rows_kernel(int8_t *q, v
     if (lane == 0) red[0] = t;
   }
   __syncthreads();
-  const float s = fmaxf(red[0] / 127.0f, 1e-12f);
+  const float s = fmaxf(red[0] * (1.0f / 127.0f), 1e-12f);
   if (threadIdx.x == 0) {
     if (scale_bf16)
       ((uint16_t *)scale)[row] = f32_to_bf16_bits(s);

@@ -9,11 +9,23 @@ from .bf16 import round_bf16
 MAX_DECODE_ROWS = 16  # int8_linear.py:18
 
 
-def quantize_weight(w):
+def quantize_weight(w, semantics='cuda'):
     """int8_linear.py:106-117 quantize_weight: per-row s = max(max|w| / 127, 1e-12) in fp32,
-    q = clamp(round_half_even(w / s), -127, 127) as int8. (The 8192-row chunking there is elementwise per row.)"""
+    q = clamp(round_half_even(w / s), -127, 127) as int8. (The 8192-row chunking there is elementwise per row.)
+
+    `max|w| / 127.0` divides a tensor by a Python scalar. On CUDA tensors (where the reference quantises: the
+    model is moved to the GPU first, assistant/backends.py:198-202) PyTorch evaluates that as a multiplication
+    by fl32(1/127); on CPU tensors as a true division. semantics='cuda' | 'cpu' selects which; `w / s` is a true
+    division in both."""
     w = np.ascontiguousarray(w, dtype=np.float32)
-    s = np.maximum(np.abs(w).max(axis=1) / np.float32(127.0), np.float32(1e-12)).astype(np.float32)
+    amax = np.abs(w).max(axis=1)
+    if semantics == 'cuda':
+        s0 = amax * (np.float32(1.0) / np.float32(127.0))
+    elif semantics == 'cpu':
+        s0 = amax / np.float32(127.0)
+    else:
+        raise ValueError(semantics)
+    s = np.maximum(s0.astype(np.float32), np.float32(1e-12)).astype(np.float32)
     with np.errstate(invalid='ignore'):
         q = np.clip(np.rint(w / s[:, None]), -127, 127).astype(np.int8)
     return q, s

@@ -70,8 +70,9 @@ class Qwen3Ref:
         self.v = np.zeros((len(layers), nkv, cap, d), np.float32)
 
     @classmethod
-    def from_hf(cls, model, cap, scale_dtype='fp32'):
-        """Build from an (unquantised, bf16) transformers Qwen3ForCausalLM."""
+    def from_hf(cls, model, cap, scale_dtype='fp32', semantics='cuda'):
+        """Build from an (unquantised, bf16) transformers Qwen3ForCausalLM. `semantics` selects the quantiser's
+        scalar-division behaviour ('cuda': the reference quantising on the GPU; 'cpu': on the host)."""
         c = model.config
         cfg = {'hidden': c.hidden_size, 'n_q_heads': c.num_attention_heads, 'n_kv_heads': c.num_key_value_heads,
                'head_dim': getattr(c, 'head_dim', c.hidden_size // c.num_attention_heads),
@@ -79,7 +80,7 @@ class Qwen3Ref:
                'inv_freq': from_torch(model.model.rotary_emb.inv_freq)}
 
         def quant(lin):
-            q, s = quantize_weight(from_torch(lin.weight))
+            q, s = quantize_weight(from_torch(lin.weight), semantics)
             return q, (round_bf16(s) if scale_dtype == 'bf16' else s)
 
         layers = []

@@ -12,20 +12,39 @@ from oracle.qwen3_ref import Qwen3Ref
 pytestmark = pytest.mark.gpu
 
 
-def _tiny(scale_dtype=torch.float32, quantize=True):
-    from efficientgpt_b200.int8_linear import quantize_model
+def _quantize(model, scale_dtype, semantics):
+    """quantize_model, then (semantics='cpu') overwrite q/s with the quantiser evaluated as the golden run did:
+    the goldens come from the reference on CPU, where `max|w| / 127.0` is a true division, while on the GPU
+    PyTorch (and the product) multiply by fl32(1/127); a few q elements differ between the two."""
+    from efficientgpt_b200.int8_linear import Int8Linear, quantize_model
+    orig = {n: m.weight.detach().clone() for n, m in model.named_modules() if isinstance(m, torch.nn.Linear)}
+    quantize_model(model, scale_dtype=scale_dtype)
+    if semantics == 'cpu':
+        for n, m in model.named_modules():
+            if isinstance(m, Int8Linear):
+                w = orig[n].float()
+                amax = w.abs().amax(1)
+                s = (amax / torch.full_like(amax, 127.0)).clamp_min(1e-12)  # tensor divisor: true division
+                m.qweight.copy_(torch.round(w / s[:, None]).clamp(-127, 127).to(torch.int8))
+                m.scale.copy_(s.to(m.scale.dtype))
+    return model
+
+
+def _tiny(scale_dtype=torch.float32, quantize=True, semantics='cuda'):
     model = gi.build_model(gi.tiny_config())
     cpu_hash = gi.state_hash(model)
     model = model.cuda()
     if quantize:
-        quantize_model(model, scale_dtype=scale_dtype)
+        _quantize(model, scale_dtype, semantics)
     return model, cpu_hash
 
 
+@pytest.mark.parametrize('semantics', ['cpu', 'cuda'])
 @pytest.mark.parametrize('scale_dtype', [torch.float32, torch.bfloat16])
-def test_tokens_match_reference_golden(cuda, golden, scale_dtype):
+def test_tokens_match_reference_golden(cuda, golden, scale_dtype, semantics):
+    """semantics='cpu': the golden's exact weights; 'cuda': the product's own quantiser (a few q differ)."""
     from efficientgpt_b200.fast_decode import GraphGreedyDecoder
-    model, h = _tiny(scale_dtype)
+    model, h = _tiny(scale_dtype, semantics=semantics)
     assert h == golden['tiny_qwen3']['state_sha256'], 'HF random init changed: golden tokens do not apply'
     key = 'fp32' if scale_dtype == torch.float32 else 'bf16'
     dec = GraphGreedyDecoder(model, max_cache_len=128)
@@ -58,13 +77,13 @@ def test_logits_match_reference_and_oracle(cuda, scale_dtype):
     from conftest import ROOT
     from efficientgpt_b200.engine import Qwen3Engine
     sd = torch.float32 if scale_dtype == 'fp32' else torch.bfloat16
-    model, _ = _tiny(sd)
+    model, _ = _tiny(sd, semantics='cpu')  # the golden's quantisation (see _quantize)
     eng = Qwen3Engine(model, 128, keep_logits=True)
     x = gi.tiny_prompts()[5]
     eng.prefill(x.cuda())
     z = np.load(ROOT / 'tests' / 'golden' / 'tiny_qwen3.npz')
     np.testing.assert_allclose(from_torch(eng.logits), from_bits(z[f'logits_p5_{scale_dtype}']), atol=1e-2, rtol=1e-2)
-    ref = Qwen3Ref.from_hf(gi.build_model(gi.tiny_config()), 128, scale_dtype)
+    ref = Qwen3Ref.from_hf(gi.build_model(gi.tiny_config()), 128, scale_dtype, semantics='cpu')
     lg = ref.forward(x[0].tolist(), 0)
     np.testing.assert_allclose(from_torch(eng.logits), lg, atol=1e-2, rtol=1e-2)
     pos = 5
@@ -135,12 +154,11 @@ def test_guards(cuda):
 def test_qwen3_1p7b_shape_matches_reference_golden(cuda, golden):
     """BASELINE config 2 at full size: the reference's 16 greedy tokens (CPU, bf16 scales) vs the native path."""
     from efficientgpt_b200.fast_decode import GraphGreedyDecoder
-    from efficientgpt_b200.int8_linear import quantize_model
     g = golden['qwen3_1p7b']
     model = gi.build_model(gi.qwen3_1p7b_config())
     assert gi.state_hash(model) == g['state_sha256'], 'HF random init changed: golden tokens do not apply'
     model = model.cuda()
-    quantize_model(model, scale_dtype=torch.bfloat16)
+    _quantize(model, torch.bfloat16, 'cpu')
     dec = GraphGreedyDecoder(model, max_cache_len=64)
     got, st = dec.generate(gi.big_prompt().cuda(), 16)
     ok, first, detail = parity.near_tie_match(g['tokens'], g['margins'], g['tops'], got)

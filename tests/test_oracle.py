@@ -29,12 +29,12 @@ def test_quantize_matches_reference_golden(golden):
     z = _npz('quantize.npz')
     w = gi.quantize_input()
     assert gi.sha(w) == golden['quantize']['w_sha256'], 'torch CPU generator changed: golden inputs differ'
-    q, s = int8_ref.quantize_weight(from_torch(w))
+    q, s = int8_ref.quantize_weight(from_torch(w), 'cpu')  # the golden ran on CPU
     np.testing.assert_array_equal(q, z['q'])
     np.testing.assert_array_equal(s, z['s'])
     e = gi.quantize_edge_rows()
     assert gi.sha(e) == golden['quantize']['edge_sha256']
-    qe, se = int8_ref.quantize_weight(e.numpy())
+    qe, se = int8_ref.quantize_weight(e.numpy(), 'cpu')
     np.testing.assert_array_equal(qe, z['edge_q'])
     np.testing.assert_array_equal(se, z['edge_s'])
 
@@ -51,6 +51,17 @@ def test_prefill_branch_matches_reference_golden(golden):
         ulp = np.maximum(np.abs(ref), 1e-30) * 2.0 ** -7
         assert np.all(diff <= ulp), (m, k, n)
         assert (diff > 0).mean() < 0.01, (m, k, n)
+
+
+def test_cuda_and_cpu_quantiser_semantics_differ_only_by_the_scalar_division():
+    w = from_torch(gi.quantize_input())
+    qc, sc = int8_ref.quantize_weight(w, 'cuda')
+    qh, sh = int8_ref.quantize_weight(w, 'cpu')
+    amax = np.abs(w).max(axis=1)
+    np.testing.assert_array_equal(sc, np.maximum(amax * np.float32(1 / 127), np.float32(1e-12)))
+    diff = sc != sh
+    assert diff.mean() < 0.5  # the reciprocal product is off by one ulp on a minority of rows
+    np.testing.assert_array_equal(qc[~diff], qh[~diff])
 
 
 def test_decode_branch_refuses_more_than_16_rows():
@@ -104,7 +115,7 @@ def test_tiny_model_greedy_tokens_match_reference(golden, scale_dtype):
     exact = 0
     for p, x in gi.tiny_prompts().items():
         run = golden['tiny_qwen3']['runs'][scale_dtype][str(p)]
-        ref = Qwen3Ref.from_hf(model, 128, scale_dtype)
+        ref = Qwen3Ref.from_hf(model, 128, scale_dtype, semantics='cpu')
         toks, _ = ref.generate(x[0].tolist(), 40)
         ok, first, detail = parity.near_tie_match(run['tokens'], run['margins'], run['tops'], toks)
         assert ok, (scale_dtype, p, detail)
@@ -117,7 +128,7 @@ def test_tiny_model_greedy_tokens_match_reference(golden, scale_dtype):
 def test_tiny_model_first_logits_match_reference(scale_dtype):
     z = _npz('tiny_qwen3.npz')
     model = gi.build_model(gi.tiny_config())
-    ref = Qwen3Ref.from_hf(model, 128, scale_dtype)
+    ref = Qwen3Ref.from_hf(model, 128, scale_dtype, semantics='cpu')
     x = gi.tiny_prompts()[5]
     lg = ref.forward(x[0].tolist(), 0)
     gold = from_bits(z[f'logits_p5_{scale_dtype}'])
