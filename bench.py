@@ -3,8 +3,8 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-A step is one decode token: one replay of the CUDA graph that holds the native decode step (141 kernels for
-28 layers). Workload = BASELINE config 2: random-init weights (seed 0), int8 per-row weights with bf16 scales,
+A step is one decode token: one replay of the CUDA graph that holds the native decode step (one persistent
+cooperative kernel per token; 141 kernels per token on the launch-sequence path). Workload = BASELINE config 2: random-init weights (seed 0), int8 per-row weights with bf16 scales,
 a 32-token uniform prompt, then 256 greedy tokens; the timed loop replays that 256-token window (position reset
 to 32 every 256 steps), so contexts run 33..288 as in the config. The 1.72 GB of weights streamed per token are
 far larger than L2 (126 MB), so no flush is needed between steps.
@@ -15,8 +15,11 @@ Printed JSON line (rank 0):
                per-token D2H token reads, (n - 1) / (total - ttft) as research/realmodel/bench_int8.py
   step_roofline  algorithmic bytes per token (weights + scales + norms + embedding row + KV at each step's
                context) / step time, against the measured HBM copy bandwidth
-  roofline     the dominant kernel (gemv_i8_tma_kernel): the step's 113 GEMV launches replayed alone as one
-               PDL-chained graph, algorithmic bytes / time; traffic from the committed ncu summary
+  roofline     the dominant kernel. Persistent step (default on this shape): decode_step_kernel, one launch
+               per token, so achieved = algorithmic bytes per token / (device time / K); traffic = its ncu
+               dram bytes per launch from the committed summary. Launch sequence: the step's GEMV launches
+               replayed alone as one PDL-chained graph (gemv_i8_kernel).
+  gemv_chain   the GEMV launches of the launch-sequence path replayed alone (for comparison)
   cpu_baseline the reference's CPU path (oracle/torch_ref.py) on this host's cores, bounded sample
 With N > 1 every rank runs an independent replica (no collective on the data path; scaling "weak").
 """
@@ -36,7 +39,7 @@ ROOT = Path(__file__).resolve().parent
 METRIC = 'batch-1 decode tok/s and % of HBM roofline, Qwen3-1.7B-shape int8, 1 B200'
 PROMPT_LEN, NEW_TOKENS = 32, 256
 FALLBACK_PEAKS = {'hbm_gbs': 6650.0}
-PROFILE_SUMMARY = ROOT / 'profiles' / 'gemv_i8_tma_kernel_qwen3_1p7b.md'
+PROFILE_SUMMARY = ROOT / 'profiles' / 'decode_step_kernel_qwen3_1p7b.md'
 
 
 def parse():
@@ -48,6 +51,7 @@ def parse():
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-pdl', action='store_true')
+    ap.add_argument('--launch-sequence', action='store_true', help='per-stage kernels instead of the persistent step')
     ap.add_argument('--cpu-sample', type=int, default=3, help='timed CPU decode tokens (after one warm-up token)')
     a = ap.parse_args()
     if a.warmup < 3:
@@ -142,18 +146,18 @@ def profile_traffic():
     """dram bytes read+write per launch of the dominant kernel, from the committed ncu summary (or None)."""
     if not PROFILE_SUMMARY.exists():
         return None
-    m = re.search(r'traffic_bytes_per_step_gemv\s*[:=]\s*([0-9.eE+]+)', PROFILE_SUMMARY.read_text())
+    m = re.search(r'traffic_bytes_per_launch\s*[:=]\s*([0-9.eE+]+)', PROFILE_SUMMARY.read_text())
     return float(m.group(1)) if m else None
 
 
-def build(device, pdl):
+def build(device, pdl, persistent=None):
     from efficientgpt_b200.configs import qwen3_1p7b_config, random_model
     from efficientgpt_b200.fast_decode import GraphGreedyDecoder
     from efficientgpt_b200.int8_linear import quantize_model
     model = random_model(qwen3_1p7b_config(), device, seed=0)
     quantize_model(model, scale_dtype=torch.bfloat16)
     torch.cuda.empty_cache()
-    dec = GraphGreedyDecoder(model, max_cache_len=PROMPT_LEN + NEW_TOKENS, pdl=pdl)
+    dec = GraphGreedyDecoder(model, max_cache_len=PROMPT_LEN + NEW_TOKENS, pdl=pdl, persistent=persistent)
     prompt = torch.randint(0, model.config.vocab_size, (1, PROMPT_LEN), generator=torch.Generator().manual_seed(0))
     return model, dec, prompt
 
@@ -257,7 +261,7 @@ def main():
     if a.impl == 'reference':
         run_reference(a, world, rank)
         return
-    model, dec, prompt = build('cuda', pdl=not a.no_pdl)
+    model, dec, prompt = build('cuda', pdl=not a.no_pdl, persistent=False if a.launch_sequence else None)
     eng = dec.engine
     dec._capture()
     eng.prefill(prompt.cuda())
@@ -288,13 +292,24 @@ def main():
     hbm = float(peaks['hbm_gbs'])
     step_gbs = bytes_tok / (ms / 1e3 / a.steps) / 1e9
 
-    # dominant kernel: the GEMV chain alone
+    # the GEMV launches of the launch-sequence path alone
     g, gemv_bytes, gemv_launches = gemv_chain_graph(eng)
     reps = 64
     time_replays(g, 4)
     gms = time_replays(g, reps) / reps
     gemv_gbs = gemv_bytes / (gms / 1e3) / 1e9
-    traffic = profile_traffic()
+    gemv = {'kernel': 'gemv_i8_kernel', 'achieved': round(gemv_gbs, 1), 'peak': hbm, 'unit': 'GB/s',
+            'frac': round(gemv_gbs / hbm, 4), 'launches_per_step': gemv_launches, 'bytes_per_step': gemv_bytes,
+            'avg_launch_us': round(gms * 1e3 / gemv_launches, 3)}
+    if eng.persistent:  # one launch per token: the kernel's duration is the step's device time
+        roofline = {'bound': 'hbm', 'kernel': 'decode_step_kernel', 'achieved': round(step_gbs, 1), 'peak': hbm,
+                    'unit': 'GB/s', 'frac': round(step_gbs / hbm, 4), 'traffic': profile_traffic(),
+                    'launches_per_step': 1, 'bytes_per_launch': round(bytes_tok),
+                    'avg_launch_us': round(ms * 1e3 / a.steps, 3), 'peak_source': peak_src}
+        launches = a.steps
+    else:
+        roofline = dict(gemv, bound='hbm', traffic=None, peak_source=peak_src)
+        launches = a.steps * (5 * eng.n_layers + 1)
 
     e2e = None
     if not a.no_e2e:
@@ -321,17 +336,15 @@ def main():
                        'new_tokens': NEW_TOKENS, 'scale_dtype': 'bf16', 'init': 'HF random init N(0,0.02), seed 0',
                        'parallelism': f'replicas{world}' if world > 1 else 'single',
                        'l2': 'no flush: 1.72 GB of weights streamed per step, larger than L2',
-                       'pdl': not a.no_pdl},
+                       'pdl': not a.no_pdl, 'step': 'persistent' if eng.persistent else 'launch sequence'},
             'tok_s_per_gpu': round(tok_s / world, 2),
             'step_roofline': {'bound': 'hbm', 'bytes_per_token': round(bytes_tok), 'achieved': round(step_gbs, 1),
                               'peak': hbm, 'unit': 'GB/s', 'frac': round(step_gbs / hbm, 4), 'peak_source': peak_src},
-            'roofline': {'bound': 'hbm', 'kernel': 'gemv_i8_tma_kernel', 'achieved': round(gemv_gbs, 1), 'peak': hbm,
-                         'unit': 'GB/s', 'frac': round(gemv_gbs / hbm, 4), 'traffic': traffic,
-                         'launches_per_step': gemv_launches, 'bytes_per_step': gemv_bytes,
-                         'avg_launch_us': round(gms * 1e3 / gemv_launches, 3), 'peak_source': peak_src},
+            'roofline': roofline,
+            'gemv_chain': gemv,
             'e2e': e2e,
             'cpu_baseline': cb,
-            'gpu_launches': a.steps * (5 * eng.n_layers + 1),
+            'gpu_launches': launches,
             'clocks': clocks,
         }
         print(json.dumps(line), flush=True)

@@ -17,6 +17,7 @@ EGPT_OK, EGPT_ERR_SHAPE, EGPT_ERR_DTYPE, EGPT_ERR_ALIGN, EGPT_ERR_LAUNCH, EGPT_E
 EGPT_F32, EGPT_BF16 = 0, 1
 EPI_NONE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_GELU = 0, 1, 2, 3
 FLAG_DOUBLE_ROUND, FLAG_RMSNORM, FLAG_PDL, FLAG_EMBED, FLAG_ADVANCE, FLAG_APPEND, FLAG_NO_TMA = 1, 2, 4, 8, 16, 32, 64
+FLAG_REF_SOFTMAX = 128
 
 _VALUE_ERRORS = {EGPT_ERR_SHAPE, EGPT_ERR_DTYPE, EGPT_ERR_ALIGN, EGPT_ERR_ARG, EGPT_ERR_WORKSPACE}
 
@@ -41,7 +42,8 @@ class Qwen3Plan(ctypes.Structure):
                 ('flags', ctypes.c_uint32), ('attn_max_split', ctypes.c_int32), ('layers', ctypes.POINTER(Qwen3Layer)),
                 ('embed', P), ('final_norm', P), ('w_lm', P), ('s_lm', P), ('rope_cos', P), ('rope_sin', P),
                 ('token', P), ('position', P), ('h', P), ('qkv', P), ('attn', P), ('act', P), ('logits', P),
-                ('attn_ws', P), ('attn_ws_bytes', SZ), ('lm_ws', P), ('lm_ws_bytes', SZ)]
+                ('attn_ws', P), ('attn_ws_bytes', SZ), ('lm_ws', P), ('lm_ws_bytes', SZ),
+                ('layers_dev', P), ('sync_ws', P), ('trace', P)]
 
 
 # name -> (restype, argtypes)
@@ -63,6 +65,9 @@ SIGNATURES = {
                                U32, P]),
     'egpt_argmax_rows': (I32, [P, P, I64, I64, I64, I32, P]),
     'egpt_decode_step': (I32, [ctypes.POINTER(Qwen3Plan), P]),
+    'egpt_step_sync_ws_bytes': (SZ, []),
+    'egpt_decode_step_persistent': (I32, [ctypes.POINTER(Qwen3Plan), P]),
+    'egpt_decode_step_persistent_check': (I32, [ctypes.POINTER(Qwen3Plan)]),
 }
 
 _lib = None

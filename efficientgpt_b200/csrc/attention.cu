@@ -6,15 +6,22 @@
 //   out = SDPA(q, K[0..pos], V[0..pos], scale = d^-0.5) with GQA (q head h reads kv head h / group).
 // Rounding points follow HF eager bf16: RMSNorm rounds x*rsqrt to bf16 then the weight product to bf16;
 // RoPE rounds q*cos, rotate_half(q)*sin and their sum to bf16; the cos/sin table is HF's own bf16 table.
-// Softmax runs in fp32 (online softmax); for bf16 caches the probabilities enter P.V rounded to bf16 (as in
-// the SDPA kernels the reference runs: PyTorch's CPU flash attention and the GPU memory-efficient kernel)
-// while the denominator sums fp32 values; the output is rounded once to the activation dtype.
+// Softmax runs in fp32. For bf16 caches the probabilities enter P.V rounded to bf16 while the denominator
+// sums fp32 values, and the reference point of that rounding follows the SDPA kernel the reference runs on the
+// GPU (fmha_cutlassF_bf16_aligned_64x128_rf_sm80, named by the reference's own profile of this path): it walks
+// the cache in 128-key blocks with a running maximum, so the keys of block j are rounded relative to the
+// maximum score over blocks 0..j. The output is rounded once to the activation dtype.
 //
 // Layout: caches are [nkv][cap][d] per layer, so the keys of one head are one contiguous stream.
 // Work split: grid (nkv, max_split, rows). A CTA owns one kv head, all `group` q heads that read it (K/V
-// are read once per group) and one key range. Each warp processes 32 keys per step: lane l holds dims
-// [l*d/32, (l+1)*d/32) of every key, so K/V rows are read fully coalesced; the 32 partial dot products
-// per head are reduced with a transpose-butterfly that leaves lane j holding key j's score.
+// are read once per group) and one range of whole 128-key blocks. Each warp processes 32 keys per step:
+// lane l holds dims [l*d/32, (l+1)*d/32) of every key, so K/V rows are read fully coalesced; the 32 partial
+// dot products per head are reduced with a transpose-butterfly that leaves lane l holding key l's score.
+// Pass A scores the range into shared memory (and prefetches the V rows into L2), the block maxima give the
+// running maximum of every block, pass B accumulates bf16(p) V per warp; warps merge in a fixed order and
+// split ranges combine by log-sum-exp in the last CTA of each kv head. The running maximum of the blocks
+// before the range comes from rescoring the keys [0, k0) (EGPT_FLAG_REF_SOFTMAX) or, in the persistent decode
+// step, from the other ranges through global memory; without the flag a range starts its own walk.
 #include <algorithm>
 
 #include "common.cuh"
@@ -22,9 +29,22 @@
 
 namespace egpt {
 
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = 256;  // 8 warps walk the key tiles
 constexpr int kAttnWarps = kAttnThreads / 32;
-constexpr int kKeysPerSplitTarget = 128;
+constexpr int kRefBlock = 128;     // keys per softmax block of the reference's GPU SDPA kernel
+constexpr int kKeyTile = 32;       // keys per warp step
+
+// Keys per split range whose scores fit the scratch ([group][keys] fp32 = 8 KB).
+__host__ __device__ constexpr int split_keys_max(int grp) { return 2048 / grp; }
+// Blocks per split range: ranges are whole 128-key blocks, at most max_split of them.
+__host__ __device__ inline int split_blocks(int64_t L, int max_split) {
+  const int64_t nb = (L + kRefBlock - 1) / kRefBlock;
+  return (int)((nb + max_split - 1) / max_split);
+}
+__host__ __device__ inline int split_count(int64_t L, int bps) {
+  const int64_t nb = (L + kRefBlock - 1) / kRefBlock;
+  return (int)((nb + bps - 1) / bps);
+}
 
 struct AttnParams {
   void *out;
@@ -168,64 +188,134 @@ __device__ __forceinline__ float transpose_reduce32(float (&s)[32]) {
   return s[0];
 }
 
+// ---------------------------------------------------------------------------------------------- core
+// Shared-memory scratch of one attention task (one kv head, its q heads, one key range).
+template <int DPL, int GRP>
+struct AttnScratch {
+  static constexpr int D = DPL * 32;
+  static constexpr int KS = split_keys_max(GRP);
+  float q[GRP][D];                        // rotated q heads (fp32 values of bf16 numbers)
+  float sc[GRP][KS];                      // scores of the range
+  float tmax[KS / kKeyTile][GRP];         // per-tile maxima
+  float pref[KS / kRefBlock][GRP];        // running maximum of each block of the range
+  float mb[GRP];                          // running maximum before the range (-inf: none)
+  float w_m[kAttnWarps][GRP], w_l[kAttnWarps][GRP];
+  float w_acc[kAttnWarps][GRP][D];
+  int flag;
+};
+
+template <int NT>
+__device__ __forceinline__ void nt_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory");
+}
+
+struct AttnTask {
+  const void *K, *V;  // this kv head's [cap][D] cache rows
+  int64_t k0, k1;     // key range [k0, k1), k0 a multiple of kRefBlock
+  float scale;
+};
+
+// Scores of keys t0 .. t0 + nkeys - 1 (nkeys <= 32) for every head of the group: lane l returns key t0 + l's.
 template <int DPL, int GRP, bool BF16>
-__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) {
+__device__ __forceinline__ void tile_scores(const void *K, int64_t t0, int nkeys, const float (&qv)[GRP][DPL],
+                                            float scale, float (&sc)[GRP]) {
   constexpr int D = DPL * 32;
-  __shared__ float q_s[GRP][D];
-  __shared__ float tmp[D];
-  __shared__ float red[32];
-  __shared__ float w_m[kAttnWarps][GRP], w_l[kAttnWarps][GRP];
-  __shared__ float w_acc[kAttnWarps][GRP][D];
-  __shared__ int s_last;
-
-  pdl_wait();
-  pdl_launch_dependents();
-
-  const int g = blockIdx.x, split = blockIdx.y;
-  const int64_t row = blockIdx.z;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t pos = *p.position + row;
-  const int64_t L = pos + 1;
-  if (L > p.cap || pos < 0) {
-    if (threadIdx.x == 0) set_device_error(EGPT_ERR_SHAPE);
-    return;
-  }
-  int nsplit = (int)((L + kKeysPerSplitTarget - 1) / kKeysPerSplitTarget);
-  nsplit = nsplit < 1 ? 1 : (nsplit > p.max_split ? p.max_split : nsplit);
-  if (split >= nsplit) return;
-  const int64_t chunk = (L + nsplit - 1) / nsplit;
-  const int64_t k0 = split * chunk;
-  const int64_t k1 = min(L, k0 + chunk);
-
-  const int64_t kv_base = (int64_t)g * p.cap * D;
-  // ---- q (and, with APPEND, this step's k/v) ----
-  if (p.flags & EGPT_FLAG_APPEND) {
-    const uint16_t *qkv = (const uint16_t *)p.q + row * p.ldq;
-    for (int j = 0; j < GRP; ++j)
-      head_norm_rope(qkv + (int64_t)(g * GRP + j) * D, p.q_norm_w, p.eps, p.rope_cos, p.rope_sin, pos, D, q_s[j],
-                     nullptr, tmp, red);
-    if (pos >= k0 && pos < k1) {  // this CTA's range holds the new slot: write it before reading the range
-      uint16_t *kd = (uint16_t *)p.k_cache + kv_base + pos * D;
-      head_norm_rope(qkv + (int64_t)(p.nq + g) * D, p.k_norm_w, p.eps, p.rope_cos, p.rope_sin, pos, D, tmp, kd,
-                     w_acc[0][0], red);
-      const uint16_t *vs = qkv + (int64_t)(p.nq + p.nkv + g) * D;
-      uint16_t *vd = (uint16_t *)p.v_cache + kv_base + pos * D;
-      for (int t = threadIdx.x; t < D; t += blockDim.x) vd[t] = vs[t];
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < GRP; ++j) {  // one head at a time keeps 32 partial sums live, not 32 x GRP
+    float part[32];
+#pragma unroll
+    for (int kk = 0; kk < 32; ++kk) {
+      float kv[4] = {0.f, 0.f, 0.f, 0.f};
+      if (kk < nkeys) load_dims<BF16>(K, (t0 + kk) * D + lane * DPL, kv, DPL);
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) s = fmaf(qv[j][e], kv[e], s);
+      part[kk] = s;
     }
-  } else {
-    for (int j = 0; j < GRP; ++j)
-      for (int t = threadIdx.x; t < D; t += blockDim.x)
-        q_s[j][t] = BF16 ? bf16_bits_to_f32(((const uint16_t *)p.q)[row * p.ldq + (int64_t)(g * GRP + j) * D + t])
-                         : ((const float *)p.q)[row * p.ldq + (int64_t)(g * GRP + j) * D + t];
+    sc[j] = transpose_reduce32(part) * scale;
   }
-  __syncthreads();
+}
 
-  // ---- per-warp online softmax over 32-key tiles ----
-  float qv[GRP][DPL];
+template <int DPL, int GRP>
+__device__ __forceinline__ void load_q(const AttnScratch<DPL, GRP> &S, float (&qv)[GRP][DPL]) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int j = 0; j < GRP; ++j)
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) qv[j][e] = q_s[j][lane * DPL + e];
+    for (int e = 0; e < DPL; ++e) qv[j][e] = S.q[j][lane * DPL + e];
+}
+
+// Pass A: scores of the range into S.sc, tile maxima into S.tmax, V rows of the range prefetched into L2.
+// Needs S.q; the caller synchronises afterwards.
+template <int DPL, int GRP, bool BF16>
+__device__ void attn_pass_a(const AttnTask &t, AttnScratch<DPL, GRP> &S) {
+  constexpr int D = DPL * 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (warp >= kAttnWarps) return;
+  float qv[GRP][DPL];
+  load_q(S, qv);
+  const int ntiles = (int)((t.k1 - t.k0 + kKeyTile - 1) / kKeyTile);
+  for (int ti = warp; ti < ntiles; ti += kAttnWarps) {
+    const int64_t t0 = t.k0 + (int64_t)ti * kKeyTile;
+    const int nkeys = (int)min((int64_t)kKeyTile, t.k1 - t0);
+    if (lane < nkeys) {
+      const char *vr = (const char *)t.V + (t0 + lane) * D * (BF16 ? 2 : 4);
+#pragma unroll
+      for (int off = 0; off < D * (BF16 ? 2 : 4); off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(vr + off));
+    }
+    float sc[GRP];
+    tile_scores<DPL, GRP, BF16>(t.K, t0, nkeys, qv, t.scale, sc);
+#pragma unroll
+    for (int j = 0; j < GRP; ++j) {
+      const float sj = lane < nkeys ? sc[j] : -INFINITY;
+      if (lane < nkeys) S.sc[j][ti * kKeyTile + lane] = sj;
+      const float mx = warp_max(sj);
+      if (lane == 0) S.tmax[ti][j] = mx;
+    }
+  }
+}
+
+// Running maximum before the range by rescoring keys [0, k0) into S.mb (uses S.w_m; synchronises inside).
+template <int DPL, int GRP, bool BF16, int NT>
+__device__ void attn_max_before(const AttnTask &t, AttnScratch<DPL, GRP> &S) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (warp < kAttnWarps) {
+    float qv[GRP][DPL];
+    load_q(S, qv);
+    float run[GRP];
+#pragma unroll
+    for (int j = 0; j < GRP; ++j) run[j] = -INFINITY;
+    for (int64_t t0 = (int64_t)warp * kKeyTile; t0 < t.k0; t0 += kKeyTile * kAttnWarps) {
+      const int nkeys = (int)min((int64_t)kKeyTile, t.k0 - t0);
+      float sc[GRP];
+      tile_scores<DPL, GRP, BF16>(t.K, t0, nkeys, qv, t.scale, sc);
+#pragma unroll
+      for (int j = 0; j < GRP; ++j) run[j] = fmaxf(run[j], warp_max(lane < nkeys ? sc[j] : -INFINITY));
+    }
+    if (lane == 0)
+#pragma unroll
+      for (int j = 0; j < GRP; ++j) S.w_m[warp][j] = run[j];
+  }
+  nt_sync<NT>();
+  if (threadIdx.x < GRP) {
+    float m = -INFINITY;
+    for (int w = 0; w < kAttnWarps; ++w) m = fmaxf(m, S.w_m[w][threadIdx.x]);
+    S.mb[threadIdx.x] = m;
+  }
+}
+
+// Walk the range in chunks of at most KS keys: pass A scores a chunk (unless `scored`: the caller already ran
+// pass A on a range of one chunk), the block maxima extend the running maximum (S.mb on entry: the running
+// maximum before the range), then pass B accumulates per warp sum_k bf16(exp(s_k - m_block)) V_k and
+// sum_k exp(s_k - m_block), rescaled in fp32 whenever a block raises the maximum. Tile i of the range is
+// walked by warp i % 8 in increasing order whatever the chunking. Warp partials end in S.w_*.
+template <int DPL, int GRP, bool BF16, int NT>
+__device__ void attn_walk(const AttnTask &t, AttnScratch<DPL, GRP> &S, bool scored) {
+  constexpr int D = DPL * 32;
+  constexpr int KS = AttnScratch<DPL, GRP>::KS;
+  constexpr int TPB = kRefBlock / kKeyTile;  // tiles per block
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float m_run[GRP], l_run[GRP], acc[GRP][DPL];
 #pragma unroll
   for (int j = 0; j < GRP; ++j) {
@@ -234,87 +324,112 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
 #pragma unroll
     for (int e = 0; e < DPL; ++e) acc[j][e] = 0.f;
   }
-  const void *K = p.k_cache, *V = p.v_cache;
-  for (int64_t t0 = k0 + (int64_t)warp * 32; t0 < k1; t0 += 32 * kAttnWarps) {
-    const int nkeys = (int)min((int64_t)32, k1 - t0);
-    float sc[GRP];
-    {
-      float part[GRP][32];
-#pragma unroll
-      for (int kk = 0; kk < 32; ++kk) {
-        float kv[4] = {0.f, 0.f, 0.f, 0.f};
-        if (kk < nkeys) load_dims<BF16>(K, kv_base + (t0 + kk) * D + lane * DPL, kv, DPL);
-#pragma unroll
-        for (int j = 0; j < GRP; ++j) {
-          float s = 0.f;
-#pragma unroll
-          for (int e = 0; e < DPL; ++e) s = fmaf(qv[j][e], kv[e], s);
-          part[j][kk] = s;
-        }
+  for (int64_t c0 = t.k0; c0 < t.k1; c0 += KS) {
+    AttnTask c = t;
+    c.k0 = c0;
+    c.k1 = min(t.k1, c0 + (int64_t)KS);
+    if (!scored || c0 > t.k0) {
+      nt_sync<NT>();  // the previous chunk's scores are consumed
+      attn_pass_a<DPL, GRP, BF16>(c, S);
+    }
+    const int ntiles = (int)((c.k1 - c.k0 + kKeyTile - 1) / kKeyTile);
+    nt_sync<NT>();
+    if (threadIdx.x < GRP) {
+      const int j = threadIdx.x;
+      const int nblk = (ntiles + TPB - 1) / TPB;
+      float run = S.mb[j];
+      for (int b = 0; b < nblk; ++b) {
+        for (int tt = b * TPB; tt < min((b + 1) * TPB, ntiles); ++tt) run = fmaxf(run, S.tmax[tt][j]);
+        S.pref[b][j] = run;
       }
-#pragma unroll
-      for (int j = 0; j < GRP; ++j) sc[j] = transpose_reduce32(part[j]) * p.scale;
+      S.mb[j] = run;  // running maximum before the next chunk
     }
-    // lane l now holds the score of key t0 + l for each head
-#pragma unroll
-    for (int j = 0; j < GRP; ++j) {
-      const float s = lane < nkeys ? sc[j] : -INFINITY;
-      const float tmax = warp_max(s);
-      const float m_new = fmaxf(m_run[j], tmax);
-      const float alpha = expf(m_run[j] - m_new);
-      const float pj = lane < nkeys ? expf(s - m_new) : 0.f;
-      l_run[j] = l_run[j] * alpha + warp_sum(pj);
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) acc[j][e] *= alpha;
-      m_run[j] = m_new;
-      sc[j] = pj;
-    }
-    for (int kk = 0; kk < nkeys; ++kk) {
-      float vv[4] = {0.f, 0.f, 0.f, 0.f};
-      load_dims<BF16>(V, kv_base + (t0 + kk) * D + lane * DPL, vv, DPL);
+    nt_sync<NT>();
+    if (warp >= kAttnWarps) continue;
+    for (int ti = warp; ti < ntiles; ti += kAttnWarps) {
+      const int64_t t0 = c.k0 + (int64_t)ti * kKeyTile;
+      const int nkeys = (int)min((int64_t)kKeyTile, c.k1 - t0);
+      const int b = ti / TPB;
+      float pj[GRP];
 #pragma unroll
       for (int j = 0; j < GRP; ++j) {
-        // bf16 inputs: probabilities enter P.V rounded to bf16 (the SDPA kernels' rounding point), while
-        // the denominator l sums the fp32 values.
-        const float p32 = __shfl_sync(0xffffffffu, sc[j], kk);
-        const float pk = BF16 ? round_bf16(p32) : p32;
+        const float mref = S.pref[b][j];
+        if (mref != m_run[j]) {  // a block raised the running maximum: bring the sums to it (fp32)
+          const float alpha = expf(m_run[j] - mref);
+          l_run[j] *= alpha;
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) acc[j][e] = fmaf(pk, vv[e], acc[j][e]);
+          for (int e = 0; e < DPL; ++e) acc[j][e] *= alpha;
+          m_run[j] = mref;
+        }
+        const float p = lane < nkeys ? expf(S.sc[j][ti * kKeyTile + lane] - mref) : 0.f;
+        l_run[j] += warp_sum(p);
+        pj[j] = p;
+      }
+      for (int kk = 0; kk < nkeys; ++kk) {
+        float vv[4] = {0.f, 0.f, 0.f, 0.f};
+        load_dims<BF16>(t.V, (t0 + kk) * D + lane * DPL, vv, DPL);
+#pragma unroll
+        for (int j = 0; j < GRP; ++j) {
+          const float p32 = __shfl_sync(0xffffffffu, pj[j], kk);
+          const float pk = BF16 ? round_bf16(p32) : p32;
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) acc[j][e] = fmaf(pk, vv[e], acc[j][e]);
+        }
       }
     }
   }
-  // ---- merge the warps (fixed order) ----
+  const int64_t ntot = (t.k1 - t.k0 + kKeyTile - 1) / kKeyTile;
+  if (warp < min((int64_t)kAttnWarps, ntot)) {
 #pragma unroll
-  for (int j = 0; j < GRP; ++j) {
-    if (lane == 0) {
-      w_m[warp][j] = m_run[j];
-      w_l[warp][j] = l_run[j];
+    for (int j = 0; j < GRP; ++j) {
+      if (lane == 0) {
+        S.w_m[warp][j] = m_run[j];
+        S.w_l[warp][j] = l_run[j];
+      }
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) S.w_acc[warp][j][lane * DPL + e] = acc[j][e];
     }
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) w_acc[warp][j][lane * DPL + e] = acc[j][e];
   }
-  __syncthreads();
-  const bool single = nsplit == 1;
-  for (int idx = threadIdx.x; idx < GRP * D; idx += blockDim.x) {
+}
+
+struct AttnOut {
+  void *out;          // this row's output; head h at element offset h * D
+  float *part;        // this row's split partials: head h, split s at (h * max_split + s) * (D + 2)
+  unsigned *cnt;      // combine counter of this (row, kv head)
+  int g, split, nsplit, max_split, busy;
+};
+
+template <bool BF16>
+__device__ __forceinline__ void store_out(void *out, int64_t i, float v) {
+  if (BF16)
+    ((uint16_t *)out)[i] = f32_to_bf16_bits(v);
+  else
+    ((float *)out)[i] = v;
+}
+
+// Merge the warps (fixed order); one range: write the output; several: write the partial, and the last
+// range of this kv head to arrive combines all of them.
+template <int DPL, int GRP, bool BF16, int NT>
+__device__ void attn_finish(AttnScratch<DPL, GRP> &S, const AttnOut &o) {
+  constexpr int D = DPL * 32;
+  nt_sync<NT>();
+  const bool single = o.nsplit == 1;
+  for (int idx = threadIdx.x; idx < GRP * D; idx += NT) {
     const int j = idx / D, dd = idx - j * D;
     float M = -INFINITY;
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, w_m[w][j]);
+    for (int w = 0; w < o.busy; ++w) M = fmaxf(M, S.w_m[w][j]);
     float lsum = 0.f, a = 0.f;
-    for (int w = 0; w < kAttnWarps; ++w) {
-      if (w_l[w][j] == 0.f) continue;
-      const float f = expf(w_m[w][j] - M);
-      lsum += w_l[w][j] * f;
-      a += w_acc[w][j][dd] * f;
+    for (int w = 0; w < o.busy; ++w) {
+      if (S.w_l[w][j] == 0.f) continue;
+      const float f = expf(S.w_m[w][j] - M);
+      lsum += S.w_l[w][j] * f;
+      a += S.w_acc[w][j][dd] * f;
     }
-    const int h = g * GRP + j;
+    const int h = o.g * GRP + j;
     if (single) {
-      const float o = a / lsum;
-      if (BF16)
-        ((uint16_t *)p.out)[row * p.ldo + (int64_t)h * D + dd] = f32_to_bf16_bits(o);
-      else
-        ((float *)p.out)[row * p.ldo + (int64_t)h * D + dd] = o;
+      store_out<BF16>(o.out, (int64_t)h * D + dd, a / lsum);
     } else {
-      float *slot = p.ws_f + (((row * p.nq + h) * p.max_split) + split) * (D + 2);
+      float *slot = o.part + ((int64_t)h * o.max_split + o.split) * (D + 2);
       slot[2 + dd] = a;
       if (dd == 0) {
         slot[0] = M;
@@ -323,38 +438,105 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
     }
   }
   if (single) return;
-  // ---- last CTA of this (row, kv head) combines the splits ----
   __threadfence();
-  __syncthreads();
+  nt_sync<NT>();
   if (threadIdx.x == 0) {
-    unsigned *cnt = p.ws_cnt + row * p.nkv + g;
-    const unsigned prev = atomicAdd(cnt, 1u);
-    s_last = prev == (unsigned)(nsplit - 1);
-    if (s_last) *cnt = 0u;
+    const unsigned prev = atomicAdd(o.cnt, 1u);
+    S.flag = prev == (unsigned)(o.nsplit - 1);
+    if (S.flag) *o.cnt = 0u;
   }
-  __syncthreads();
-  if (!s_last) return;
+  nt_sync<NT>();
+  if (!S.flag) return;
   __threadfence();
-  for (int idx = threadIdx.x; idx < GRP * D; idx += blockDim.x) {
+  for (int idx = threadIdx.x; idx < GRP * D; idx += NT) {
     const int j = idx / D, dd = idx - j * D;
-    const int h = g * GRP + j;
-    const float *base = p.ws_f + ((row * p.nq + h) * p.max_split) * (D + 2);
+    const int h = o.g * GRP + j;
+    const float *base = o.part + (int64_t)h * o.max_split * (D + 2);
     float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(base + s * (D + 2)));
+    for (int s = 0; s < o.nsplit; ++s) M = fmaxf(M, __ldcg(base + s * (D + 2)));
     float lsum = 0.f, a = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
+    for (int s = 0; s < o.nsplit; ++s) {
       const float ls = __ldcg(base + s * (D + 2) + 1);
       if (ls == 0.f) continue;
       const float f = expf(__ldcg(base + s * (D + 2)) - M);
       lsum += ls * f;
       a += __ldcg(base + s * (D + 2) + 2 + dd) * f;
     }
-    const float o = a / lsum;
-    if (BF16)
-      ((uint16_t *)p.out)[row * p.ldo + (int64_t)h * D + dd] = f32_to_bf16_bits(o);
-    else
-      ((float *)p.out)[row * p.ldo + (int64_t)h * D + dd] = o;
+    store_out<BF16>(o.out, (int64_t)h * D + dd, a / lsum);
   }
+}
+
+// ---------------------------------------------------------------------------------------------- split kernel
+template <int DPL, int GRP, bool BF16>
+__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) {
+  constexpr int D = DPL * 32;
+  __shared__ AttnScratch<DPL, GRP> S;
+  __shared__ float tmp[D];
+  __shared__ float red[32];
+
+  pdl_wait();
+  pdl_launch_dependents();
+
+  const int g = blockIdx.x, split = blockIdx.y;
+  const int64_t row = blockIdx.z;
+  const int64_t pos = *p.position + row;
+  const int64_t L = pos + 1;
+  if (L > p.cap || pos < 0) {
+    if (threadIdx.x == 0) set_device_error(EGPT_ERR_SHAPE);
+    return;
+  }
+  const int bps = split_blocks(L, p.max_split);
+  const int nsplit = split_count(L, bps);
+  if (split >= nsplit) return;
+  const int64_t k0 = (int64_t)split * bps * kRefBlock;
+  const int64_t k1 = min(L, k0 + (int64_t)bps * kRefBlock);
+
+  const int64_t kv_base = (int64_t)g * p.cap * D;
+  // ---- q (and, with APPEND, this step's k/v) ----
+  if (p.flags & EGPT_FLAG_APPEND) {
+    const uint16_t *qkv = (const uint16_t *)p.q + row * p.ldq;
+    for (int j = 0; j < GRP; ++j)
+      head_norm_rope(qkv + (int64_t)(g * GRP + j) * D, p.q_norm_w, p.eps, p.rope_cos, p.rope_sin, pos, D, S.q[j],
+                     nullptr, tmp, red);
+    if (pos >= k0 && pos < k1) {  // this CTA's range holds the new slot: write it before reading the range
+      uint16_t *kd = (uint16_t *)p.k_cache + kv_base + pos * D;
+      head_norm_rope(qkv + (int64_t)(p.nq + g) * D, p.k_norm_w, p.eps, p.rope_cos, p.rope_sin, pos, D, tmp, kd,
+                     S.w_acc[0][0], red);
+      const uint16_t *vs = qkv + (int64_t)(p.nq + p.nkv + g) * D;
+      uint16_t *vd = (uint16_t *)p.v_cache + kv_base + pos * D;
+      for (int t = threadIdx.x; t < D; t += blockDim.x) vd[t] = vs[t];
+    }
+  } else {
+    for (int j = 0; j < GRP; ++j)
+      for (int t = threadIdx.x; t < D; t += blockDim.x)
+        S.q[j][t] = BF16 ? bf16_bits_to_f32(((const uint16_t *)p.q)[row * p.ldq + (int64_t)(g * GRP + j) * D + t])
+                         : ((const float *)p.q)[row * p.ldq + (int64_t)(g * GRP + j) * D + t];
+  }
+  __syncthreads();
+
+  const size_t esz = BF16 ? 2 : 4;
+  AttnTask t;
+  t.K = (const char *)p.k_cache + kv_base * esz;
+  t.V = (const char *)p.v_cache + kv_base * esz;
+  t.k0 = k0;
+  t.k1 = k1;
+  t.scale = p.scale;
+  if ((p.flags & EGPT_FLAG_REF_SOFTMAX) && k0 > 0) {
+    attn_max_before<DPL, GRP, BF16, kAttnThreads>(t, S);
+  } else if (threadIdx.x < GRP) {
+    S.mb[threadIdx.x] = -INFINITY;
+  }
+  attn_walk<DPL, GRP, BF16, kAttnThreads>(t, S, false);
+  AttnOut o;
+  o.out = (char *)p.out + row * p.ldo * esz;
+  o.part = p.ws_f ? p.ws_f + row * p.nq * p.max_split * (D + 2) : nullptr;
+  o.cnt = p.ws_cnt ? p.ws_cnt + row * p.nkv + g : nullptr;
+  o.g = g;
+  o.split = split;
+  o.nsplit = nsplit;
+  o.max_split = p.max_split;
+  o.busy = (int)min((int64_t)kAttnWarps, (k1 - k0 + kKeyTile - 1) / kKeyTile);
+  attn_finish<DPL, GRP, BF16, kAttnThreads>(S, o);
 }
 
 template <int DPL, bool BF16>
@@ -415,10 +597,16 @@ extern "C" int egpt_qk_norm_rope_kv_append(void *q_out, const void *qkv, int64_t
                       "qk_norm_rope_append_kernel");
 }
 
+// Workspace layout: fp32 split partials [m][nq][max_split][d + 2] and range maxima [m][nq][max_split]
+// (padded to 256 bytes), then u32 counters [3][m][nkv]: combine arrivals, max-exchange arrivals and
+// max-exchange generation (the last two are used by the persistent decode step).
+size_t attn_ws_float_bytes(int64_t m, int nq, int d, int max_split) {
+  const size_t floats = (size_t)m * nq * max_split * (d + 3);
+  return (floats * 4 + 255) / 256 * 256;
+}
+
 extern "C" size_t egpt_attn_ws_bytes(int64_t m, int nq, int nkv, int d, int max_split) {
-  const size_t floats = (size_t)m * nq * max_split * (d + 2);
-  const size_t fbytes = (floats * 4 + 255) / 256 * 256;
-  return fbytes + (size_t)m * nkv * 4;
+  return attn_ws_float_bytes(m, nq, d, max_split) + 3 * (size_t)m * nkv * 4;
 }
 
 extern "C" int egpt_attn_decode(void *out, int64_t ldo, const void *q, int64_t ldq, void *k_cache, void *v_cache,
@@ -464,7 +652,7 @@ extern "C" int egpt_attn_decode(void *out, int64_t ldo, const void *q, int64_t l
   p.scale = scale;
   p.max_split = max_split;
   p.ws_f = (float *)ws;
-  p.ws_cnt = ws ? (unsigned *)((char *)ws + (egpt_attn_ws_bytes(m, nq, nkv, d, max_split) - (size_t)m * nkv * 4)) : nullptr;
+  p.ws_cnt = ws ? (unsigned *)((char *)ws + attn_ws_float_bytes(m, nq, d, max_split)) : nullptr;
   p.flags = flags;
   const dim3 grid(nkv, max_split, (unsigned)m);
   const bool pdl = (flags & EGPT_FLAG_PDL) != 0;

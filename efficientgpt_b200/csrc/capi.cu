@@ -39,6 +39,18 @@ int num_sms() {
   return cache[dev];
 }
 
+size_t smem_limit() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 227 * 1024;
+  if (!cache[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0) v = 227 * 1024;
+    cache[dev] = v;
+  }
+  return (size_t)cache[dev];
+}
+
 }  // namespace egpt
 
 using namespace egpt;
@@ -87,7 +99,8 @@ extern "C" int egpt_decode_step(const egpt_qwen3_plan *P, void *stream) {
     if (rc) return rc;
     rc = egpt_attn_decode(P->attn, NQ * D, P->qkv, nqkv, L.k_cache, L.v_cache, P->cap, P->position, 1, (int)NQ,
                           (int)NKV, (int)D, L.q_norm, L.k_norm, P->eps, P->rope_cos, P->rope_sin, P->attn_scale,
-                          P->attn_max_split, P->attn_ws, P->attn_ws_bytes, EGPT_BF16, EGPT_FLAG_APPEND | pdl, stream);
+                          P->attn_max_split, P->attn_ws, P->attn_ws_bytes, EGPT_BF16,
+                          EGPT_FLAG_APPEND | EGPT_FLAG_REF_SOFTMAX | pdl, stream);
     if (rc) return rc;
     rc = egpt_gemv_i8(P->h, P->attn, EGPT_BF16, 1, NQ * D, H, L.w_o, L.s_o, sdt, H, NQ * D, nullptr, P->h,
                       EGPT_EPI_RESIDUAL, nullptr, 0.f, nullptr, pdl, stream);

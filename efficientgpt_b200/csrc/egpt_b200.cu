@@ -4,3 +4,4 @@
 #include "elementwise.cu"
 #include "gemv_i8.cu"
 #include "attention.cu"
+#include "decode_step.cu"

@@ -18,6 +18,8 @@ void clear_error();
 int check_launch(cudaError_t e, const char *what);
 // SM count of the current device (cached per device).
 int num_sms();
+// Largest dynamic shared memory one CTA may opt in to on the current device (bytes).
+size_t smem_limit();
 
 // cudaLaunchKernelExC wrapper: optional programmatic-stream-serialization attribute (PDL).
 template <typename... Args>

@@ -30,7 +30,9 @@ def _ptr(t):
 
 
 class Qwen3Engine:
-    def __init__(self, model, max_cache_len, pdl=True, attn_max_split=None, keep_logits=False):
+    def __init__(self, model, max_cache_len, pdl=True, attn_max_split=None, keep_logits=False, persistent=None):
+        """persistent: True = one cooperative kernel per token (egpt_decode_step_persistent), False = the
+        per-stage launch sequence (egpt_decode_step), None = persistent when the model's shapes allow it."""
         if not torch.cuda.is_available():
             raise RuntimeError('Qwen3Engine needs a CUDA device (there is no CPU path)')
         self.model = model
@@ -111,11 +113,17 @@ class Qwen3Engine:
         self.act = torch.zeros(self.inter, dtype=torch.bfloat16, device=dev)
         self.logits = torch.zeros(self.vocab, dtype=torch.bfloat16, device=dev) if keep_logits else None
         nsm = L.load().egpt_num_sms()
-        self.attn_max_split = attn_max_split or max(1, min(64, math.ceil(nsm / self.nkv)))
+        self.attn_max_split = attn_max_split or max(1, min(64, nsm // self.nkv))
         self.attn_ws = ops.attn_ws(1, self.nq, self.nkv, self.d, self.attn_max_split, dev)
         self.lm_ws = ops.lm_head_ws(self.vocab, dev)
+        self.sync_ws = torch.zeros(int(L.load().egpt_step_sync_ws_bytes()), dtype=torch.uint8, device=dev)
         self.pdl = pdl
         self._build_plan()
+        fits = self.vocab // 2 >= nsm and L.load().egpt_decode_step_persistent_check(ctypes.byref(self.plan)) == 0
+        if persistent and not fits:
+            raise ValueError('the persistent decode step is not built for this model shape: '
+                             + L.last_error())
+        self.persistent = fits if persistent is None else bool(persistent)
 
     def _build_plan(self):
         arr = (L.Qwen3Layer * self.n_layers)()
@@ -141,14 +149,21 @@ class Qwen3Engine:
         p.logits = self.logits.data_ptr() if self.logits is not None else None
         p.attn_ws, p.attn_ws_bytes = self.attn_ws.data_ptr(), self.attn_ws.numel()
         p.lm_ws, p.lm_ws_bytes = self.lm_ws.data_ptr(), self.lm_ws.numel()
+        raw = bytes(memoryview(arr).cast('B'))
+        self.layers_dev = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(self.device)
+        p.layers_dev = self.layers_dev.data_ptr()
+        p.sync_ws = self.sync_ws.data_ptr()
         self._layer_arr = arr  # keep alive
         self.plan = p
 
     # ------------------------------------------------------------------------------------------ decode
     def step(self):
         """One decode token on the current stream: token <- argmax(model(token, position)); position += 1."""
-        L.check(L.load().egpt_decode_step(ctypes.byref(self.plan), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
-                'decode_step')
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        if self.persistent:
+            L.check(L.load().egpt_decode_step_persistent(ctypes.byref(self.plan), stream), 'decode_step_persistent')
+        else:
+            L.check(L.load().egpt_decode_step(ctypes.byref(self.plan), stream), 'decode_step')
 
     # ------------------------------------------------------------------------------------------ prefill
     def _linear(self, x, w, s, **kw):
@@ -172,7 +187,7 @@ class Qwen3Engine:
                                            q_norm_w=lay['q_norm'], k_norm_w=lay['k_norm'], eps=self.eps,
                                            rope_cos=self.rope_cos, rope_sin=self.rope_sin)
             a = ops.attn_decode(q, self.kv[i, 0], self.kv[i, 1], self.position, self.nq, self.nkv, self.d,
-                                scale=self.scale, max_split=self.attn_max_split, ws=ws)
+                                scale=self.scale, max_split=self.attn_max_split, ws=ws, ref_softmax=True)
             h = self._linear(a, lay['w_o'], lay['s_o'], epilogue=L.EPI_RESIDUAL, residual=h)
             x = ops.rmsnorm(h, lay['ln_post'], self.eps)
             act = self._linear(x, lay['w_gu'], lay['s_gu'], epilogue=L.EPI_SILU_MUL)

@@ -22,9 +22,9 @@ from .engine import Qwen3Engine
 class GraphGreedyDecoder:
     """One CUDA graph per decode step; token and position live on the device."""
 
-    def __init__(self, model, max_cache_len, lookahead=8, pdl=True):
+    def __init__(self, model, max_cache_len, lookahead=8, pdl=True, persistent=None):
         self.model, self.max_cache_len, self.lookahead = model, max_cache_len, lookahead
-        self.engine = Qwen3Engine(model, max_cache_len, pdl=pdl)
+        self.engine = Qwen3Engine(model, max_cache_len, pdl=pdl, persistent=persistent)
         self.device = self.engine.device
         self.token = self.engine.token
         self.position = self.engine.position

@@ -54,6 +54,7 @@ extern "C" {
 #define EGPT_FLAG_ADVANCE 16u     /* lm_head argmax: also *position += 1                                  */
 #define EGPT_FLAG_APPEND 32u      /* attention: q/k-RMSNorm + RoPE + KV append of this step's row in-kernel */
 #define EGPT_FLAG_NO_TMA 64u      /* GEMV: force the plain-load kernel (any K)                            */
+#define EGPT_FLAG_REF_SOFTMAX 128u /* attention: bf16 probabilities rounded as the reference GPU kernel does */
 
 /* ---- library ---------------------------------------------------------------------------------------- */
 EGPT_API const char *egpt_version(void);
@@ -119,8 +120,11 @@ EGPT_API int egpt_embed(void *out, const int64_t *ids, int64_t rows, const void 
  * egpt_attn_decode: out[i, h] = softmax(scale * q_i,h . K[0..L_i)) V[0..L_i), L_i = pos0 + i + 1, GQA head
  *   h uses kv head h / (nq / nkv). With EGPT_FLAG_APPEND (m must be 1) the norm/RoPE/append above is done
  *   in-kernel from the raw qkv row, else q comes from q (ldq) already rotated.
- *   Work is split over up to max_split key ranges per kv head; ws must hold
+ *   Work is split over up to max_split ranges of whole 128-key blocks per kv head; ws must hold
  *   egpt_attn_ws_bytes(m, nq, nkv, d, max_split) bytes, zero-filled once before first use.
+ *   bf16: probabilities enter P.V rounded to bf16. With EGPT_FLAG_REF_SOFTMAX they are rounded relative to
+ *   the running maximum of the 128-key block walk of the reference's GPU SDPA kernel (a range then rescores
+ *   the keys before it); without it each range starts its own walk (same accuracy, less work).
  *   dtype: bf16 (Qwen) or fp32 (nanoGPT, no norm/RoPE). */
 EGPT_API int egpt_qk_norm_rope_kv_append(void *q_out, const void *qkv, int64_t ldqkv, void *k_cache, void *v_cache,
                                 int64_t cap, const int64_t *position, int64_t m, int nq, int nkv, int d,
@@ -178,9 +182,30 @@ typedef struct egpt_qwen3_plan {
   size_t attn_ws_bytes;
   void *lm_ws;
   size_t lm_ws_bytes;
+  /* used by egpt_decode_step_persistent only */
+  const egpt_qwen3_layer *layers_dev; /* device copy of `layers`                                          */
+  void *sync_ws;                /* egpt_step_sync_ws_bytes() bytes, zero-filled once (grid barrier state) */
+  uint64_t *trace;              /* nullable: 5 + 15 * n_layers %globaltimer stamps (ns) written by CTA 0:
+                                   [0] start, [1+2b] / [2+2b] arrival at / release from grid barrier b,
+                                   [1+2B] lm_head stage done, [2+2B] token written, [3+2B] unused,
+                                   [4+2B+k] stage k's input ready (k < B: the stage before barrier k+1;
+                                   k = B: lm_head) (B = 5 * n_layers barriers)                            */
 } egpt_qwen3_plan;
 
 EGPT_API int egpt_decode_step(const egpt_qwen3_plan *plan, void *stream);
+
+/* Persistent variant of egpt_decode_step: the whole token in ONE cooperative kernel with one CTA per SM.
+ * Every warp streams its share of every weight matrix of the step (row pairs, 2048-column chunks) through
+ * its own shared-memory ring (cp.async, 3 chunks in flight, plus L2 prefetch further ahead) across stage
+ * boundaries, while the CTAs run the stages separated by bounded grid barriers; same arithmetic and results
+ * as egpt_decode_step. Needs plan->layers_dev and plan->sync_ws; after a device error (egpt_device_error)
+ * sync_ws and the workspaces must be zero-filled again. Built for head_dim 128 with 2 or 4 q heads per kv
+ * head and head_dim 32 with 2; other shapes, and activations too wide for shared memory next to the ring
+ * (max(hidden, intermediate, nq*d) above about 6400 on a 227 KB part), return EGPT_ERR_SHAPE.
+ * egpt_decode_step_persistent_check runs the same host-side checks without launching anything. */
+EGPT_API size_t egpt_step_sync_ws_bytes(void);
+EGPT_API int egpt_decode_step_persistent(const egpt_qwen3_plan *plan, void *stream);
+EGPT_API int egpt_decode_step_persistent_check(const egpt_qwen3_plan *plan);
 
 #ifdef __cplusplus
 }

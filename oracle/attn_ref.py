@@ -24,11 +24,23 @@ def decode_attention_truth(q, k, v, length, scale):
     return out
 
 
-def decode_attention_fp32(q, k, v, length, scale, p_bf16=False):
-    """Single-pass fp32 softmax attention, [nq, d] float32: s = (K q) * scale, p = exp(s - max s),
-    out = (p @ V) / sum(p). With p_bf16 the probabilities enter p @ V rounded to bf16 while the denominator
-    sums the fp32 values: the rounding point of the SDPA kernels that serve bf16 inputs (PyTorch's CPU flash
-    attention and the GPU memory-efficient/flash kernels both feed bf16 probabilities to the second product)."""
+# Keys per softmax block of the SDPA kernel the reference runs for bf16 decode on the GPU
+# (fmha_cutlassF_bf16_aligned_64x128_rf_sm80: 64 queries x 128 keys per iteration; the reference's own profile of
+# the int8 decode path names it). It walks the cache in 128-key blocks with a running maximum and feeds each
+# block's probabilities, rounded to bf16 relative to the running maximum, to the P.V product.
+REF_KEY_BLOCK = 128
+
+
+def decode_attention_fp32(q, k, v, length, scale, p_bf16=False, block=None):
+    """fp32 softmax attention, [nq, d] float32: s = (K q) * scale, p = exp(s - m), out = (p @ V) / sum(p).
+
+    With p_bf16 the probabilities enter p @ V rounded to bf16 while the denominator sums the fp32 values: the
+    rounding point of the SDPA kernels that serve bf16 inputs (PyTorch's CPU flash attention and the GPU
+    memory-efficient kernel both feed bf16 probabilities to the second product). The reference point m of that
+    rounding is the maximum over all keys when block is None (one block: what both kernels do while the
+    cache fits one of their key blocks), else the running maximum of the kernel's block walk: keys of block
+    j = [j*block, (j+1)*block) are rounded relative to max(s[0 : (j+1)*block]), and the blocks' sums are
+    brought to the final maximum in fp32 (exp(m_j - M) factors)."""
     q = np.asarray(q, np.float32)
     k = np.asarray(k, np.float32)[:, :length]
     v = np.asarray(v, np.float32)[:, :length]
@@ -37,9 +49,23 @@ def decode_attention_fp32(q, k, v, length, scale, p_bf16=False):
     out = np.empty_like(q)
     for h in range(nq):
         s = (k[h // grp] @ q[h]) * np.float32(scale)
-        p = np.exp(s - s.max())
-        num = (round_bf16(p) if p_bf16 else p) @ v[h // grp]
-        out[h] = num / p.sum(dtype=np.float32)
+        if block is None or length <= block:
+            p = np.exp(s - s.max())
+            num = (round_bf16(p) if p_bf16 else p) @ v[h // grp]
+            out[h] = num / p.sum(dtype=np.float32)
+            continue
+        M = s.max()
+        num = np.zeros(v.shape[-1], np.float32)
+        den = np.float32(0)
+        run = -np.inf
+        for a in range(0, length, block):
+            b = min(length, a + block)
+            run = max(run, s[a:b].max())
+            p = np.exp(s[a:b] - run)
+            f = np.float32(np.exp(np.float32(run - M)))
+            num += f * ((round_bf16(p) if p_bf16 else p) @ v[h // grp, a:b])
+            den += f * p.sum(dtype=np.float32)
+        out[h] = num / den
     return out
 
 

@@ -34,3 +34,19 @@ def near_tie_match(ref_tokens, ref_margins, ref_tops, got_tokens):
             ok = ref_margins[i] <= thr
             return ok, i, f'step {i}: ref margin {ref_margins[i]:.5g}, near-tie threshold {thr:.5g}'
     return True, None, 'identical'
+
+
+def logits_close(got, want, atol=1e-2, rtol=1e-2, frac=0.99, hard=4e-2):
+    """Logit rule for long sequences. fp32 transcendental functions of CUDA (expf in softmax and SiLU, rsqrtf in
+    RMSNorm) and of numpy can differ by one fp32 ulp; now and then that moves a value across a bf16 rounding
+    boundary, and a high-gain model carries the flip into a few bf16 ulps of the logits. The rule: at least
+    `frac` of the logits within atol + rtol |want|, and every logit within `hard` + rtol |want|.
+    Returns (ok, detail)."""
+    import numpy as np
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    d = np.abs(got - want)
+    soft = d <= atol + rtol * np.abs(want)
+    firm = d <= hard + rtol * np.abs(want)
+    ok = bool(soft.mean() >= frac and firm.all())
+    return ok, f'within 1e-2: {soft.mean():.4f}, max |diff| {d.max():.4g}'

@@ -7,14 +7,15 @@ op (research/realmodel/int8_linear.py:88-157):
   RMSNorm      modeling_qwen3.py:59-64   w * bf16(x * rsqrt(mean(x^2) + eps))
   RoPE         modeling_qwen3.py:137-148 cos/sin of inv_freq * pos in fp32, cast to bf16; :159-180 rotate-half
   attention    modeling_qwen3.py:258-291 q/k norm after the projections, RoPE, cache write, GQA SDPA, o_proj
-               (SDPA with fp32 scores/softmax and bf16 probabilities into P.V, see attn_ref)
+               (SDPA with fp32 scores/softmax and bf16 probabilities into P.V, rounded per 128-key block of
+               the reference GPU kernel's cache walk, see attn_ref.REF_KEY_BLOCK)
   MLP          modeling_qwen3.py:81-82   down(bf16(silu(gate)) * up)
   layer        modeling_qwen3.py:305-335 bf16 residual adds
   lm_head      modeling_qwen3.py:503-505 int8 op on the last row only, bf16 logits; argmax, first index on ties
 """
 import numpy as np
 
-from .attn_ref import decode_attention_fp32
+from .attn_ref import REF_KEY_BLOCK, decode_attention_fp32
 from .bf16 import from_torch, round_bf16
 from .int8_ref import int8_linear, int8_matmul, quantize_weight
 
@@ -116,7 +117,8 @@ class Qwen3Ref:
             k = apply_rope(rmsnorm(k, L['k_norm'], eps), cos, sin)
             self.k[li, :, pos0:pos0 + m] = k.transpose(1, 0, 2)
             self.v[li, :, pos0:pos0 + m] = v.transpose(1, 0, 2)
-            o = np.stack([decode_attention_fp32(q[i], self.k[li], self.v[li], pos0 + i + 1, scale, p_bf16=True)
+            o = np.stack([decode_attention_fp32(q[i], self.k[li], self.v[li], pos0 + i + 1, scale, p_bf16=True,
+                                                block=REF_KEY_BLOCK)
                           for i in range(m)])
             o = round_bf16(o).reshape(m, nq * d)
             h = round_bf16(h + int8_linear(o, *L['o']))

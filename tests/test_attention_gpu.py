@@ -7,7 +7,7 @@ import torch
 import torch.nn.functional as F
 
 from oracle import attn_ref
-from oracle.bf16 import from_torch
+from oracle.bf16 import from_torch, round_bf16
 from oracle.qwen3_ref import apply_rope, rmsnorm
 
 pytestmark = pytest.mark.gpu
@@ -58,6 +58,33 @@ def test_split_count_does_not_change_much(cuda):
     outs = [ops.attn_decode(q, k, v, pos, NQ, NKV, D, scale=SCALE, max_split=ms).float() for ms in (1, 2, 7, 24, 64)]
     for o in outs[1:]:
         torch.testing.assert_close(o, outs[0], atol=4e-3, rtol=1e-2)
+
+
+@pytest.mark.parametrize('length', [100, 128, 129, 300, 1000, 3000])
+@pytest.mark.parametrize('max_split', [1, 3, 18])
+def test_ref_softmax_matches_oracle_block_walk(cuda, length, max_split):
+    """EGPT_FLAG_REF_SOFTMAX: probabilities rounded relative to the running maximum of the reference GPU
+    kernel's 128-key blocks (oracle attn_ref, block=REF_KEY_BLOCK). What remains is fp32 noise: sums in
+    another order, and exp() of CUDA vs numpy one fp32 ulp apart, which now and then moves a probability
+    across a bf16 rounding boundary (one bf16 ulp of p, i.e. at most 2^-8 max|V| / sum(p) on the output).
+    Outputs agree to one bf16 ulp plus a few such moves; nearly all of them exactly."""
+    L, ops = _ops()
+    q, k, v = _inputs(L, 3072, 7 + length, cuda)
+    pos = torch.tensor([length - 1], device=cuda)
+    out = from_torch(ops.attn_decode(q, k, v, pos, NQ, NKV, D, scale=SCALE, max_split=max_split,
+                                     ref_softmax=True)).reshape(NQ, D)
+    qn, kn, vn = from_torch(q).reshape(NQ, D), from_torch(k), from_torch(v)
+    want = round_bf16(attn_ref.decode_attention_fp32(qn, kn, vn, length, SCALE, p_bf16=True,
+                                                     block=attn_ref.REF_KEY_BLOCK))
+    grp = NQ // NKV
+    tol = np.empty((NQ, 1))
+    for h in range(NQ):
+        sc = (kn[h // grp, :length].astype(np.float64) @ qn[h]) * SCALE
+        den = np.exp(sc - sc.max()).sum()
+        tol[h] = 4 * 2.0 ** -8 * np.abs(vn[h // grp, :length]).max() / den
+    diff = np.abs(out - want)
+    assert (diff <= np.abs(want) * 2.0 ** -7 + tol).all(), (length, max_split)
+    assert (diff == 0).mean() > 0.98, (length, max_split, float((diff == 0).mean()))
 
 
 def test_never_reads_past_position(cuda):
