@@ -332,11 +332,12 @@ struct Stream {
 };
 
 __device__ __forceinline__ void top_up_prefetch(const Params &P, Stream &S) {
-  if (kAhead == 0) return;
-  while (S.lead < kAhead && !cur_end(P, S.pf)) {
-    prefetch_item(S.pf);
-    cur_next(P, S.pf);
-    ++S.lead;
+  if constexpr (kAhead > 0) {
+    while (S.lead < kAhead && !cur_end(P, S.pf)) {
+      prefetch_item(S.pf);
+      cur_next(P, S.pf);
+      ++S.lead;
+    }
   }
 }
 
