@@ -63,6 +63,8 @@ SIGNATURES = {
     'egpt_attn_ws_bytes': (SZ, [I64, I32, I32, I32, I32]),
     'egpt_attn_decode': (I32, [P, I64, P, I64, P, P, I64, P, I64, I32, I32, I32, P, P, F32, P, P, F32, I32, P, SZ, I32,
                                U32, P]),
+    'egpt_attn_decode_noalloc': (I32, [P, I64, P, I64, P, P, I64, P, I64, I32, I32, I32, P, P, F32, P, P, F32, I32,
+                                       I32, U32, P]),
     'egpt_argmax_rows': (I32, [P, P, I64, I64, I64, I32, P]),
     'egpt_decode_step': (I32, [ctypes.POINTER(Qwen3Plan), P]),
     'egpt_step_sync_ws_bytes': (SZ, []),

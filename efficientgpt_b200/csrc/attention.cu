@@ -23,6 +23,7 @@
 // before the range comes from rescoring the keys [0, k0) (EGPT_FLAG_REF_SOFTMAX) or, in the persistent decode
 // step, from the other ranges through global memory; without the flag a range starts its own walk.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "internal.h"
@@ -665,4 +666,63 @@ extern "C" int egpt_attn_decode(void *out, int64_t ldo, const void *q, int64_t l
   else
     e = bf ? launch_split_grp<1, true>(p, grid, (cudaStream_t)stream, pdl) : launch_split_grp<1, false>(p, grid, (cudaStream_t)stream, pdl);
   return check_launch(e, "attn_split_kernel");
+}
+
+// ---------------------------------------------------------------------------------------------- no-alloc variant
+// egpt_attn_decode for callers that may not allocate device memory: the split partials and counters live in
+// one file-scope device array of EGPT_ATTN_NOALLOC_SCRATCH_BYTES that every call on a device shares. In host
+// code the array's name only stands for the symbol; its device address comes from cudaGetSymbolAddress, once
+// per device, on the first call made with that device current.
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[EGPT_ATTN_NOALLOC_SCRATCH_BYTES];
+
+static void *noalloc_scratch(int *rc) {
+  static std::mutex mu;
+  static void *ptr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    *rc = set_error(EGPT_ERR_LAUNCH, "attn_decode_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    return nullptr;
+  }
+  if (dev < 0 || dev >= 64) {
+    *rc = set_error(EGPT_ERR_ARG, "attn_decode_noalloc: device ordinal %d out of range", dev);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptr[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      *rc = set_error(EGPT_ERR_LAUNCH, "attn_decode_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    ptr[dev] = p;
+  }
+  return ptr[dev];
+}
+
+extern "C" int egpt_attn_decode_noalloc(void *out, int64_t ldo, const void *q, int64_t ldq, void *k_cache,
+                                        void *v_cache, int64_t cap, const int64_t *position, int64_t m, int nq,
+                                        int nkv, int d, const void *q_norm_w, const void *k_norm_w, float eps,
+                                        const void *rope_cos, const void *rope_sin, float scale, int max_split,
+                                        int dtype, unsigned flags, void *stream) {
+  clear_error();
+  if (m < 1 || m > 65535 || nq < 1 || nkv < 1 || d < 1 || max_split < 1 || max_split > 1024)
+    return set_error(EGPT_ERR_SHAPE, "attn_decode_noalloc: bad m, heads, head_dim or max_split");
+  const size_t need = egpt_attn_ws_bytes(m, nq, nkv, d, max_split);
+  if (need > (size_t)EGPT_ATTN_NOALLOC_SCRATCH_BYTES)
+    return set_error(EGPT_ERR_WORKSPACE,
+                     "attn_decode_noalloc: m=%lld nq=%d nkv=%d d=%d max_split=%d needs %zu bytes of scratch, above the "
+                     "built-in %d; lower max_split or m, or call egpt_attn_decode with a workspace",
+                     (long long)m, nq, nkv, d, max_split, need, EGPT_ATTN_NOALLOC_SCRATCH_BYTES);
+  int rc = EGPT_OK;
+  void *scratch = noalloc_scratch(&rc);
+  if (!scratch) return rc;
+  // the arrival counters must start at zero (the kernels leave them at zero; an aborted call may not)
+  const size_t cnt_off = attn_ws_float_bytes(m, nq, d, max_split);
+  cudaError_t e = cudaMemsetAsync((char *)scratch + cnt_off, 0, need - cnt_off, (cudaStream_t)stream);
+  if (e != cudaSuccess) return set_error(EGPT_ERR_LAUNCH, "attn_decode_noalloc: cudaMemsetAsync: %s", cudaGetErrorString(e));
+  return egpt_attn_decode(out, ldo, q, ldq, k_cache, v_cache, cap, position, m, nq, nkv, d, q_norm_w, k_norm_w, eps,
+                          rope_cos, rope_sin, scale, max_split, scratch, (size_t)EGPT_ATTN_NOALLOC_SCRATCH_BYTES, dtype,
+                          flags, stream);
 }

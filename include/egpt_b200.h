@@ -136,6 +136,24 @@ EGPT_API int egpt_attn_decode(void *out, int64_t ldo, const void *q, int64_t ldq
                      const void *k_norm_w, float eps, const void *rope_cos, const void *rope_sin, float scale,
                      int max_split, void *ws, size_t ws_bytes, int dtype, unsigned flags, void *stream);
 
+/* egpt_attn_decode_noalloc: egpt_attn_decode without a caller workspace. No counterpart in the reference.
+ * For callers that must not allocate device memory themselves: code running inside another framework's
+ * operator whose device memory belongs to that framework's allocator, or a serving path that plans all of its
+ * memory up front and forbids allocations afterwards. The split partials and counters use one built-in device
+ * array of EGPT_ATTN_NOALLOC_SCRATCH_BYTES (512 KiB, held by every GPU that loads the library until exit);
+ * calls whose egpt_attn_ws_bytes(m, nq, nkv, d, max_split) exceeds it return EGPT_ERR_WORKSPACE and launch
+ * nothing. No cudaMalloc, cudaFree or other allocating call is made. The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress, with that device current); make that first call before any
+ * stream capture. Every call clears the array's arrival counters on `stream` (cudaMemsetAsync) before its
+ * kernel; the partials are overwritten by each call. All calls on a device share the array, so calls whose
+ * kernels can overlap on the GPU (different streams without ordering between them) race: order them. */
+#define EGPT_ATTN_NOALLOC_SCRATCH_BYTES 524288
+EGPT_API int egpt_attn_decode_noalloc(void *out, int64_t ldo, const void *q, int64_t ldq, void *k_cache,
+                                      void *v_cache, int64_t cap, const int64_t *position, int64_t m, int nq,
+                                      int nkv, int d, const void *q_norm_w, const void *k_norm_w, float eps,
+                                      const void *rope_cos, const void *rope_sin, float scale, int max_split,
+                                      int dtype, unsigned flags, void *stream);
+
 /* ---- argmax over rows of bf16/fp32 logits -----------------------------------------------------------
  * replaces: logits[:, -1].argmax(-1) (research/realmodel/fast_decode.py:48,84): first index on ties. */
 EGPT_API int egpt_argmax_rows(int64_t *out, const void *logits, int64_t rows, int64_t n, int64_t ld, int dtype, void *stream);
