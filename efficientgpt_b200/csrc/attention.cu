@@ -37,10 +37,14 @@ constexpr int kKeyTile = 32;       // keys per warp step
 
 // Keys per split range whose scores fit the scratch ([group][keys] fp32 = 8 KB).
 __host__ __device__ constexpr int split_keys_max(int grp) { return 2048 / grp; }
-// Blocks per split range: ranges are whole 128-key blocks, at most max_split of them.
+// Blocks per split range: ranges are whole 128-key blocks, at most max_split of them, and at least
+// kMinSplitBlocks blocks each: below that a range's keys cost less time than the exchange and combine that a
+// second range brings.
+constexpr int kMinSplitBlocks = 4;
 __host__ __device__ inline int split_blocks(int64_t L, int max_split) {
   const int64_t nb = (L + kRefBlock - 1) / kRefBlock;
-  return (int)((nb + max_split - 1) / max_split);
+  const int64_t b = (nb + max_split - 1) / max_split;
+  return (int)(b > kMinSplitBlocks ? b : kMinSplitBlocks);
 }
 __host__ __device__ inline int split_count(int64_t L, int bps) {
   const int64_t nb = (L + kRefBlock - 1) / kRefBlock;

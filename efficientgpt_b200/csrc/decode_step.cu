@@ -34,22 +34,15 @@ namespace ps {
 
 constexpr int kNC = 16;                // warps (all compute)
 constexpr int kCT = kNC * 32;          // threads
-constexpr int kChunk = 2048;           // columns per stream item: 4 x 16-byte segments per lane and row
+constexpr int kTileRows = 16;          // rows per tensor-core tile (mma m16n8k32)
+constexpr int kChunkCols = 256;        // columns per stream item: 16 rows x 256 int8 = 4 KB
+constexpr int kItemBytes = kTileRows * kChunkCols;
 #ifndef EGPT_PS_RING
 #define EGPT_PS_RING 2
 #endif
-#ifndef EGPT_PS_AHEAD
-#define EGPT_PS_AHEAD 0
-#endif
-#ifndef EGPT_PS_PF_LAST
-#define EGPT_PS_PF_LAST 1
-#endif
-#ifndef EGPT_PS_HOT_PF
-#define EGPT_PS_HOT_PF 0
-#endif
 constexpr int kRing = EGPT_PS_RING;    // stream items in flight per warp (shared-memory ring filled by cp.async)
-constexpr int kSlot = 2 * kChunk + 32; // ring slot: 2 rows x 2048 int8, then the rows' 16-byte scale blocks
-constexpr int kAhead = EGPT_PS_AHEAD;  // L2 prefetch distance beyond the ring, in stream items per warp
+constexpr int kSlot = kItemBytes + 64; // ring slot: the item, then its tile's 16 scales (up to 64 bytes)
+constexpr int kXPad = 64;              // bytes between the digit planes of the staged input (bank spread)
 
 enum Kind { QKV = 0, OPROJ = 1, GATEUP = 2, DOWN = 3, LMHEAD = 4 };
 
@@ -71,20 +64,36 @@ struct Params {
   unsigned *lm_cnt;
   unsigned long long *bar;
   unsigned *epoch;
+  int part_bytes;            // shared memory for the layer stages' per-item row sums
   unsigned long long *trace;  // nullable: per-barrier %globaltimer stamps of CTA 0
 };
 
+// A GEMV stage: n logical rows in tiles of 16 (GATEUP: tile t = gate rows 8t..8t+7 then up rows 8t..8t+7),
+// k columns in chunks of 256; tile t belongs to CTA t % G. Layer stages split a tile's chunks over the CTA's
+// warps (item i of the CTA's list -> warp i % 16) and reduce the exact partial sums through shared memory;
+// the lm_head gives whole tiles to warps (tile t -> warp (t / G) % 16), so its argmax epilogue stays in the warp.
 struct Stage {
   const int8_t *w;
   const void *s;
-  int64_t n, k;
-  int kind;
+  int64_t n, k, tiles;
+  int kind, nk;
 };
 
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"r"(kCT) : "memory"); }
 
-__device__ __forceinline__ Stage stage_desc(const Params &P, int s) {
-  Stage st;
+// Stage table in shared memory (built once per launch from the device layer array): a stage's weights and
+// scales are then found without a global load on the stream's critical path.
+struct StageT {
+  const int8_t *w;
+  const void *s;
+  int64_t n, k;
+  int kind, pad;
+};
+constexpr int kStabOffset = 256;  // after the 64-float reduction scratch
+
+__device__ __forceinline__ StageT stage_from_layers(const Params &P, int s) {
+  StageT st;
+  st.pad = 0;
   if (s == 4 * P.L) {
     st.w = P.w_lm, st.s = P.s_lm, st.n = P.V, st.k = P.H, st.kind = LMHEAD;
     return st;
@@ -99,36 +108,85 @@ __device__ __forceinline__ Stage stage_desc(const Params &P, int s) {
   return st;
 }
 
-__device__ __forceinline__ int64_t phys_row(const Stage &st, int64_t lr) {
-  if (st.kind != GATEUP) return lr;
-  return (lr & 1) ? (st.n >> 1) + (lr >> 1) : (lr >> 1);
+__device__ __forceinline__ StageT *stage_table() {
+  extern __shared__ __align__(128) uint8_t smem[];
+  return (StageT *)(smem + kStabOffset);
 }
 
+__device__ __forceinline__ Stage stage_desc(const Params &P, int s) {
+  const StageT &t = stage_table()[s];
+  Stage st;
+  st.w = t.w, st.s = t.s, st.n = t.n, st.k = t.k, st.kind = t.kind;
+  st.tiles = st.n / kTileRows;
+  st.nk = (int)((st.k + kChunkCols - 1) / kChunkCols);
+  return st;
+}
+
+// Tiles of a stage that belong to this CTA.
+__device__ __forceinline__ int64_t cta_tiles(const Stage &st) {
+  const int64_t b = blockIdx.x;
+  return b < st.tiles ? (st.tiles - b + gridDim.x - 1) / gridDim.x : 0;
+}
+
+// Physical weight row of row r (< 16) of tile t.
+__device__ __forceinline__ int64_t tile_row(const Stage &st, int64_t t, int r) {
+  if (st.kind != GATEUP) return t * kTileRows + r;
+  return r < 8 ? t * 8 + r : (st.n >> 1) + t * 8 + (r - 8);
+}
+// Byte offset of row r's scale in the slot's scale block (lm_head items carry their tile's scales).
+__device__ __forceinline__ int scale_pos(int r, int esz) { return r * esz; }
+
 // ------------------------------------------------------------------------------------------------ stream
-// A warp's flattened stream of (stage, pair, chunk) items.
+// A warp's flattened stream of (stage, tile, chunk) items across all stages of the step (32-bit arithmetic,
+// no divisions: this runs once per item on the stage's critical path).
 struct Cursor {
   Stage st;
   int s;          // stage index; 4L + 1 = end of the stream
-  int c, nk;      // chunk of the current pair, chunks per row
-  int64_t q;      // pair index within the stage
+  int c;          // chunk
+  int tile;       // tile index within the stage
+  int tl, ntl;    // layer stages: tile-local index in this CTA's list, tiles of this CTA
+  int item;       // layer stages: item index in the CTA's list (tl * nk + c)
 };
 
 __device__ __forceinline__ void cur_stage(const Params &P, Cursor &cu, int s) {
-  const int64_t step0 = (int64_t)blockIdx.x + (int64_t)gridDim.x * (threadIdx.x >> 5);
+  const int w = threadIdx.x >> 5;
   for (; s <= 4 * P.L; ++s) {
     const Stage st = stage_desc(P, s);
-    if (step0 < (st.n >> 1)) {
-      cu.st = st, cu.s = s, cu.c = 0, cu.nk = (int)((st.k + kChunk - 1) / kChunk), cu.q = step0;
-      return;
+    if (st.kind == LMHEAD) {
+      const int t0 = (int)blockIdx.x + (int)gridDim.x * w;
+      if (t0 < st.tiles) {
+        cu.st = st, cu.s = s, cu.c = 0, cu.tile = t0, cu.tl = cu.ntl = cu.item = 0;
+        return;
+      }
+    } else {
+      const int ntl = (int)cta_tiles(st);
+      if (w < ntl * st.nk) {
+        cu.st = st, cu.s = s, cu.item = w, cu.ntl = ntl;
+        cu.tl = 0, cu.c = w;
+        while (cu.c >= st.nk) cu.c -= st.nk, ++cu.tl;
+        cu.tile = (int)blockIdx.x + (int)gridDim.x * cu.tl;
+        return;
+      }
     }
   }
   cu.s = 4 * P.L + 1;
 }
 __device__ __forceinline__ void cur_next(const Params &P, Cursor &cu) {
-  if (++cu.c < cu.nk) return;
-  cu.c = 0;
-  cu.q += (int64_t)gridDim.x * kNC;
-  if (cu.q >= (cu.st.n >> 1)) cur_stage(P, cu, cu.s + 1);
+  if (cu.st.kind == LMHEAD) {
+    if (++cu.c < cu.st.nk) return;
+    cu.c = 0;
+    cu.tile += (int)gridDim.x * kNC;
+    if (cu.tile >= cu.st.tiles) cur_stage(P, cu, cu.s + 1);
+    return;
+  }
+  cu.item += kNC;
+  cu.c += kNC;
+  while (cu.c >= cu.st.nk) cu.c -= cu.st.nk, ++cu.tl;
+  if (cu.tl >= cu.ntl) {
+    cur_stage(P, cu, cu.s + 1);
+    return;
+  }
+  cu.tile = (int)blockIdx.x + (int)gridDim.x * cu.tl;
 }
 __device__ __forceinline__ bool cur_end(const Params &P, const Cursor &cu) { return cu.s > 4 * P.L; }
 
@@ -141,48 +199,25 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Byte offset of row pr's scale inside the 16-byte block that holds it.
-__device__ __forceinline__ int scale_off(const Params &P, const Stage &st, int64_t pr) {
-  return (int)(((uintptr_t)st.s + (uintptr_t)(pr << (P.scale_bf16 ? 1 : 2))) & 15);
-}
-
-// Issue the copies of one item into a ring slot: each lane copies segments j * 32 + lane of both rows
-// (8 x 16 B; the lane later reads back exactly the bytes it copied, so no cross-lane sync is needed) and
-// lanes 0 and 1 copy the 16-byte block holding their row's scale. The caller commits the group.
+// Copy one item into a ring slot: piece p (16 bytes) of tile row r lands at r * 256 + 16 * (p ^ 4 (r & 1)),
+// which spreads the MMA fragment reads of rows g and g + 8 over all banks; for the lm_head, lanes 0..3 also
+// copy the tile's scales. Pieces past the end of the row are not copied (their x digits are zero). The caller
+// commits.
 __device__ __forceinline__ void fill_item(const Params &P, const Cursor &cu, uint8_t *slot) {
   const int lane = threadIdx.x & 31;
-  const int64_t col0 = (int64_t)cu.c * kChunk;
-  const int cw = (int)min((int64_t)kChunk, cu.st.k - col0);
+  const Stage &st = cu.st;
+  const int64_t col0 = (int64_t)cu.c * kChunkCols;
+  const int cw = (int)min((int64_t)kChunkCols, st.k - col0);
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int8_t *row = cu.st.w + phys_row(cu.st, 2 * cu.q + r) * cu.st.k + col0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int sl = j * 32 + lane;
-      if (sl * 16 < cw) cp_async16(slot + r * kChunk + sl * 16, row + sl * 16);
-    }
+  for (int i = 0; i < kItemBytes / 16 / 32; ++i) {
+    const int id = i * 32 + lane, r = id >> 4, pc = id & 15;
+    if (pc * 16 < cw)
+      cp_async16(slot + r * kChunkCols + 16 * (pc ^ ((r & 1) << 2)),
+                 st.w + tile_row(st, cu.tile, r) * st.k + col0 + pc * 16);
   }
-  if (lane < 2) {
-    const int64_t pr = phys_row(cu.st, 2 * cu.q + lane);
-    const uintptr_t a = (uintptr_t)cu.st.s + (uintptr_t)(pr << (P.scale_bf16 ? 1 : 2));
-    cp_async16(slot + 2 * kChunk + lane * 16, (const void *)(a & ~(uintptr_t)15));
-  }
-}
-
-// L2 prefetch of one item: lanes 0-15 take row 0, 16-31 row 1, one 128-byte line each.
-__device__ __forceinline__ void prefetch_item(const Cursor &cu) {
-  const int lane = threadIdx.x & 31;
-  const int64_t col0 = (int64_t)cu.c * kChunk;
-  const int cw = (int)min((int64_t)kChunk, cu.st.k - col0);
-  const int off = (lane & 15) * 128;
-  if (off < cw) {
-    const int8_t *p = cu.st.w + phys_row(cu.st, 2 * cu.q + (lane >> 4)) * cu.st.k + col0 + off;
-#if EGPT_PS_PF_LAST
-    asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
-#else
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-#endif
-  }
+  const int esz = P.scale_bf16 ? 2 : 4;
+  if (st.kind == LMHEAD && lane * 16 < kTileRows * esz)
+    cp_async16(slot + kItemBytes + lane * 16, (const char *)st.s + cu.tile * kTileRows * esz + lane * 16);
 }
 
 // ------------------------------------------------------------------------------------------------ sync
@@ -231,28 +266,6 @@ __device__ __forceinline__ void stamp(const Params &P, int k) {
   if (P.trace && blockIdx.x == 0 && threadIdx.x == 0) P.trace[4 + 10 * P.L + k] = globaltimer_ns();
 }
 
-// Small data read on the step's critical path (norm weights), marked evict_last in L2 so that the weight stream
-// (normal priority) does not push it out between steps: one 128-byte line per thread, grid-strided.
-__device__ void hot_prefetch(const Params &P) {
-  const int64_t gt = (int64_t)blockIdx.x * kCT + threadIdx.x, gs = (int64_t)gridDim.x * kCT;
-  const int64_t lh = ((int64_t)P.H * 2 + 127) / 128, ld = ((int64_t)P.D * 2 + 127) / 128;
-  const int64_t per_layer = 2 * lh + 2 * ld;
-  for (int64_t i = gt; i < per_layer * P.L + lh; i += gs) {
-    const char *a;
-    if (i >= per_layer * P.L) {
-      a = (const char *)P.final_norm + (i - per_layer * P.L) * 128;
-    } else {
-      const egpt_qwen3_layer &Ly = P.layers[i / per_layer];
-      int64_t r = i % per_layer;
-      if (r < lh) a = (const char *)Ly.ln_in + r * 128;
-      else if ((r -= lh) < lh) a = (const char *)Ly.ln_post + r * 128;
-      else if ((r -= lh) < ld) a = (const char *)Ly.q_norm + r * 128;
-      else a = (const char *)Ly.k_norm + (r - ld) * 128;
-    }
-    asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(a));
-  }
-}
-
 // CTA-wide sum in a fixed order: per-warp butterfly, then every thread adds the warp partials in order.
 __device__ __forceinline__ float csum(float v, float *red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -267,55 +280,116 @@ __device__ __forceinline__ float csum(float v, float *red) {
 }
 
 constexpr int kMaxPerThread = 12;  // staged inputs up to 12 * 512 = 6144 elements
+constexpr int kGroups = kMaxPerThread / 4;  // a thread stages groups of 4 consecutive elements
 
 // RMSNorm weights of a stage input, loaded into registers BEFORE the grid barrier that precedes the stage
 // (they do not depend on the step), so their latency hides behind the barrier instead of adding to it.
+// Thread t holds elements 4 (t + 512 j) .. + 3, j < kGroups.
 struct NormW {
   float w[kMaxPerThread];
 };
 __device__ __forceinline__ void load_norm(const uint16_t *nw, int64_t k, NormW &n) {
 #pragma unroll
-  for (int e = 0; e < kMaxPerThread; ++e) {
-    const int64_t i = threadIdx.x + (int64_t)e * kCT;
-    n.w[e] = i < k ? bf16_bits_to_f32(nw[i]) : 0.f;
+  for (int j = 0; j < kGroups; ++j) {
+    const int64_t i = 4 * ((int64_t)threadIdx.x + (int64_t)j * kCT);
+    uint2 u = make_uint2(0u, 0u);
+    if (i < k) u = *(const uint2 *)(nw + i);
+    n.w[4 * j] = bf16_lo(u.x), n.w[4 * j + 1] = bf16_hi(u.x), n.w[4 * j + 2] = bf16_lo(u.y), n.w[4 * j + 3] = bf16_hi(u.y);
   }
 }
 
-// Stage an input vector of k bf16 values into xs (fp32, [4][k/16] float4 layout), optionally RMSNorm'd with
-// the preloaded weights nw (HF rounding points): one pass over global memory, one CTA reduction. copy_to
-// (nullable) receives the raw values (layer 0: h = embedding row).
-__device__ void stage_input(const uint16_t *src, int64_t k, const NormW *nw, float eps, float4 *xs, float *red,
-                            uint16_t *copy_to) {
-  const int t = threadIdx.x;
+// y * 2^e for any e the staged inputs produce (exact unless the result underflows).
+__device__ __forceinline__ float mul_pow2(float y, int e) {
+  if (e < -126) {
+    y *= __int_as_float((e + 100 + 127) << 23);
+    e = -100;
+  } else if (e > 127) {
+    y *= __int_as_float((127 + 127) << 23);
+    e -= 127;
+  }
+  return y * __int_as_float((e + 127) << 23);
+}
+
+// Padded stride of the digit planes for an input of k values.
+__host__ __device__ __forceinline__ int x_stride(int64_t k) {
+  return (int)((k + kChunkCols - 1) / kChunkCols * kChunkCols) + kXPad;
+}
+
+// Balanced base-256 digit d (0..3) of X, |X| < 2^30: X = sum_d digit_d 256^d with every digit in [-128, 127].
+__device__ __forceinline__ void digits4(int X, int (&d)[4]) {
+  d[0] = (int)(int8_t)(X & 0xFF);
+  X = (X - d[0]) >> 8;
+  d[1] = (int)(int8_t)(X & 0xFF);
+  X = (X - d[1]) >> 8;
+  d[2] = (int)(int8_t)(X & 0xFF);
+  d[3] = (X - d[2]) >> 8;
+}
+
+// Stage an input vector of k bf16 values (k a multiple of 4; optionally RMSNorm'd with the preloaded weights
+// nw, HF rounding points) as exact fixed point: x[i] = X[i] * 2^E with |X| < 2^30, E from a bound on the largest
+// |x[i]| (values far below it round to the fixed-point grid), and X split into four balanced base-256 digit
+// planes xd[d][i] in [-128, 127], zero-padded to whole 256-column chunks. One CTA reduction gives both the sum
+// of squares and the bound (max |x w| * rsqrt(...) * (1 + 2^-8)^2 covers the two bf16 roundings of the norm).
+// copy_to (nullable) receives the raw values (layer 0: h = embedding row). Returns E.
+__device__ int stage_input(const uint16_t *src, int64_t k, const NormW *nw, float eps, int8_t *xd, float *red,
+                           uint16_t *copy_to) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   float v[kMaxPerThread];
-  float ss = 0.f;
+  float ss = 0.f, mx = 0.f;
+#pragma unroll
+  for (int j = 0; j < kGroups; ++j) {
+    const int64_t i = 4 * ((int64_t)t + (int64_t)j * kCT);
+    uint2 u = make_uint2(0u, 0u);
+    if (i < k) {
+      u = __ldcg((const uint2 *)(src + i));
+      if (copy_to) *(uint2 *)(copy_to + i) = u;
+    }
+    v[4 * j] = bf16_lo(u.x), v[4 * j + 1] = bf16_hi(u.x), v[4 * j + 2] = bf16_lo(u.y), v[4 * j + 3] = bf16_hi(u.y);
+  }
 #pragma unroll
   for (int e = 0; e < kMaxPerThread; ++e) {
-    const int64_t i = t + (int64_t)e * kCT;
-    v[e] = 0.f;
-    if (i < k) {
-      const uint16_t raw = __ldcg(src + i);
-      if (copy_to) copy_to[i] = raw;
-      v[e] = bf16_bits_to_f32(raw);
-    }
     ss = fmaf(v[e], v[e], ss);
+    mx = fmaxf(mx, fabsf(nw ? v[e] * nw->w[e] : v[e]));
   }
+  ss = warp_sum(ss);
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = ss, red[kNC + warp] = mx;
+  csync();
+  float tot = 0.f, bound = red[kNC];
+#pragma unroll
+  for (int w = 0; w < kNC; ++w) tot += red[w];
+#pragma unroll
+  for (int w = 1; w < kNC; ++w) bound = fmaxf(bound, red[kNC + w]);
   if (nw) {
-    const float inv = rsqrtf(csum(ss, red) / (float)k + eps);
+    const float inv = rsqrtf(tot / (float)k + eps);
 #pragma unroll
     for (int e = 0; e < kMaxPerThread; ++e) v[e] = round_bf16(round_bf16(v[e] * inv) * nw->w[e]);
+    bound = bound * inv * 1.0079f;
   }
-  const int segs = (int)(k >> 4);
-  float *xsf = (float *)xs;
+  const int ex = bound > 0.f ? ((__float_as_int(bound) >> 23) & 0xFF) - 127 : 0;  // floor(log2 bound)
+  const int E = ex - 29;
+  const int xs = x_stride(k);
+  const int64_t kpad = xs - kXPad;
 #pragma unroll
-  for (int e = 0; e < kMaxPerThread; ++e) {
-    const int64_t i = t + (int64_t)e * kCT;
-    if (i < k) {
-      const int sg = (int)(i >> 4), el = (int)(i & 15);
-      xsf[((el >> 2) * segs + sg) * 4 + (el & 3)] = v[e];
+  for (int j = 0; j < kGroups; ++j) {
+    const int64_t i = 4 * ((int64_t)t + (int64_t)j * kCT);
+    if (i < kpad) {
+      uint32_t word[4] = {0u, 0u, 0u, 0u};
+      if (i < k) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          int d[4];
+          digits4(__float2int_rn(mul_pow2(v[4 * j + q], -E)), d);
+#pragma unroll
+          for (int p = 0; p < 4; ++p) word[p] |= ((uint32_t)d[p] & 0xFFu) << (8 * q);
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < 4; ++p) *(uint32_t *)(xd + (int64_t)p * xs + i) = word[p];
     }
   }
   csync();
+  return E;
 }
 
 // ------------------------------------------------------------------------------------------------ GEMV stage
@@ -325,23 +399,12 @@ struct Best {
 };
 
 struct Stream {
-  Cursor cur, fill, pf;  // consumption, ring-fill (kRing items ahead of cur) and L2-prefetch cursors
-  int lead;              // items pf is ahead of fill
-  int slot;              // ring slot holding cur's item
-  uint8_t *ring;         // this warp's kRing slots
+  Cursor cur, fill;  // consumption and ring-fill (kRing items ahead of cur) cursors
+  int slot;          // ring slot holding cur's item
+  uint8_t *ring;     // this warp's kRing slots
 };
 
-__device__ __forceinline__ void top_up_prefetch(const Params &P, Stream &S) {
-  if constexpr (kAhead > 0) {
-    while (S.lead < kAhead && !cur_end(P, S.pf)) {
-      prefetch_item(S.pf);
-      cur_next(P, S.pf);
-      ++S.lead;
-    }
-  }
-}
-
-// Start the stream: kRing items in flight (one commit group each, empty past the end), prefetch beyond.
+// Start the stream: kRing items in flight (one commit group each, empty past the end).
 __device__ __forceinline__ void stream_start(const Params &P, Stream &S, uint8_t *ring) {
   S.ring = ring;
   S.slot = 0;
@@ -355,88 +418,121 @@ __device__ __forceinline__ void stream_start(const Params &P, Stream &S, uint8_t
     }
     cp_async_commit();
   }
-  S.pf = S.fill;
-  S.lead = 0;
-  top_up_prefetch(P, S);
 }
 
-// Consume this warp's items of stage s (the stream's cursor is at stage s or later). Each consumed slot is
-// refilled at once with the item kRing ahead, whatever stage it belongs to: weights do not depend on the
-// activations, so the copies for the next stages run on while this warp waits at a barrier.
-__device__ void gemv_stage(const Params &P, int s, Stream &S, const float4 *xs, Best &best) {
-  const int lane = threadIdx.x & 31;
-  uint64_t acc0 = 0ull, acc1 = 0ull;
-  float s_e = 0.f, res_e = 0.f;
+__device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float load_scale(const Params &P, const void *s, int64_t row) {
+  return P.scale_bf16 ? bf16_bits_to_f32(((const uint16_t *)s)[row]) : ((const float *)s)[row];
+}
+
+// Consume this warp's items of stage s (the stream's cursor is at stage s or later). Per item and lane (g =
+// lane / 4, t = lane % 4): 16 bytes of tile rows g and g + 8 and (g < 4) 16 bytes of digit plane g for each of
+// four 64-column steps feed two int8 tensor-core MMAs; column d of the accumulator is row . plane d, exact in
+// int32, and lane t = 0 folds the planes into the exact int64 row sums. Every consumed slot is refilled at once
+// with the item kRing ahead, whatever stage it belongs to. Layer stages leave each item's sums in `part` and,
+// after a CTA barrier, threads e < (CTA tiles) x 16 (x 8 for gate/up pairs) add a row's items in order and
+// apply the epilogue; their scales and residuals are fetched before the items stream. The lm_head epilogue
+// (bf16 logits, argmax) runs in the warp that owns the tile.
+__device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, int E, long long *part, Best &best) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const Stage sd = stage_desc(P, s);
+  const bool lm = sd.kind == LMHEAD;
+  const int per_tile = sd.kind == GATEUP ? 8 : kTileRows;
+  const int e = threadIdx.x;
+  const bool epi = !lm && e < cta_tiles(sd) * per_tile;
+  const int64_t etile = blockIdx.x + (int64_t)gridDim.x * (e / per_tile);
+  const int er = e % per_tile;
+  float es0 = 0.f, es1 = 0.f, eres = 0.f;
+  if (epi) {
+    es0 = load_scale(P, sd.s, tile_row(sd, etile, er));
+    if (sd.kind == GATEUP) es1 = load_scale(P, sd.s, tile_row(sd, etile, er + 8));
+    if (sd.kind == OPROJ || sd.kind == DOWN) eres = bf16_bits_to_f32(__ldcg(P.h + etile * kTileRows + er));
+  }
+  const int xs = x_stride(sd.k);
+  int c4[4] = {0, 0, 0, 0};
   while (S.cur.s == s) {
-    const Stage st = S.cur.st;
-    const int64_t q = S.cur.q;
     const int c = S.cur.c;
-    const bool last = c == S.cur.nk - 1;
-    const bool resid = st.kind == OPROJ || st.kind == DOWN;
-    if (c == 0) {
-      acc0 = acc1 = 0ull;
-      if (resid && lane < 2) res_e = bf16_bits_to_f32(__ldcg(P.h + 2 * q + lane));
-    }
-    cp_async_wait<kRing - 1>();  // this lane's copies of cur's item have landed
+    const int64_t tile = S.cur.tile, item = S.cur.item;
+    const bool last = c == sd.nk - 1;
+    if (!lm || c == 0) c4[0] = c4[1] = c4[2] = c4[3] = 0;
+    cp_async_wait<kRing - 1>();  // this lane's copies of the item have landed
+    __syncwarp();                // ... and every other lane's
     const uint8_t *slot = S.ring + S.slot * kSlot;
-    if (last && lane < 2) {  // read the scale before the slot is refilled
-      const int64_t pr = phys_row(st, 2 * q + lane);
-      const uint8_t *blk = slot + 2 * kChunk + lane * 16 + scale_off(P, st, pr);
-      s_e = P.scale_bf16 ? bf16_bits_to_f32(*(const uint16_t *)blk) : *(const float *)blk;
-    }
-    const int64_t col0 = (int64_t)c * kChunk;
-    const int cw = (int)min((int64_t)kChunk, st.k - col0);
-    const int xsegs = (int)(st.k >> 4);
+    const int8_t *xb = xd + (int64_t)c * kChunkCols + g * xs + 16 * t;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int sl = j * 32 + lane;
-      if (sl * 16 < cw) {
-        const ulonglong2 *xb = (const ulonglong2 *)(xs + c * (kChunk / 16) + sl);
-        uint64_t x2[8];
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const ulonglong2 v = xb[(size_t)g * xsegs];
-          x2[2 * g] = v.x;
-          x2[2 * g + 1] = v.y;
-        }
-        acc0 = dot16x2(x2, *(const uint4 *)(slot + sl * 16), acc0);
-        acc1 = dot16x2(x2, *(const uint4 *)(slot + kChunk + sl * 16), acc1);
+      const int sw = 16 * ((4 * j + t) ^ ((g & 1) << 2));
+      const uint4 wa = *(const uint4 *)(slot + g * kChunkCols + sw);
+      const uint4 wb = *(const uint4 *)(slot + (g + 8) * kChunkCols + sw);
+      uint4 xv = make_uint4(0u, 0u, 0u, 0u);
+      if (g < 4) xv = *(const uint4 *)(xb + 64 * j);
+      mma_s8(c4, wa.x, wb.x, wa.y, wb.y, xv.x, xv.y);
+      mma_s8(c4, wa.z, wb.z, wa.w, wb.w, xv.z, xv.w);
+    }
+    float s0 = 0.f, s1 = 0.f;
+    if (lm && last && t == 0) {
+      const uint8_t *sb = slot + kItemBytes;
+      if (P.scale_bf16) {
+        s0 = bf16_bits_to_f32(*(const uint16_t *)(sb + scale_pos(g, 2)));
+        s1 = bf16_bits_to_f32(*(const uint16_t *)(sb + scale_pos(g + 8, 2)));
+      } else {
+        s0 = *(const float *)(sb + scale_pos(g, 4));
+        s1 = *(const float *)(sb + scale_pos(g + 8, 4));
       }
     }
-    // refill the slot (the FMAs above consumed its bytes) with the item kRing ahead; top up the L2 prefetch
+    __syncwarp();  // every lane's reads of the slot are done before any lane refills it
     if (!cur_end(P, S.fill)) {
       fill_item(P, S.fill, S.ring + S.slot * kSlot);
       cur_next(P, S.fill);
-      --S.lead;
     }
     cp_async_commit();
-    top_up_prefetch(P, S);
     S.slot = S.slot + 1 == kRing ? 0 : S.slot + 1;
     cur_next(P, S.cur);
-    if (!last) continue;
-    const float2 a0 = unpack2(acc0), a1 = unpack2(acc1);
-    const float t0 = warp_sum(a0.x + a0.y), t1 = warp_sum(a1.x + a1.y);
-    const float s_up = __shfl_down_sync(0xffffffffu, s_e, 1);
-    if (lane < 2) {
-      const float y = round_bf16((lane == 0 ? t0 : t1) * s_e);
-      const int64_t lr = 2 * q + lane;
-      switch (st.kind) {
-        case QKV: P.qkv[lr] = f32_to_bf16_bits(y); break;
-        case OPROJ:
-        case DOWN: P.h[lr] = f32_to_bf16_bits(round_bf16(res_e + y)); break;
-        case GATEUP:
-          if (lane == 0) {
-            const float up = round_bf16(t1 * s_up);
-            P.act[q] = f32_to_bf16_bits(round_bf16(round_bf16(y / (1.0f + expf(-y))) * up));
-          }
-          break;
-        default:
-          if (P.logits) P.logits[lr] = f32_to_bf16_bits(y);
-          if (argmax_better(y, (int)lr, best.v, best.i)) {
-            best.v = y;
-            best.i = (int)lr;
-          }
-      }
+    if (lm && !last) continue;
+    // digit planes 2t, 2t+1 of rows g, g + 8 sit in lane t: lane t = 0 gathers planes 2, 3 from lane t = 1
+    const int o0 = __shfl_down_sync(0xffffffffu, c4[0], 1), o1 = __shfl_down_sync(0xffffffffu, c4[1], 1);
+    const int o2 = __shfl_down_sync(0xffffffffu, c4[2], 1), o3 = __shfl_down_sync(0xffffffffu, c4[3], 1);
+    if (t != 0) continue;
+    const long long T0 = (long long)c4[0] + ((long long)c4[1] << 8) + ((long long)o0 << 16) + ((long long)o1 << 24);
+    const long long T1 = (long long)c4[2] + ((long long)c4[3] << 8) + ((long long)o2 << 16) + ((long long)o3 << 24);
+    if (!lm) {
+      part[item * kTileRows + g] = T0;
+      part[item * kTileRows + g + 8] = T1;
+      continue;
+    }
+    const int64_t r0 = tile * kTileRows + g, r1 = r0 + 8;
+    const float l0 = round_bf16(mul_pow2(__ll2float_rn(T0), E) * s0), l1 = round_bf16(mul_pow2(__ll2float_rn(T1), E) * s1);
+    if (P.logits) {
+      P.logits[r0] = f32_to_bf16_bits(l0);
+      P.logits[r1] = f32_to_bf16_bits(l1);
+    }
+    if (argmax_better(l0, (int)r0, best.v, best.i)) best.v = l0, best.i = (int)r0;
+    if (argmax_better(l1, (int)r1, best.v, best.i)) best.v = l1, best.i = (int)r1;
+  }
+  if (lm) return;
+  csync();  // all items' sums are in `part`
+  if (!epi) return;
+  const int64_t tl = e / per_tile;
+  long long T0 = 0, T1 = 0;
+  for (int c = 0; c < sd.nk; ++c) {
+    T0 += part[(tl * sd.nk + c) * kTileRows + er];
+    if (sd.kind == GATEUP) T1 += part[(tl * sd.nk + c) * kTileRows + er + 8];
+  }
+  const float y0 = mul_pow2(__ll2float_rn(T0), E);
+  switch (sd.kind) {
+    case QKV: P.qkv[etile * kTileRows + er] = f32_to_bf16_bits(y0 * es0); break;
+    case OPROJ:
+    case DOWN: P.h[etile * kTileRows + er] = f32_to_bf16_bits(eres + round_bf16(y0 * es0)); break;
+    default: {  // GATEUP: act = bf16(bf16(silu(gate)) * up)
+      const float gt = round_bf16(y0 * es0), up = round_bf16(mul_pow2(__ll2float_rn(T1), E) * es1);
+      P.act[etile * 8 + er] = f32_to_bf16_bits(round_bf16(gt / (1.0f + expf(-gt))) * up);
     }
   }
 }
@@ -601,9 +697,17 @@ template <int DPL, int GRP>
 __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
   extern __shared__ __align__(128) uint8_t smem[];
   float *red = (float *)smem;                    // 64 floats
-  uint8_t *ring = smem + 256;                    // kNC x kRing weight slots
-  float *u = (float *)(ring + kNC * kRing * kSlot);  // union: staged input (float4) / attention scratch
-  float4 *xs = (float4 *)u;
+  // stage table (4L + 1 entries) and a copy of the layer array, then the weight rings
+  const int stab_bytes = ((4 * P.L + 1) * (int)sizeof(StageT) + 127) / 128 * 128;
+  const int lay_bytes = (P.L * (int)sizeof(egpt_qwen3_layer) + 127) / 128 * 128;
+  egpt_qwen3_layer *layers = (egpt_qwen3_layer *)(smem + kStabOffset + stab_bytes);
+  for (int i = threadIdx.x; i <= 4 * P.L; i += kCT) stage_table()[i] = stage_from_layers(P, i);
+  for (int i = threadIdx.x; i < P.L; i += kCT) layers[i] = P.layers[i];
+  csync();
+  uint8_t *ring = smem + kStabOffset + stab_bytes + lay_bytes;  // kNC x kRing weight slots
+  long long *part = (long long *)(ring + kNC * kRing * kSlot);  // layer stages: per-item exact row sums
+  float *u = (float *)((uint8_t *)part + P.part_bytes);  // union: staged input digit planes / attention scratch
+  int8_t *xd = (int8_t *)u;
   __shared__ int s_flag;
   __shared__ float s_bv[kNC];
   __shared__ int s_bi[kNC];
@@ -612,9 +716,6 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
   // Start the weight stream immediately: it does not depend on the token, the position or the activations.
   Stream S;
   stream_start(P, S, ring + (size_t)warp * kRing * kSlot);
-#if EGPT_PS_HOT_PF
-  hot_prefetch(P);
-#endif
 
   const unsigned long long nb = 5ull * (unsigned long long)P.L;  // grid barriers per step
   const unsigned long long base = (unsigned long long)(*(volatile unsigned *)P.epoch) * nb;
@@ -639,43 +740,36 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
   // weights and RoPE row, the KV ranges) is requested before the barrier that precedes the stage.
   const bool attn_cta = (int)blockIdx.x < P.NKV * nsplit;
   NormW nw;
-  load_norm((const uint16_t *)P.layers[0].ln_in, P.H, nw);
-  for (int l = 0; l < P.L; ++l) {
-    const egpt_qwen3_layer &Ly = P.layers[l];
-    if (attn_cta) attn_prefetch_kv<DPL, GRP>(P, Ly, blockIdx.x, nsplit, bps, pos);
-    // ---- q|k|v = Wqkv . RMSNorm(h)  (layer 0: h = embed[token], CTA 0 stores it)
-    const uint16_t *hin = l == 0 ? P.embed + (ok ? tok : 0) * P.H : P.h;
-    stage_input(hin, P.H, &nw, P.eps, xs, red, (l == 0 && blockIdx.x == 0) ? P.h : nullptr);
-    stamp(P, 5 * l);
-    gemv_stage(P, 4 * l, S, xs, best);
-    AttnPre<DPL> pre;
-    if (attn_cta) attn_preload<DPL, GRP>(P, Ly, blockIdx.x, nsplit, bps, pos, pre);
-    ok = grid_barrier(P, base, ++bidx, &s_flag) && ok;
-    // ---- attention (q/k norm + RoPE + KV append + split-K softmax . V + combine)
-    if (ok && attn_cta) attention_task<DPL, GRP>(P, Ly, blockIdx.x, nsplit, bps, pos, u, pre, 5 * l + 1);
-    ok = grid_barrier(P, base, ++bidx, &s_flag) && ok;
-    // ---- h += Wo . attn
-    stage_input(P.attn, (int64_t)P.NQ * P.D, nullptr, 0.f, xs, red, nullptr);
-    stamp(P, 5 * l + 2);
-    gemv_stage(P, 4 * l + 1, S, xs, best);
-    load_norm((const uint16_t *)Ly.ln_post, P.H, nw);
-    ok = grid_barrier(P, base, ++bidx, &s_flag) && ok;
-    // ---- act = silu(Wg . RMSNorm(h)) * (Wu . RMSNorm(h))
-    stage_input(P.h, P.H, &nw, P.eps, xs, red, nullptr);
-    stamp(P, 5 * l + 3);
-    gemv_stage(P, 4 * l + 2, S, xs, best);
-    ok = grid_barrier(P, base, ++bidx, &s_flag) && ok;
-    // ---- h += Wdown . act
-    stage_input(P.act, P.I, nullptr, 0.f, xs, red, nullptr);
-    stamp(P, 5 * l + 4);
-    gemv_stage(P, 4 * l + 3, S, xs, best);
-    load_norm(l + 1 < P.L ? (const uint16_t *)P.layers[l + 1].ln_in : P.final_norm, P.H, nw);
-    ok = grid_barrier(P, base, ++bidx, &s_flag) && ok;
+  load_norm((const uint16_t *)layers[0].ln_in, P.H, nw);
+  AttnPre<DPL> pre;
+  // One pass per stage: 5 per layer (q|k|v, attention, o, gate|up, down), then the lm_head. Each stage body
+  // exists once in the code (the kernel's instruction footprint decides how fast a stage that runs once per
+  // layer executes).
+  for (int st = 0; st <= 5 * P.L; ++st) {
+    const int l = st / 5, ph = st == 5 * P.L ? 5 : st % 5;
+    const egpt_qwen3_layer &Ly = layers[l < P.L ? l : P.L - 1];
+    if (ph == 1) {
+      // ---- attention (q/k norm + RoPE + KV append + split-K softmax . V + combine)
+      if (ok && attn_cta) attention_task<DPL, GRP>(P, Ly, blockIdx.x, nsplit, bps, pos, u, pre, st);
+    } else {
+      // ---- GEMV stages: q|k|v = Wqkv . RMSNorm(h) (layer 0: h = embed[token], CTA 0 stores it);
+      //      h += Wo . attn;  act = silu(Wg . RMSNorm(h)) * (Wu . RMSNorm(h));  h += Wdown . act;
+      //      token = argmax(lm_head . RMSNorm(h))
+      if (ph == 0 && attn_cta) attn_prefetch_kv<DPL, GRP>(P, Ly, blockIdx.x, nsplit, bps, pos);
+      const uint16_t *src = ph == 2 ? P.attn : ph == 4 ? P.act : (ph == 0 && l == 0) ? P.embed + (ok ? tok : 0) * P.H : P.h;
+      const int64_t k = ph == 2 ? (int64_t)P.NQ * P.D : ph == 4 ? P.I : P.H;
+      const bool norm = ph == 0 || ph == 3 || ph == 5;
+      const int E = stage_input(src, k, norm ? &nw : nullptr, P.eps, xd, red,
+                                (st == 0 && blockIdx.x == 0) ? P.h : nullptr);
+      stamp(P, st);
+      gemv_stage(P, ph == 5 ? 4 * P.L : 4 * l + (ph == 0 ? 0 : ph - 1), S, xd, E, part, best);
+      // step-invariant inputs of the next stage, requested before the barrier
+      if (ph == 0 && attn_cta) attn_preload<DPL, GRP>(P, Ly, blockIdx.x, nsplit, bps, pos, pre);
+      if (ph == 2) load_norm((const uint16_t *)Ly.ln_post, P.H, nw);
+      if (ph == 4) load_norm(l + 1 < P.L ? (const uint16_t *)layers[l + 1].ln_in : P.final_norm, P.H, nw);
+    }
+    if (st < 5 * P.L) ok = grid_barrier(P, base, ++bidx, &s_flag) && ok;
   }
-  // ---- token = argmax(lm_head . RMSNorm(h)); the last CTA also advances position and the step epoch
-  stage_input(P.h, P.H, &nw, P.eps, xs, red, nullptr);
-  stamp(P, 5 * P.L);
-  gemv_stage(P, 4 * P.L, S, xs, best);
   if (P.trace && blockIdx.x == 0 && threadIdx.x == 0) P.trace[1 + 10 * P.L] = globaltimer_ns();
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -728,6 +822,17 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
   }
 }
 
+// Shared memory for the per-item row sums of the largest layer stage: (its tiles per CTA) x chunks x 16 x 8 B.
+static size_t part_bytes(const egpt_qwen3_plan *Pl, int G) {
+  const int64_t D = Pl->head_dim, H = Pl->hidden, I = Pl->intermediate;
+  const int64_t nk[4] = {(H + kChunkCols - 1) / kChunkCols, (Pl->n_q_heads * D + kChunkCols - 1) / kChunkCols,
+                         (H + kChunkCols - 1) / kChunkCols, (I + kChunkCols - 1) / kChunkCols};
+  const int64_t n[4] = {(Pl->n_q_heads + 2 * Pl->n_kv_heads) * D, H, 2 * I, H};
+  int64_t items = 0;
+  for (int i = 0; i < 4; ++i) items = std::max(items, (n[i] / kTileRows + G - 1) / G * nk[i]);
+  return (size_t)items * kTileRows * 8;
+}
+
 template <int DPL, int GRP>
 static cudaError_t launch(const Params &P, size_t smem, cudaStream_t st) {
   auto kern = decode_step_kernel<DPL, GRP>;
@@ -769,13 +874,14 @@ static int persistent_validate(const egpt_qwen3_plan *Pl, size_t *smem_out) {
   const int grp = NQ / NKV;
   const bool shape_ok = (D == 128 && (grp == 2 || grp == 4)) || (D == 32 && grp == 2);
   if (!shape_ok) return set_error(EGPT_ERR_SHAPE, "decode_step_persistent: head_dim %d / group %d not built", D, grp);
-  if (H % 16 || I % 16 || ((int64_t)NQ * D) % 16 || Pl->vocab % 2 ||
+  if (H % 16 || I % 16 || ((int64_t)NQ * D) % 16 || Pl->vocab % 16 ||
       std::max<int64_t>({H, I, (int64_t)NQ * D}) > (int64_t)ps::kMaxPerThread * ps::kCT)
-    return set_error(EGPT_ERR_SHAPE, "decode_step_persistent: sizes must be multiples of 16 (vocab even)");
+    return set_error(EGPT_ERR_SHAPE, "decode_step_persistent: hidden, intermediate, nq*d and vocab must be multiples "
+                     "of 16 and at most %d", ps::kMaxPerThread * ps::kCT);
   const int G = num_sms();
   if (G > kArgmaxMaxCtas) return set_error(EGPT_ERR_SHAPE, "decode_step_persistent: too many SMs");
-  // weights are copied in 16-byte pieces; a scale is read from the 16-byte block that holds it
-  const size_t sal = Pl->scale_dtype == EGPT_BF16 ? 2 : 4;
+  // weights and each tile's scales are copied in 16-byte pieces
+  const size_t sal = 16;
   bool aligned = (uintptr_t)Pl->w_lm % 16 == 0 && (uintptr_t)Pl->s_lm % sal == 0;
   for (int l = 0; l < Pl->n_layers; ++l) {
     const egpt_qwen3_layer &Ly = Pl->layers[l];
@@ -784,14 +890,17 @@ static int persistent_validate(const egpt_qwen3_plan *Pl, size_t *smem_out) {
               (uintptr_t)Ly.s_o % sal == 0 && (uintptr_t)Ly.s_gu % sal == 0 && (uintptr_t)Ly.s_down % sal == 0;
   }
   if (!aligned)
-    return set_error(EGPT_ERR_ALIGN, "decode_step_persistent: weights must be 16-byte aligned, scales element aligned");
+    return set_error(EGPT_ERR_ALIGN, "decode_step_persistent: weights and scales must be 16-byte aligned");
   if (Pl->attn_ws_bytes < egpt_attn_ws_bytes(1, NQ, NKV, D, Pl->attn_max_split) ||
       Pl->lm_ws_bytes < egpt_lm_head_ws_bytes(Pl->vocab))
     return set_error(EGPT_ERR_WORKSPACE, "decode_step_persistent: workspace too small");
-  // shared memory: reduction scratch + weight ring + union(staged input, attention scratch)
+  // shared memory: reduction scratch + weight ring + union(staged input digit planes, attention scratch)
   const int64_t kmax = std::max<int64_t>({H, I, (int64_t)NQ * D});
   const size_t attn_bytes = D == 32 ? sizeof(AttnScratch<1, 2>) : grp == 2 ? sizeof(AttnScratch<4, 2>) : sizeof(AttnScratch<4, 4>);
-  const size_t smem = 256 + (size_t)ps::kNC * ps::kRing * ps::kSlot + std::max<size_t>((size_t)kmax * 4, (attn_bytes + 15) / 16 * 16);
+  const size_t stab = ((size_t)(4 * Pl->n_layers + 1) * sizeof(ps::StageT) + 127) / 128 * 128 +
+                      ((size_t)Pl->n_layers * sizeof(egpt_qwen3_layer) + 127) / 128 * 128;
+  const size_t smem = ps::kStabOffset + stab + (size_t)ps::kNC * ps::kRing * ps::kSlot + ps::part_bytes(Pl, G) +
+                      std::max<size_t>(4 * (size_t)ps::x_stride(kmax), (attn_bytes + 15) / 16 * 16);
   const int max_split = std::max(1, std::min(Pl->attn_max_split, G / NKV));
   if ((int64_t)split_blocks(Pl->cap, max_split) * kRefBlock > split_keys_max(grp))
     return set_error(EGPT_ERR_SHAPE, "decode_step_persistent: cap %lld needs more than %d attention ranges per kv head",
@@ -840,6 +949,7 @@ extern "C" int egpt_decode_step_persistent(const egpt_qwen3_plan *Pl, void *stre
   P.lm_cnt = (unsigned *)((char *)Pl->lm_ws + kArgmaxMaxCtas * 8);
   P.bar = (unsigned long long *)Pl->sync_ws;
   P.epoch = (unsigned *)((char *)Pl->sync_ws + 8);
+  P.part_bytes = (int)ps::part_bytes(Pl, num_sms());
   P.trace = (unsigned long long *)Pl->trace;
   cudaError_t e;
   if (D == 128 && grp == 2)

@@ -30,6 +30,14 @@ def _quantize(model, scale_dtype, semantics):
     return model
 
 
+def _cfg05():
+    """The tiny config with N(0, 0.05) weights (fresh each time: quantize_model unties the lm_head in the config
+    it is given)."""
+    c = gi.tiny_config()
+    c.initializer_range = 0.05
+    return c
+
+
 def _tiny(scale_dtype=torch.float32, quantize=True, semantics='cuda'):
     model = gi.build_model(gi.tiny_config())
     cpu_hash = gi.state_hash(model)
@@ -102,27 +110,36 @@ def test_logits_match_reference_and_oracle(cuda, scale_dtype):
 
 @pytest.mark.parametrize('scale_dtype', [torch.float32, torch.bfloat16])
 def test_persistent_step_matches_launch_sequence(cuda, scale_dtype):
-    """egpt_decode_step_persistent (one cooperative kernel) vs egpt_decode_step (launch sequence): the same
-    GEMV arithmetic, the same attention ranges, tiles and merge order (the persistent kernel exchanges range
-    maxima where the launch sequence rescores earlier keys: the same values), so logits, tokens and caches are
-    bit-identical, also past 128 and 256 keys where attention splits over several ranges."""
+    """egpt_decode_step_persistent (one cooperative kernel) vs egpt_decode_step (launch sequence), teacher-forced
+    for 600 steps (past 512 keys, where attention splits over several ranges and the persistent kernel exchanges
+    range maxima). Attention, norms and RoPE are the same code; the GEMVs differ in summation: the persistent
+    kernel's int8 tensor-core dot products are exact (one rounding), the per-stage kernels sum in fp32. Logits
+    agree under the long-sequence rule and tokens differ only at near-ties of the launch sequence's logits."""
     from efficientgpt_b200 import _lib
     from efficientgpt_b200.engine import Qwen3Engine
-    model, _ = _tiny(scale_dtype)
-    a = Qwen3Engine(model, 320, keep_logits=True, persistent=False)
-    b = Qwen3Engine(model, 320, keep_logits=True, persistent=True)
+    model = gi.build_model(_cfg05(), seed=3).cuda()  # moderate gain: flips do not snowball over 600 steps
+    _quantize(model, scale_dtype, 'cuda')
+    a = Qwen3Engine(model, 640, keep_logits=True, persistent=False)
+    b = Qwen3Engine(model, 640, keep_logits=True, persistent=True)
     assert b.persistent and not a.persistent and a.attn_max_split == b.attn_max_split
     x = gi.tiny_prompts()[37].cuda()
     a.prefill(x)
     b.prefill(x)
-    for i in range(250):
+    same = 0
+    for i in range(600):
         b.token.copy_(a.token)  # teacher-force b onto a's tokens
         a.step()
         b.step()
         assert int(a.position) == int(b.position) == 38 + i
-        assert torch.equal(b.logits, a.logits), i
-        assert int(a.token) == int(b.token), i
-    assert torch.equal(b.kv[:, :, :, :288], a.kv[:, :, :, :288])
+        la, lb = from_torch(a.logits), from_torch(b.logits)
+        ok, detail = parity.logits_close(lb, la)
+        assert ok, (i, detail)
+        if int(a.token) != int(b.token):
+            top = np.sort(la)[-2:]
+            assert top[1] - top[0] <= parity.near_tie_threshold(top[1]), i
+        else:
+            same += 1
+    assert same >= 590
     assert _lib.device_error() == 0
 
 
@@ -134,16 +151,12 @@ def test_logits_past_one_softmax_block_match_oracle(cuda):
     is amplified well past that over a 120-token prompt."""
     from efficientgpt_b200.engine import Qwen3Engine
 
-    def cfg():  # fresh each time: quantize_model unties the lm_head in the config it is given
-        c = gi.tiny_config()
-        c.initializer_range = 0.05
-        return c
-    model = gi.build_model(cfg(), seed=3).cuda()
+    model = gi.build_model(_cfg05(), seed=3).cuda()
     _quantize(model, torch.bfloat16, 'cpu')
     eng = Qwen3Engine(model, 192, keep_logits=True)
     x = torch.randint(0, 512, (1, 120), generator=torch.Generator().manual_seed(11))
     eng.prefill(x.cuda())
-    ref = Qwen3Ref.from_hf(gi.build_model(cfg(), seed=3), 192, 'bf16', semantics='cpu')
+    ref = Qwen3Ref.from_hf(gi.build_model(_cfg05(), seed=3), 192, 'bf16', semantics='cpu')
     lg = ref.forward(x[0].tolist(), 0)
     ok, detail = parity.logits_close(from_torch(eng.logits), lg)
     assert ok, ('prefill', detail)
