@@ -52,6 +52,7 @@ def parse():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-pdl', action='store_true')
     ap.add_argument('--launch-sequence', action='store_true', help='per-stage kernels instead of the persistent step')
+    ap.add_argument('--no-gemv-chain', action='store_true', help='skip the GEMV-launches-alone comparison graph')
     ap.add_argument('--cpu-sample', type=int, default=3, help='timed CPU decode tokens (after one warm-up token)')
     a = ap.parse_args()
     if a.warmup < 3:
@@ -293,14 +294,16 @@ def main():
     step_gbs = bytes_tok / (ms / 1e3 / a.steps) / 1e9
 
     # the GEMV launches of the launch-sequence path alone
-    g, gemv_bytes, gemv_launches = gemv_chain_graph(eng)
-    reps = 64
-    time_replays(g, 4)
-    gms = time_replays(g, reps) / reps
-    gemv_gbs = gemv_bytes / (gms / 1e3) / 1e9
-    gemv = {'kernel': 'gemv_i8_kernel', 'achieved': round(gemv_gbs, 1), 'peak': hbm, 'unit': 'GB/s',
-            'frac': round(gemv_gbs / hbm, 4), 'launches_per_step': gemv_launches, 'bytes_per_step': gemv_bytes,
-            'avg_launch_us': round(gms * 1e3 / gemv_launches, 3)}
+    gemv, g = None, None
+    if not a.no_gemv_chain or not eng.persistent:
+        g, gemv_bytes, gemv_launches = gemv_chain_graph(eng)
+        reps = 64
+        time_replays(g, 4)
+        gms = time_replays(g, reps) / reps
+        gemv_gbs = gemv_bytes / (gms / 1e3) / 1e9
+        gemv = {'kernel': 'gemv_i8_kernel', 'achieved': round(gemv_gbs, 1), 'peak': hbm, 'unit': 'GB/s',
+                'frac': round(gemv_gbs / hbm, 4), 'launches_per_step': gemv_launches, 'bytes_per_step': gemv_bytes,
+                'avg_launch_us': round(gms * 1e3 / gemv_launches, 3)}
     if eng.persistent:  # one launch per token: the kernel's duration is the step's device time
         roofline = {'bound': 'hbm', 'kernel': 'decode_step_kernel', 'achieved': round(step_gbs, 1), 'peak': hbm,
                     'unit': 'GB/s', 'frac': round(step_gbs / hbm, 4), 'traffic': profile_traffic(),

@@ -14,9 +14,10 @@
 //
 // Layout: caches are [nkv][cap][d] per layer, so the keys of one head are one contiguous stream.
 // Work split: grid (nkv, max_split, rows). A CTA owns one kv head, all `group` q heads that read it (K/V
-// are read once per group) and one range of whole 128-key blocks. Each warp processes 32 keys per step:
-// lane l holds dims [l*d/32, (l+1)*d/32) of every key, so K/V rows are read fully coalesced; the 32 partial
-// dot products per head are reduced with a transpose-butterfly that leaves lane l holding key l's score.
+// are read once per group) and one range of whole 128-key blocks. Each warp processes 32 keys per step: for the
+// scores lane l reads key l's row in 16-byte pieces and dots it with the q heads in shared memory; for P.V each
+// half-warp reads whole value rows (lane l holds d/16 dims), the halves take even and odd keys, 8 independent
+// row loads per batch.
 // Pass A scores the range into shared memory (and prefetches the V rows into L2), the block maxima give the
 // running maximum of every block, pass B accumulates bf16(p) V per warp; warps merge in a fixed order and
 // split ranges combine by log-sum-exp in the last CTA of each kv head. The running maximum of the blocks
@@ -175,24 +176,6 @@ __device__ __forceinline__ void load_dims(const void *base, int64_t elem_off, fl
   }
 }
 
-// Transpose-butterfly: on entry lane l holds s[j] = partial for key j (j < 32) from its dims; on exit the
-// return value of lane l is the full sum over lanes for key l. 31 shuffles for 32 keys, fixed order.
-__device__ __forceinline__ float transpose_reduce32(float (&s)[32]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int w = 16; w >= 1; w >>= 1) {
-    const bool upper = (lane & w) != 0;
-#pragma unroll
-    for (int j = 0; j < w; ++j) {
-      // keep half of the keys: lanes with bit w set keep keys [w, 2w) of each 2w block, others [0, w)
-      const float send = upper ? s[j] : s[j + w];
-      const float keep = upper ? s[j + w] : s[j];
-      s[j] = keep + __shfl_xor_sync(0xffffffffu, send, w);
-    }
-  }
-  return s[0];
-}
-
 // ---------------------------------------------------------------------------------------------- core
 // Shared-memory scratch of one attention task (one kv head, its q heads, one key range).
 template <int DPL, int GRP>
@@ -220,35 +203,96 @@ struct AttnTask {
   float scale;
 };
 
-// Scores of keys t0 .. t0 + nkeys - 1 (nkeys <= 32) for every head of the group: lane l returns key t0 + l's.
+// HD consecutive elements of a cache row, kept raw (bf16: 4, 8 or 16 bytes; fp32: 8, 16 or 32 bytes) until
+// unpacked to fp32; a row that is not loaded unpacks to zeros.
+template <bool BF16, int HD>
+struct RawRow {
+  static constexpr int W = HD * (BF16 ? 2 : 4) / 4;  // 32-bit words
+  uint32_t w[W];
+  __device__ __forceinline__ void load(const void *base, int64_t elem_off, bool valid) {
+    const char *b = (const char *)base + elem_off * (BF16 ? 2 : 4);
+#pragma unroll
+    for (int i = 0; i < W; ++i) w[i] = 0u;
+    if (!valid) return;
+    if (W % 4 == 0) {
+#pragma unroll
+      for (int i = 0; i < W; i += 4) {
+        const uint4 u = *(const uint4 *)(b + 4 * i);
+        w[i] = u.x, w[(i + 1) % W] = u.y, w[(i + 2) % W] = u.z, w[(i + 3) % W] = u.w;
+      }
+    } else if (W % 2 == 0) {
+#pragma unroll
+      for (int i = 0; i < W; i += 2) {
+        const uint2 u = *(const uint2 *)(b + 4 * i);
+        w[i] = u.x, w[(i + 1) % W] = u.y;
+      }
+    } else {
+      w[0] = *(const uint32_t *)b;
+    }
+  }
+  __device__ __forceinline__ void unpack(float (&v)[HD]) const {
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
+      if (BF16) {
+        v[(2 * i) % HD] = bf16_lo(w[i]);
+        v[(2 * i + 1) % HD] = bf16_hi(w[i]);
+      } else {
+        v[i % HD] = __uint_as_float(w[i]);
+      }
+    }
+  }
+};
+
+// Scores of keys t0 .. t0 + nkeys - 1 (nkeys <= 32) for every head of the group: lane l reads key t0 + l's row
+// in 16-byte pieces (batches of 8 independent loads) and dots it with each q head from shared memory (broadcast
+// reads), four partial sums per head; lane l returns key t0 + l's scores (0 for lanes past nkeys).
 template <int DPL, int GRP, bool BF16>
-__device__ __forceinline__ void tile_scores(const void *K, int64_t t0, int nkeys, const float (&qv)[GRP][DPL],
+__device__ __forceinline__ void tile_scores(const void *K, int64_t t0, int nkeys, const AttnScratch<DPL, GRP> &S,
                                             float scale, float (&sc)[GRP]) {
   constexpr int D = DPL * 32;
+  constexpr int ESZ = BF16 ? 2 : 4;
+  constexpr int EPP = 16 / ESZ;          // elements per 16-byte piece
+  constexpr int NP = D * ESZ / 16;       // pieces per row
+  constexpr int NB = NP < 8 ? NP : 8;    // pieces per batch
   const int lane = threadIdx.x & 31;
+  float acc[GRP][4];
 #pragma unroll
-  for (int j = 0; j < GRP; ++j) {  // one head at a time keeps 32 partial sums live, not 32 x GRP
-    float part[32];
+  for (int j = 0; j < GRP; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  if (lane < nkeys) {
+    const uint4 *row = (const uint4 *)((const char *)K + (t0 + lane) * (int64_t)D * ESZ);
 #pragma unroll
-    for (int kk = 0; kk < 32; ++kk) {
-      float kv[4] = {0.f, 0.f, 0.f, 0.f};
-      if (kk < nkeys) load_dims<BF16>(K, (t0 + kk) * D + lane * DPL, kv, DPL);
-      float s = 0.f;
+    for (int pb = 0; pb < NP; pb += NB) {
+      uint4 w[NB];
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) s = fmaf(qv[j][e], kv[e], s);
-      part[kk] = s;
+      for (int u = 0; u < NB; ++u) w[u] = row[pb + u];
+#pragma unroll
+      for (int u = 0; u < NB; ++u) {
+        float kv[EPP];
+        if (BF16) {
+          const uint32_t x[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) kv[2 * h] = bf16_lo(x[h]), kv[2 * h + 1] = bf16_hi(x[h]);
+        } else {
+          kv[0] = __uint_as_float(w[u].x), kv[1] = __uint_as_float(w[u].y);
+          kv[2] = __uint_as_float(w[u].z), kv[3] = __uint_as_float(w[u].w);
+        }
+        const int d0 = (pb + u) * EPP;
+#pragma unroll
+        for (int j = 0; j < GRP; ++j) {
+#pragma unroll
+          for (int e = 0; e < EPP; e += 4) {
+            const float4 qq = *(const float4 *)&S.q[j][d0 + e];
+            acc[j][0] = fmaf(qq.x, kv[e], acc[j][0]);
+            acc[j][1] = fmaf(qq.y, kv[e + 1], acc[j][1]);
+            acc[j][2] = fmaf(qq.z, kv[e + 2], acc[j][2]);
+            acc[j][3] = fmaf(qq.w, kv[e + 3], acc[j][3]);
+          }
+        }
+      }
     }
-    sc[j] = transpose_reduce32(part) * scale;
   }
-}
-
-template <int DPL, int GRP>
-__device__ __forceinline__ void load_q(const AttnScratch<DPL, GRP> &S, float (&qv)[GRP][DPL]) {
-  const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int j = 0; j < GRP; ++j)
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) qv[j][e] = S.q[j][lane * DPL + e];
+  for (int j = 0; j < GRP; ++j) sc[j] = ((acc[j][0] + acc[j][1]) + (acc[j][2] + acc[j][3])) * scale;
 }
 
 // Pass A: scores of the range into S.sc, tile maxima into S.tmax, V rows of the range prefetched into L2.
@@ -258,8 +302,6 @@ __device__ void attn_pass_a(const AttnTask &t, AttnScratch<DPL, GRP> &S) {
   constexpr int D = DPL * 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (warp >= kAttnWarps) return;
-  float qv[GRP][DPL];
-  load_q(S, qv);
   const int ntiles = (int)((t.k1 - t.k0 + kKeyTile - 1) / kKeyTile);
   for (int ti = warp; ti < ntiles; ti += kAttnWarps) {
     const int64_t t0 = t.k0 + (int64_t)ti * kKeyTile;
@@ -270,7 +312,7 @@ __device__ void attn_pass_a(const AttnTask &t, AttnScratch<DPL, GRP> &S) {
       for (int off = 0; off < D * (BF16 ? 2 : 4); off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(vr + off));
     }
     float sc[GRP];
-    tile_scores<DPL, GRP, BF16>(t.K, t0, nkeys, qv, t.scale, sc);
+    tile_scores<DPL, GRP, BF16>(t.K, t0, nkeys, S, t.scale, sc);
 #pragma unroll
     for (int j = 0; j < GRP; ++j) {
       const float sj = lane < nkeys ? sc[j] : -INFINITY;
@@ -286,15 +328,13 @@ template <int DPL, int GRP, bool BF16, int NT>
 __device__ void attn_max_before(const AttnTask &t, AttnScratch<DPL, GRP> &S) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (warp < kAttnWarps) {
-    float qv[GRP][DPL];
-    load_q(S, qv);
     float run[GRP];
 #pragma unroll
     for (int j = 0; j < GRP; ++j) run[j] = -INFINITY;
     for (int64_t t0 = (int64_t)warp * kKeyTile; t0 < t.k0; t0 += kKeyTile * kAttnWarps) {
       const int nkeys = (int)min((int64_t)kKeyTile, t.k0 - t0);
       float sc[GRP];
-      tile_scores<DPL, GRP, BF16>(t.K, t0, nkeys, qv, t.scale, sc);
+      tile_scores<DPL, GRP, BF16>(t.K, t0, nkeys, S, t.scale, sc);
 #pragma unroll
       for (int j = 0; j < GRP; ++j) run[j] = fmaxf(run[j], warp_max(lane < nkeys ? sc[j] : -INFINITY));
     }
@@ -320,14 +360,15 @@ __device__ void attn_walk(const AttnTask &t, AttnScratch<DPL, GRP> &S, bool scor
   constexpr int D = DPL * 32;
   constexpr int KS = AttnScratch<DPL, GRP>::KS;
   constexpr int TPB = kRefBlock / kKeyTile;  // tiles per block
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float m_run[GRP], l_run[GRP], acc[GRP][DPL];
+  constexpr int HD = 2 * DPL;  // dims per lane: each half-warp covers a whole row, the halves take even / odd keys
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = lane >> 4;
+  float m_run[GRP], l_run[GRP], acc[GRP][HD];
 #pragma unroll
   for (int j = 0; j < GRP; ++j) {
     m_run[j] = -INFINITY;
     l_run[j] = 0.f;
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) acc[j][e] = 0.f;
+    for (int e = 0; e < HD; ++e) acc[j][e] = 0.f;
   }
   for (int64_t c0 = t.k0; c0 < t.k1; c0 += KS) {
     AttnTask c = t;
@@ -363,26 +404,41 @@ __device__ void attn_walk(const AttnTask &t, AttnScratch<DPL, GRP> &S, bool scor
           const float alpha = expf(m_run[j] - mref);
           l_run[j] *= alpha;
 #pragma unroll
-          for (int e = 0; e < DPL; ++e) acc[j][e] *= alpha;
+          for (int e = 0; e < HD; ++e) acc[j][e] *= alpha;
           m_run[j] = mref;
         }
         const float p = lane < nkeys ? expf(S.sc[j][ti * kKeyTile + lane] - mref) : 0.f;
         l_run[j] += warp_sum(p);
         pj[j] = p;
       }
-      for (int kk = 0; kk < nkeys; ++kk) {
-        float vv[4] = {0.f, 0.f, 0.f, 0.f};
-        load_dims<BF16>(t.V, (t0 + kk) * D + lane * DPL, vv, DPL);
+      // V rows: half-warp h takes keys kb + 2u + h, each lane 2 DPL dims of the row, 8 independent loads per
+      // batch (16 keys per round trip); keys past the tile's end load nothing and carry p = 0
+      for (int kb = 0; kb < nkeys; kb += 16) {
+        RawRow<BF16, HD> raw[8];  // loaded first, unpacked when used: 8 rows in flight at HD * 2 or 4 bytes each
 #pragma unroll
-        for (int j = 0; j < GRP; ++j) {
-          const float p32 = __shfl_sync(0xffffffffu, pj[j], kk);
-          const float pk = BF16 ? round_bf16(p32) : p32;
+        for (int u = 0; u < 8; ++u) {
+          const int key = kb + 2 * u + half;
+          raw[u].load(t.V, (t0 + (key < nkeys ? key : 0)) * D + (lane & 15) * HD, key < nkeys);
+        }
 #pragma unroll
-          for (int e = 0; e < DPL; ++e) acc[j][e] = fmaf(pk, vv[e], acc[j][e]);
+        for (int u = 0; u < 8; ++u) {
+          float vv[HD];
+          raw[u].unpack(vv);
+#pragma unroll
+          for (int j = 0; j < GRP; ++j) {
+            const float p32 = __shfl_sync(0xffffffffu, pj[j], (kb + 2 * u + half) & 31);
+            const float pk = BF16 ? round_bf16(p32) : p32;
+#pragma unroll
+            for (int e = 0; e < HD; ++e) acc[j][e] = fmaf(pk, vv[e], acc[j][e]);
+          }
         }
       }
     }
   }
+#pragma unroll
+  for (int j = 0; j < GRP; ++j)
+#pragma unroll
+    for (int e = 0; e < HD; ++e) acc[j][e] += __shfl_xor_sync(0xffffffffu, acc[j][e], 16);  // even + odd keys
   const int64_t ntot = (t.k1 - t.k0 + kKeyTile - 1) / kKeyTile;
   if (warp < min((int64_t)kAttnWarps, ntot)) {
 #pragma unroll
@@ -391,8 +447,9 @@ __device__ void attn_walk(const AttnTask &t, AttnScratch<DPL, GRP> &S, bool scor
         S.w_m[warp][j] = m_run[j];
         S.w_l[warp][j] = l_run[j];
       }
+      if (lane < 16)
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) S.w_acc[warp][j][lane * DPL + e] = acc[j][e];
+        for (int e = 0; e < HD; ++e) S.w_acc[warp][j][lane * HD + e] = acc[j][e];
     }
   }
 }
