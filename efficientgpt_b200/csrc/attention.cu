@@ -260,7 +260,7 @@ __device__ __forceinline__ void tile_scores(const void *K, int64_t t0, int nkeys
   for (int j = 0; j < GRP; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
   if (lane < nkeys) {
     const uint4 *row = (const uint4 *)((const char *)K + (t0 + lane) * (int64_t)D * ESZ);
-#pragma unroll
+#pragma unroll 1
     for (int pb = 0; pb < NP; pb += NB) {
       uint4 w[NB];
 #pragma unroll
@@ -350,13 +350,13 @@ __device__ void attn_max_before(const AttnTask &t, AttnScratch<DPL, GRP> &S) {
   }
 }
 
-// Walk the range in chunks of at most KS keys: pass A scores a chunk (unless `scored`: the caller already ran
-// pass A on a range of one chunk), the block maxima extend the running maximum (S.mb on entry: the running
+// Walk the range in chunks of at most KS keys: pass A scores each chunk (SCORED: the caller already ran pass A
+// on a range of one chunk), the block maxima extend the running maximum (S.mb on entry: the running
 // maximum before the range), then pass B accumulates per warp sum_k bf16(exp(s_k - m_block)) V_k and
 // sum_k exp(s_k - m_block), rescaled in fp32 whenever a block raises the maximum. Tile i of the range is
 // walked by warp i % 8 in increasing order whatever the chunking. Warp partials end in S.w_*.
-template <int DPL, int GRP, bool BF16, int NT>
-__device__ void attn_walk(const AttnTask &t, AttnScratch<DPL, GRP> &S, bool scored) {
+template <int DPL, int GRP, bool BF16, int NT, bool SCORED>
+__device__ void attn_walk(const AttnTask &t, AttnScratch<DPL, GRP> &S) {
   constexpr int D = DPL * 32;
   constexpr int KS = AttnScratch<DPL, GRP>::KS;
   constexpr int TPB = kRefBlock / kKeyTile;  // tiles per block
@@ -374,7 +374,7 @@ __device__ void attn_walk(const AttnTask &t, AttnScratch<DPL, GRP> &S, bool scor
     AttnTask c = t;
     c.k0 = c0;
     c.k1 = min(t.k1, c0 + (int64_t)KS);
-    if (!scored || c0 > t.k0) {
+    if (!SCORED) {
       nt_sync<NT>();  // the previous chunk's scores are consumed
       attn_pass_a<DPL, GRP, BF16>(c, S);
     }
@@ -588,7 +588,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
   } else if (threadIdx.x < GRP) {
     S.mb[threadIdx.x] = -INFINITY;
   }
-  attn_walk<DPL, GRP, BF16, kAttnThreads>(t, S, false);
+  attn_walk<DPL, GRP, BF16, kAttnThreads, false>(t, S);
   AttnOut o;
   o.out = (char *)p.out + row * p.ldo * esz;
   o.part = p.ws_f ? p.ws_f + row * p.nq * p.max_split * (D + 2) : nullptr;

@@ -40,7 +40,11 @@ constexpr int kItemBytes = kTileRows * kChunkCols;
 #ifndef EGPT_PS_RING
 #define EGPT_PS_RING 2
 #endif
+#ifndef EGPT_PS_AHEAD
+#define EGPT_PS_AHEAD 0
+#endif
 constexpr int kRing = EGPT_PS_RING;    // stream items in flight per warp (shared-memory ring filled by cp.async)
+constexpr int kAhead = EGPT_PS_AHEAD;  // items prefetched into L2 beyond the ring (0: none)
 constexpr int kSlot = kItemBytes + 64; // ring slot: the item, then its tile's 16 scales (up to 64 bytes)
 constexpr int kXPad = 64;              // bytes between the digit planes of the staged input (bank spread)
 
@@ -229,14 +233,19 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 
 // Grid barrier: arrivals accumulate on a monotonic counter; barrier idx (1-based) of the step with epoch
 // base completes when the counter reaches (base + idx) * G. Bounded: records EGPT_ERR_TIMEOUT, returns false.
-__device__ bool grid_barrier(const Params &P, unsigned long long base, unsigned long long idx, int *s_ok) {
-  const unsigned long long target = (base + idx) * gridDim.x;
+// Split in two so that work can go between arriving and waiting: grid_arrive publishes this CTA's writes and
+// counts it in (thread 0: fence, then one atomic add); grid_wait spins (thread 0) until every CTA arrived.
+__device__ __forceinline__ void grid_arrive(const Params &P, unsigned long long idx) {
   csync();
   if (threadIdx.x == 0) {
-    const bool tr = P.trace && blockIdx.x == 0;
-    if (tr) P.trace[2 * idx - 1] = globaltimer_ns();
+    if (P.trace && blockIdx.x == 0) P.trace[2 * idx - 1] = globaltimer_ns();
     __threadfence();
     atomicAdd(P.bar, 1ull);
+  }
+}
+__device__ bool grid_wait(const Params &P, unsigned long long base, unsigned long long idx, int *s_ok) {
+  const unsigned long long target = (base + idx) * gridDim.x;
+  if (threadIdx.x == 0) {
     int ok = 1;
     const uint64_t t0 = globaltimer_ns();
     for (int it = 0; ld_acquire_u64(P.bar) < target; ++it) {
@@ -253,7 +262,7 @@ __device__ bool grid_barrier(const Params &P, unsigned long long base, unsigned 
       }
     }
     __threadfence();
-    if (tr) P.trace[2 * idx] = globaltimer_ns();
+    if (P.trace && blockIdx.x == 0) P.trace[2 * idx] = globaltimer_ns();
     *s_ok = ok;
   }
   csync();
@@ -400,9 +409,21 @@ struct Best {
 
 struct Stream {
   Cursor cur, fill;  // consumption and ring-fill (kRing items ahead of cur) cursors
+  Cursor pf;         // L2 prefetch cursor (kAhead items ahead of fill)
   int slot;          // ring slot holding cur's item
   uint8_t *ring;     // this warp's kRing slots
 };
+
+// L2 prefetch of one item: lane l takes 128-byte line l of the 16 x 256-byte tile (pieces past the row end skipped).
+__device__ __forceinline__ void prefetch_item(const Cursor &cu) {
+  const int lane = threadIdx.x & 31, r = lane >> 1, half = lane & 1;
+  const Stage &st = cu.st;
+  const int64_t col0 = (int64_t)cu.c * kChunkCols + half * 128;
+  if (col0 < st.k) {
+    const int8_t *a = st.w + tile_row(st, cu.tile, r) * st.k + col0;
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+  }
+}
 
 // Start the stream: kRing items in flight (one commit group each, empty past the end).
 __device__ __forceinline__ void stream_start(const Params &P, Stream &S, uint8_t *ring) {
@@ -418,6 +439,11 @@ __device__ __forceinline__ void stream_start(const Params &P, Stream &S, uint8_t
     }
     cp_async_commit();
   }
+  S.pf = S.fill;
+  for (int i = 0; i < kAhead && !cur_end(P, S.pf); ++i) {
+    prefetch_item(S.pf);
+    cur_next(P, S.pf);
+  }
 }
 
 __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -432,6 +458,25 @@ __device__ __forceinline__ float load_scale(const Params &P, const void *s, int6
   return P.scale_bf16 ? bf16_bits_to_f32(((const uint16_t *)s)[row]) : ((const float *)s)[row];
 }
 
+// Epilogue inputs of a layer stage for thread e (< this CTA's tiles x 16, or x 8 for gate/up pairs): its rows'
+// scales and (o, down) the residual row, requested when the stage starts and consumed after its items.
+struct EpiIn {
+  float s0, s1, res;
+};
+__device__ __forceinline__ void load_epi(const Params &P, int gs, EpiIn &in) {
+  const Stage sd = stage_desc(P, gs);
+  in.s0 = in.s1 = in.res = 0.f;
+  if (sd.kind == LMHEAD) return;
+  const int per_tile = sd.kind == GATEUP ? 8 : kTileRows;
+  const int e = threadIdx.x;
+  if (e >= cta_tiles(sd) * per_tile) return;
+  const int64_t tile = blockIdx.x + (int64_t)gridDim.x * (e / per_tile);
+  const int r = e % per_tile;
+  in.s0 = load_scale(P, sd.s, tile_row(sd, tile, r));
+  if (sd.kind == GATEUP) in.s1 = load_scale(P, sd.s, tile_row(sd, tile, r + 8));
+  if (sd.kind == OPROJ || sd.kind == DOWN) in.res = bf16_bits_to_f32(__ldcg(P.h + tile * kTileRows + r));
+}
+
 // Consume this warp's items of stage s (the stream's cursor is at stage s or later). Per item and lane (g =
 // lane / 4, t = lane % 4): 16 bytes of tile rows g and g + 8 and (g < 4) 16 bytes of digit plane g for each of
 // four 64-column steps feed two int8 tensor-core MMAs; column d of the accumulator is row . plane d, exact in
@@ -440,7 +485,8 @@ __device__ __forceinline__ float load_scale(const Params &P, const void *s, int6
 // after a CTA barrier, threads e < (CTA tiles) x 16 (x 8 for gate/up pairs) add a row's items in order and
 // apply the epilogue; their scales and residuals are fetched before the items stream. The lm_head epilogue
 // (bf16 logits, argmax) runs in the warp that owns the tile.
-__device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, int E, long long *part, Best &best) {
+__device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, int E, long long *part,
+                           const EpiIn &ein, Best &best) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const Stage sd = stage_desc(P, s);
   const bool lm = sd.kind == LMHEAD;
@@ -449,12 +495,7 @@ __device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, 
   const bool epi = !lm && e < cta_tiles(sd) * per_tile;
   const int64_t etile = blockIdx.x + (int64_t)gridDim.x * (e / per_tile);
   const int er = e % per_tile;
-  float es0 = 0.f, es1 = 0.f, eres = 0.f;
-  if (epi) {
-    es0 = load_scale(P, sd.s, tile_row(sd, etile, er));
-    if (sd.kind == GATEUP) es1 = load_scale(P, sd.s, tile_row(sd, etile, er + 8));
-    if (sd.kind == OPROJ || sd.kind == DOWN) eres = bf16_bits_to_f32(__ldcg(P.h + etile * kTileRows + er));
-  }
+  const float es0 = ein.s0, es1 = ein.s1, eres = ein.res;
   const int xs = x_stride(sd.k);
   int c4[4] = {0, 0, 0, 0};
   while (S.cur.s == s) {
@@ -493,6 +534,10 @@ __device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, 
       cur_next(P, S.fill);
     }
     cp_async_commit();
+    if (kAhead > 0 && !cur_end(P, S.pf)) {
+      prefetch_item(S.pf);
+      cur_next(P, S.pf);
+    }
     S.slot = S.slot + 1 == kRing ? 0 : S.slot + 1;
     cur_next(P, S.cur);
     if (lm && !last) continue;
@@ -679,7 +724,7 @@ __device__ void attention_task(const Params &P, const egpt_qwen3_layer &Ly, int 
   } else if (threadIdx.x < GRP) {
     S.mb[threadIdx.x] = -INFINITY;
   }
-  attn_walk<DPL, GRP, true, kCT>(t, S, true);
+  attn_walk<DPL, GRP, true, kCT, true>(t, S);
   AttnOut o;
   o.out = P.attn;
   o.part = P.attn_ws;
@@ -740,35 +785,45 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
   // weights and RoPE row, the KV ranges) is requested before the barrier that precedes the stage.
   const bool attn_cta = (int)blockIdx.x < P.NKV * nsplit;
   NormW nw;
-  load_norm((const uint16_t *)layers[0].ln_in, P.H, nw);
   AttnPre<DPL> pre;
-  // One pass per stage: 5 per layer (q|k|v, attention, o, gate|up, down), then the lm_head. Each stage body
-  // exists once in the code (the kernel's instruction footprint decides how fast a stage that runs once per
-  // layer executes).
-  for (int st = 0; st <= 5 * P.L; ++st) {
-    const int l = st / 5, ph = st == 5 * P.L ? 5 : st % 5;
-    const egpt_qwen3_layer &Ly = layers[l < P.L ? l : P.L - 1];
-    if (ph == 1) {
-      // ---- attention (q/k norm + RoPE + KV append + split-K softmax . V + combine)
-      if (ok && attn_cta) attention_task<DPL, GRP>(P, Ly, blockIdx.x, nsplit, bps, pos, u, pre, st);
-    } else {
-      // ---- GEMV stages: q|k|v = Wqkv . RMSNorm(h) (layer 0: h = embed[token], CTA 0 stores it);
-      //      h += Wo . attn;  act = silu(Wg . RMSNorm(h)) * (Wu . RMSNorm(h));  h += Wdown . act;
-      //      token = argmax(lm_head . RMSNorm(h))
-      if (ph == 0 && attn_cta) attn_prefetch_kv<DPL, GRP>(P, Ly, blockIdx.x, nsplit, bps, pos);
-      const uint16_t *src = ph == 2 ? P.attn : ph == 4 ? P.act : (ph == 0 && l == 0) ? P.embed + (ok ? tok : 0) * P.H : P.h;
-      const int64_t k = ph == 2 ? (int64_t)P.NQ * P.D : ph == 4 ? P.I : P.H;
-      const bool norm = ph == 0 || ph == 3 || ph == 5;
-      const int E = stage_input(src, k, norm ? &nw : nullptr, P.eps, xd, red,
-                                (st == 0 && blockIdx.x == 0) ? P.h : nullptr);
-      stamp(P, st);
-      gemv_stage(P, ph == 5 ? 4 * P.L : 4 * l + (ph == 0 ? 0 : ph - 1), S, xd, E, part, best);
-      // step-invariant inputs of the next stage, requested before the barrier
-      if (ph == 0 && attn_cta) attn_preload<DPL, GRP>(P, Ly, blockIdx.x, nsplit, bps, pos, pre);
-      if (ph == 2) load_norm((const uint16_t *)Ly.ln_post, P.H, nw);
-      if (ph == 4) load_norm(l + 1 < P.L ? (const uint16_t *)layers[l + 1].ln_in : P.final_norm, P.H, nw);
+  EpiIn ein;
+  // One pass per stage: 5 per layer (q|k|v, attention, o, gate|up, down), then the lm_head. Every stage body and
+  // every request helper has ONE site in the code: the kernel's executed instruction footprint decides how fast a
+  // stage that runs once per layer executes. Pass st = -1 only issues the requests of stage 0.
+  for (int st = -1; st <= 5 * P.L; ++st) {
+    if (st >= 0) {
+      const int l = st / 5, ph = st == 5 * P.L ? 5 : st % 5;
+      const egpt_qwen3_layer &Ly = layers[l < P.L ? l : P.L - 1];
+      if (ph == 1) {
+        // ---- attention (q/k norm + RoPE + KV append + split-K softmax . V + combine)
+        if (ok && attn_cta) attention_task<DPL, GRP>(P, Ly, blockIdx.x, nsplit, bps, pos, u, pre, st);
+      } else {
+        // ---- GEMV stages: q|k|v = Wqkv . RMSNorm(h) (layer 0: h = embed[token], CTA 0 stores it);
+        //      h += Wo . attn;  act = silu(Wg . RMSNorm(h)) * (Wu . RMSNorm(h));  h += Wdown . act;
+        //      token = argmax(lm_head . RMSNorm(h))
+        const uint16_t *src = ph == 2 ? P.attn : ph == 4 ? P.act : (ph == 0 && l == 0) ? P.embed + (ok ? tok : 0) * P.H : P.h;
+        const int64_t k = ph == 2 ? (int64_t)P.NQ * P.D : ph == 4 ? P.I : P.H;
+        const bool norm = ph == 0 || ph == 3 || ph == 5;
+        const int E = stage_input(src, k, norm ? &nw : nullptr, P.eps, xd, red,
+                                  (st == 0 && blockIdx.x == 0) ? P.h : nullptr);
+        stamp(P, st);
+        load_epi(P, ph == 5 ? 4 * P.L : 4 * l + (ph == 0 ? 0 : ph - 1), ein);  // consumed after the items
+        gemv_stage(P, ph == 5 ? 4 * P.L : 4 * l + (ph == 0 ? 0 : ph - 1), S, xd, E, part, ein, best);
+      }
     }
-    if (st < 5 * P.L) ok = grid_barrier(P, base, ++bidx, &s_flag) && ok;
+    if (st < 5 * P.L) {
+      // step-invariant inputs of stage st + 1, requested between arriving at the barrier that precedes it and
+      // waiting there (after the arrival's fence, which would otherwise wait for them): norm weights, the
+      // attention prologue's weights and RoPE row, KV ranges
+      if (st >= 0) grid_arrive(P, bidx + 1);
+      const int n = st + 1, ln = n / 5, pn = n == 5 * P.L ? 5 : n % 5;
+      const egpt_qwen3_layer &Ln = layers[ln < P.L ? ln : P.L - 1];
+      if (pn == 0 || pn == 3 || pn == 5)
+        load_norm(pn == 5 ? P.final_norm : (const uint16_t *)(pn == 0 ? Ln.ln_in : Ln.ln_post), P.H, nw);
+      if (pn == 1 && attn_cta) attn_preload<DPL, GRP>(P, Ln, blockIdx.x, nsplit, bps, pos, pre);
+      if (pn == 0 && attn_cta) attn_prefetch_kv<DPL, GRP>(P, Ln, blockIdx.x, nsplit, bps, pos);
+      if (st >= 0) ok = grid_wait(P, base, ++bidx, &s_flag) && ok;
+    }
   }
   if (P.trace && blockIdx.x == 0 && threadIdx.x == 0) P.trace[1 + 10 * P.L] = globaltimer_ns();
 #pragma unroll
