@@ -18,6 +18,7 @@ EGPT_F32, EGPT_BF16 = 0, 1
 EPI_NONE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_GELU = 0, 1, 2, 3
 FLAG_DOUBLE_ROUND, FLAG_RMSNORM, FLAG_PDL, FLAG_EMBED, FLAG_ADVANCE, FLAG_APPEND, FLAG_NO_TMA = 1, 2, 4, 8, 16, 32, 64
 FLAG_REF_SOFTMAX = 128
+FLAG_X_F32 = 256
 
 _VALUE_ERRORS = {EGPT_ERR_SHAPE, EGPT_ERR_DTYPE, EGPT_ERR_ALIGN, EGPT_ERR_ARG, EGPT_ERR_WORKSPACE}
 
@@ -58,7 +59,7 @@ SIGNATURES = {
     'egpt_lm_head_argmax': (I32, [P, P, P, P, P, P, I32, I64, I64, P, F32, P, SZ, U32, P]),
     'egpt_rmsnorm': (I32, [P, P, P, I64, I64, F32, P]),
     'egpt_layernorm_f32': (I32, [P, P, P, P, I64, I64, F32, P]),
-    'egpt_embed': (I32, [P, P, I64, P, P, I64, I64, I64, I32, P]),
+    'egpt_embed': (I32, [P, P, I64, P, P, I64, P, I64, I64, I32, P]),
     'egpt_qk_norm_rope_kv_append': (I32, [P, P, I64, P, P, I64, P, I64, I32, I32, I32, P, P, F32, P, P, I32, P]),
     'egpt_attn_ws_bytes': (SZ, [I64, I32, I32, I32, I32]),
     'egpt_attn_decode': (I32, [P, I64, P, I64, P, P, I64, P, I64, I32, I32, I32, P, P, F32, P, P, F32, I32, P, SZ, I32,

@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(kRowThreads) layernorm_f32_kernel(float *out, 
 }
 
 __global__ void embed_kernel(void *out, const int64_t *ids, const void *table, const void *pos_table, int64_t pos0,
-                             int64_t vocab, int64_t dim, int bf16) {
+                             const int64_t *position, int64_t vocab, int64_t dim, int bf16) {
   pdl_wait();
   pdl_launch_dependents();
   const int64_t row = blockIdx.x;
@@ -106,7 +106,7 @@ __global__ void embed_kernel(void *out, const int64_t *ids, const void *table, c
       ((uint16_t *)out)[row * dim + i] = ((const uint16_t *)table)[id * dim + i];
     } else {
       float v = ((const float *)table)[id * dim + i];
-      if (pos_table) v += ((const float *)pos_table)[(pos0 + row) * dim + i];
+      if (pos_table) v += ((const float *)pos_table)[((position ? *position : 0) + pos0 + row) * dim + i];
       ((float *)out)[row * dim + i] = v;
     }
   }
@@ -191,14 +191,14 @@ extern "C" int egpt_layernorm_f32(float *out, const float *x, const float *w, co
 }
 
 extern "C" int egpt_embed(void *out, const int64_t *ids, int64_t rows, const void *table, const void *pos_table,
-                          int64_t pos0, int64_t vocab, int64_t dim, int dtype, void *stream) {
+                          int64_t pos0, const int64_t *position, int64_t vocab, int64_t dim, int dtype, void *stream) {
   clear_error();
   if (!out || !ids || !table) return set_error(EGPT_ERR_ARG, "embed: null pointer");
   if (rows < 1 || dim < 1 || vocab < 1 || rows > 0x7fffffff) return set_error(EGPT_ERR_SHAPE, "embed: bad shape");
   if (dtype != EGPT_BF16 && dtype != EGPT_F32) return set_error(EGPT_ERR_DTYPE, "embed: dtype");
   if (pos_table && dtype != EGPT_F32) return set_error(EGPT_ERR_DTYPE, "embed: positional table is fp32 only");
   return check_launch(launch_kernel((const void *)embed_kernel, dim3((unsigned)rows), dim3(256), 0, (cudaStream_t)stream,
-                                    false, out, ids, table, pos_table, pos0, vocab, dim, (int)(dtype == EGPT_BF16)),
+                                    false, out, ids, table, pos_table, pos0, position, vocab, dim, (int)(dtype == EGPT_BF16)),
                       "embed_kernel");
 }
 

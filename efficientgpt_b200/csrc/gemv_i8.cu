@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(kGemvThreads, MT == 1 ? 3 : 2) gemv_i8_kernel(
       const int64_t lr = row0 + r_e;
       if (p.argmax) {
         const float y = apply_scale(p, mine, s_e, bias_e);
-        if (p.logits) ((uint16_t *)p.logits)[lr] = f32_to_bf16_bits(y);
+        if (p.logits) store_act(p.logits, lr, y, bf);
         if (argmax_better(y, (int)lr, best_v, best_i)) {
           best_v = y;
           best_i = (int)lr;
@@ -593,7 +593,7 @@ extern "C" int egpt_lm_head_argmax(int64_t *token, int64_t *position, void *logi
   p.w = w;
   p.scale = scale;
   p.scale_bf16 = scale_dtype == EGPT_BF16;
-  p.x_bf16 = 1;
+  p.x_bf16 = (flags & EGPT_FLAG_X_F32) ? 0 : 1;
   p.n = n;
   p.k = k;
   p.norm_w = norm_w;

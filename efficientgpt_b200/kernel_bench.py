@@ -1,0 +1,159 @@
+"""Per-kernel sweeps of BASELINE configs 3 (int8 GEMV) and 4 (GQA decode attention) against the HBM roofline, and
+the config-1 nanoGPT decode rate.
+
+    python -m efficientgpt_b200.kernel_bench [--reps 50] [--skip-nanogpt]
+
+Each case replays a CUDA graph of `reps` launches (device time from CUDA events around the replays, so host launch
+cost is not counted) over enough weight / cache copies that one pass of the graph exceeds L2 (126 MB): every
+launch reads from HBM. Algorithmic bytes: GEMV N*K + 2N (bf16 scales) + 2K (x) + 2N (out); attention
+4096*L + 8192 (K and V of 8 kv heads x d 128 in bf16, q and out). Peak: MEASURED_PEAKS.json hbm_gbs when present.
+nanoGPT (config 1: 6 layers, 384 dims, vocab 50304, block 256, int8 weights with fp32 scales, fp32 activations,
+N(0, 0.02) init, 64-token prompt, 64 greedy tokens): graph replays of the native decode step timed with CUDA events
+(its 30 MB of weights fit in L2, so the step is launch- and latency-bound, not HBM-bound), next to the oracle's
+numpy restatement of the reference CPU path for 3 tokens on this host. Prints one JSON line per case.
+"""
+import argparse
+import json
+import math
+from pathlib import Path
+
+import torch
+
+L2_BYTES = 126 * 2 ** 20
+
+
+def peak_gbs():
+    p = Path(__file__).resolve().parent.parent / 'MEASURED_PEAKS.json'
+    if p.exists():
+        return float(json.loads(p.read_text())['hbm_gbs']), 'measured'
+    return 6650.0, 'fallback'
+
+
+def time_graph(fn, reps):
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(3):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(reps):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        g.replay()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / (5 * reps) * 1e3  # us per launch
+
+
+def gemv_cases(reps, peak, src):
+    from . import ops
+    for n, k, what in ((4096, 2048, 'qkv'), (2048, 2048, 'o'), (12288, 2048, 'gate_up'), (2048, 6144, 'down'),
+                       (151936, 2048, 'lm_head')):
+        g = torch.Generator(device='cuda').manual_seed(0)
+        copies = max(1, math.ceil(2 * L2_BYTES / (n * k)))
+        ws = [torch.randint(-127, 128, (n, k), dtype=torch.int8, device='cuda', generator=g) for _ in range(copies)]
+        s = (torch.rand(n, device='cuda', generator=g) * 0.019 + 0.001).to(torch.bfloat16)
+        x = torch.randn(1, k, device='cuda', generator=g).to(torch.bfloat16)
+        out = torch.empty(1, n, dtype=torch.bfloat16, device='cuda')
+        us = time_graph(lambda i: ops.gemv_i8(x, ws[i % copies], s, out=out), reps)
+        nbytes = n * k + 2 * n + 2 * k + 2 * n
+        gbs = nbytes / (us * 1e-6) / 1e9
+        yield {'kernel': 'gemv_i8_kernel', 'case': f'config 3 {what} N={n} K={k}', 'us': round(us, 3),
+               'bytes': nbytes, 'achieved_gbs': round(gbs, 1), 'peak_gbs': peak, 'frac': round(gbs / peak, 4),
+               'peak_source': src, 'l2': f'{copies} weight copies rotated'}
+        del ws
+
+
+def attention_cases(reps, peak, src):
+    from . import ops
+    nq, nkv, d = 16, 8, 128
+    for length in (512, 2048, 8192, 32768):
+        g = torch.Generator(device='cuda').manual_seed(length)
+        per = 2 * nkv * length * d * 2
+        copies = max(1, math.ceil(2 * L2_BYTES / per))
+        ks = [torch.randn(nkv, length, d, device='cuda', generator=g).to(torch.bfloat16) for _ in range(copies)]
+        vs = [torch.randn(nkv, length, d, device='cuda', generator=g).to(torch.bfloat16) for _ in range(copies)]
+        q = torch.randn(1, nq * d, device='cuda', generator=g).to(torch.bfloat16)
+        pos = torch.tensor([length - 1], device='cuda')
+        max_split = 64
+        ws = ops.attn_ws(1, nq, nkv, d, max_split, 'cuda')
+        out = torch.empty(1, nq * d, dtype=torch.bfloat16, device='cuda')
+        for ref in (False, True):
+            us = time_graph(lambda i: ops.attn_decode(q, ks[i % copies], vs[i % copies], pos, nq, nkv, d, scale=d ** -0.5,
+                                                      max_split=max_split, ws=ws, out=out, ref_softmax=ref), reps)
+            nbytes = 4096 * length + 8192
+            gbs = nbytes / (us * 1e-6) / 1e9
+            yield {'kernel': 'attn_split_kernel', 'case': f'config 4 L={length}' + (' ref_softmax' if ref else ''),
+                   'us': round(us, 3), 'bytes': nbytes, 'achieved_gbs': round(gbs, 1), 'peak_gbs': peak,
+                   'frac': round(gbs / peak, 4), 'peak_source': src, 'l2': f'{copies} cache copies rotated'}
+        del ks, vs
+
+
+def nanogpt_case():
+    import os
+    import sys
+    import time
+    from .int8_linear import quantize_model
+    from .nanogpt import GPT, GPTConfig, GraphDecoder
+    cfg = GPTConfig(block_size=256, vocab_size=50304, n_layer=6, n_head=6, n_embd=384, bias=True)
+    model = GPT(cfg, seed=0).cuda().eval()
+    params = {n: p.detach().cpu().numpy().copy() for n, p in model.named_parameters()}
+    quantize_model(model)
+    prompt = torch.randint(0, cfg.vocab_size, (1, 64), generator=torch.Generator().manual_seed(0)).cuda()
+    dec = GraphDecoder(model, prompt)
+    eng = dec.engine
+    eng.reset(prompt)
+    for _ in range(3):
+        dec.graph.replay()
+    eng.reset(prompt)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(63):
+        dec.graph.replay()
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / 63
+    line = {'kernel': 'nanoGPT decode step (one CUDA graph: 48 library kernels + history write)',
+            'case': 'config 1 (6x384, vocab 50304), context 65..127', 'tok_s': round(1e3 / ms, 1),
+            'ms_per_token': round(ms, 4), 'bound': 'latency (weights 30 MB, L2-resident)'}
+    root = Path(__file__).resolve().parent.parent
+    if (root / 'oracle').exists():
+        sys.path.insert(0, str(root))
+        from oracle.nanogpt_ref import NanoGPTRef
+        params['lm_head.weight'] = params['transformer.wte.weight']
+        ref = NanoGPTRef(params, {'block_size': 256, 'n_layer': 6, 'n_head': 6, 'n_embd': 384}, semantics='cuda')
+        lg = ref.forward(prompt[0].tolist(), 0)
+        t0 = time.perf_counter()
+        pos = 64
+        for _ in range(3):
+            lg = ref.forward([int(lg.argmax())], pos)
+            pos += 1
+        line['cpu_baseline'] = {'tok_s': round(3 / (time.perf_counter() - t0), 2), 'kind': 'port', 'cores': os.cpu_count(),
+                                'sample': '3 decode tokens at context 65..67, numpy restatement of the reference CPU path'}
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--reps', type=int, default=50)
+    ap.add_argument('--skip-nanogpt', action='store_true')
+    a = ap.parse_args()
+    peak, src = peak_gbs()
+    for line in gemv_cases(a.reps, peak, src):
+        print(json.dumps(line), flush=True)
+    for line in attention_cases(a.reps, peak, src):
+        print(json.dumps(line), flush=True)
+    if not a.skip_nanogpt:
+        print(json.dumps(nanogpt_case()), flush=True)
+
+
+if __name__ == '__main__':
+    main()

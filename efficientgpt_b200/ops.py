@@ -104,15 +104,18 @@ def lm_head_ws(n, device):
 
 def lm_head_argmax(x, w, s, ws, *, norm_w=None, eps=1e-6, logits=None, token=None, position=None, advance=False,
                    pdl=False):
-    """token = argmax(bf16(s * (RMSNorm(x) @ q.T))) on the device; x bf16 [K] (one row)."""
+    """token = argmax(bf16(s * (RMSNorm(x) @ q.T))) on the device; x bf16 [K] (one row). fp32 x (nanoGPT): the
+    logits are fp32 s * (x @ q.T) without rounding, written fp32 to `logits`."""
     _cuda(x, w, s, ws, norm_w, logits, token, position)
     n, k = w.shape
-    if x.numel() != k or x.dtype != torch.bfloat16:
-        raise ValueError('lm_head_argmax: x must be one bf16 row of K elements')
+    if x.numel() != k or x.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError('lm_head_argmax: x must be one bf16 or fp32 row of K elements')
+    if logits is not None and logits.dtype != x.dtype:
+        raise ValueError('lm_head_argmax: logits must have the dtype of x')
     if token is None:
         token = torch.empty(1, dtype=torch.int64, device=x.device)
     flags = (L.FLAG_RMSNORM if norm_w is not None else 0) | (L.FLAG_ADVANCE if advance else 0) \
-        | (L.FLAG_PDL if pdl else 0)
+        | (L.FLAG_PDL if pdl else 0) | (L.FLAG_X_F32 if x.dtype == torch.float32 else 0)
     L.check(L.load().egpt_lm_head_argmax(_p(token), _p(position), _p(logits), _p(x), _p(w), _p(s), _dt(s), n, k,
                                          _p(norm_w), float(eps), _p(ws), ws.numel(), flags, _stream()),
             'lm_head_argmax')
@@ -138,14 +141,15 @@ def layernorm_f32(x, w, b, eps=1e-5, out=None):
     return out.reshape(x.shape)
 
 
-def embed(ids, table, pos_table=None, pos0=0, out=None):
-    _cuda(ids, table, pos_table, out)
+def embed(ids, table, pos_table=None, pos0=0, out=None, position=None):
+    """out[i] = table[ids[i]] (+ pos_table[pos0 + i], + *position when the device position is given)."""
+    _cuda(ids, table, pos_table, out, position)
     ids = ids.reshape(-1).contiguous()
     if ids.dtype != torch.int64:
         raise ValueError('embed: ids must be int64')
     out = torch.empty((ids.numel(), table.shape[1]), dtype=table.dtype, device=table.device) if out is None else out
-    L.check(L.load().egpt_embed(_p(out), _p(ids), ids.numel(), _p(table), _p(pos_table), int(pos0), table.shape[0],
-                                table.shape[1], _dt(table), _stream()), 'embed')
+    L.check(L.load().egpt_embed(_p(out), _p(ids), ids.numel(), _p(table), _p(pos_table), int(pos0), _p(position),
+                                table.shape[0], table.shape[1], _dt(table), _stream()), 'embed')
     return out
 
 

@@ -55,6 +55,7 @@ extern "C" {
 #define EGPT_FLAG_APPEND 32u      /* attention: q/k-RMSNorm + RoPE + KV append of this step's row in-kernel */
 #define EGPT_FLAG_NO_TMA 64u      /* GEMV: force the plain-load kernel (any K)                            */
 #define EGPT_FLAG_REF_SOFTMAX 128u /* attention: bf16 probabilities rounded as the reference GPU kernel does */
+#define EGPT_FLAG_X_F32 256u      /* lm_head argmax: x and logits are fp32 (nanoGPT), no bf16 rounding      */
 
 /* ---- library ---------------------------------------------------------------------------------------- */
 EGPT_API const char *egpt_version(void);
@@ -88,7 +89,7 @@ EGPT_API int egpt_gemv_i8(void *out, const void *x, int x_dtype, int64_t m, int6
  * replaces: transformers Qwen3ForCausalLM lm_head (modeling_qwen3.py:503-505) on the int8 op, followed by
  *           research/realmodel/fast_decode.py:48 (argmax(-1), first index on ties) and :49 (position += 1)
  * token[0] = argmax_n bf16(s[n] * sum_k xn[k] q[n, k]) where xn = RMSNorm(x)*norm_w if EGPT_FLAG_RMSNORM.
- * logits (bf16 [n], nullable) receives the rounded logits. ws must hold egpt_lm_head_ws_bytes(n) bytes,
+ * logits ([n], nullable; bf16, or fp32 with EGPT_FLAG_X_F32) receives the logits. ws must hold egpt_lm_head_ws_bytes(n) bytes,
  * zero-filled once before first use (the kernel leaves its counter at zero). */
 EGPT_API size_t egpt_lm_head_ws_bytes(int64_t n);
 EGPT_API int egpt_lm_head_argmax(int64_t *token, int64_t *position, void *logits, const void *x, const int8_t *w,
@@ -102,10 +103,12 @@ EGPT_API int egpt_rmsnorm(void *out, const void *x, const void *w, int64_t rows,
 /* nanoGPT LayerNorm (model.py:18-27), fp32: y = (x - mean) / sqrt(var + eps) * w + b (b nullable). */
 EGPT_API int egpt_layernorm_f32(float *out, const float *x, const float *w, const float *b, int64_t rows, int64_t dim,
                        float eps, void *stream);
-/* Embedding rows: out[i] = table[ids[i]] (+ pos_table[pos0 + i] when pos_table is non-null, fp32 only).
+/* Embedding rows: out[i] = table[ids[i]] (+ pos_table[p0 + i] when pos_table is non-null, fp32 only, with
+ * p0 = pos0 + *position when position (device int64) is non-null, else pos0).
+ * replaces: tr.wte(ids) + tr.wpe(pos) (model.py:176-180; research/phase4/decoder.py:20,130).
  * dtype bf16 or fp32; ids int64 on the device. */
 EGPT_API int egpt_embed(void *out, const int64_t *ids, int64_t rows, const void *table, const void *pos_table,
-               int64_t pos0, int64_t vocab, int64_t dim, int dtype, void *stream);
+               int64_t pos0, const int64_t *position, int64_t vocab, int64_t dim, int dtype, void *stream);
 
 /* ---- attention --------------------------------------------------------------------------------------
  * replaces: transformers Qwen3Attention.forward core (modeling_qwen3.py:258-291: q/k RMSNorm, RoPE,

@@ -141,3 +141,19 @@ def test_near_tie_rule():
     assert parity.near_tie_match([1, 2, 3], [1.0, 0.0625, 1.0], [5.0] * 3, [1, 7, 9])[0]  # 2 ulps at 5.0
     assert not parity.near_tie_match([1, 2, 3], [1.0, 0.5, 1.0], [5.0] * 3, [1, 7, 9])[0]
     assert not parity.near_tie_match([1, 2], [1.0, 0.0], [5.0] * 2, [1])[0]
+
+
+def test_nanogpt_oracle_matches_reference_golden():
+    """oracle/nanogpt_ref.py against the reference's own nanoGPT int8 decode (tests/golden/make_golden_nanogpt.py):
+    every greedy token equal and the first-step fp32 logits within 1e-6."""
+    import json
+    from conftest import ROOT
+    from oracle.nanogpt_ref import NanoGPTRef
+    z = np.load(ROOT / 'tests' / 'golden' / 'nanogpt_tiny.npz')
+    meta = json.loads((ROOT / 'tests' / 'golden' / 'nanogpt.json').read_text())
+    params = {k[len('param.'):]: z[k] for k in z.files if k.startswith('param.')}
+    for run in meta['runs']:
+        toks, _ = NanoGPTRef(params, meta['config']).generate(run['prompt'], len(run['tokens']))
+        assert toks == run['tokens']
+        lg = NanoGPTRef(params, meta['config']).forward(run['prompt'], 0)
+        np.testing.assert_allclose(lg, z[f"logits_first_{len(run['prompt'])}"], atol=1e-6, rtol=0)
