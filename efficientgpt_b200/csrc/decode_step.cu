@@ -208,16 +208,19 @@ __device__ __forceinline__ void cp_async_wait() {
 // copy the tile's scales. Pieces past the end of the row are not copied (their x digits are zero). The caller
 // commits.
 __device__ __forceinline__ void fill_item(const Params &P, const Cursor &cu, uint8_t *slot) {
-  const int lane = threadIdx.x & 31;
+  // piece id = 32 i + lane: row r = 2 i + (lane >> 4), piece pc = lane & 15 for every i, so a lane walks its rows
+  // with one add per piece (rows 0-7 and 8-15 of a gate|up tile are two separate blocks)
+  const int lane = threadIdx.x & 31, hi = lane >> 4, pc = lane & 15;
   const Stage &st = cu.st;
   const int64_t col0 = (int64_t)cu.c * kChunkCols;
-  const int cw = (int)min((int64_t)kChunkCols, st.k - col0);
+  if (pc * 16 < st.k - col0) {
+    const int8_t *g0 = st.w + tile_row(st, cu.tile, hi) * st.k + col0 + pc * 16;
+    const int8_t *g1 = st.w + tile_row(st, cu.tile, 8 + hi) * st.k + col0 + pc * 16;
+    uint8_t *d = slot + hi * kChunkCols + 16 * (pc ^ (hi << 2));
 #pragma unroll
-  for (int i = 0; i < kItemBytes / 16 / 32; ++i) {
-    const int id = i * 32 + lane, r = id >> 4, pc = id & 15;
-    if (pc * 16 < cw)
-      cp_async16(slot + r * kChunkCols + 16 * (pc ^ ((r & 1) << 2)),
-                 st.w + tile_row(st, cu.tile, r) * st.k + col0 + pc * 16);
+    for (int i = 0; i < 4; ++i) cp_async16(d + i * 2 * kChunkCols, g0 + (int64_t)i * 2 * st.k);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) cp_async16(d + (8 + i * 2) * kChunkCols, g1 + (int64_t)i * 2 * st.k);
   }
   const int esz = P.scale_bf16 ? 2 : 4;
   if (st.kind == LMHEAD && lane * 16 < kTileRows * esz)
