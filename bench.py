@@ -21,7 +21,10 @@ Printed JSON line (rank 0):
                replayed alone as one PDL-chained graph (gemv_i8_kernel).
   gemv_chain   the GEMV launches of the launch-sequence path replayed alone (for comparison)
   cpu_baseline the reference's CPU path (oracle/torch_ref.py) on this host's cores, bounded sample
-With N > 1 every rank runs an independent replica (no collective on the data path; scaling "weak").
+With N > 1 (torchrun, one rank per GPU) the same model is split tensor-parallel over the N GPUs (efficientgpt_b200.tp:
+one persistent kernel per GPU and token, o_proj / down_proj partial sums exchanged over NVLink inside it; scaling
+"strong"); --replicas runs N independent one-GPU replicas instead (scaling "weak"). --workload qwen3_8b runs
+BASELINE config 5 (Qwen3-8B shape, 4096-token prompt fed through the step, 256 greedy tokens) at any N.
 """
 import argparse
 import json
@@ -54,6 +57,8 @@ def parse():
     ap.add_argument('--launch-sequence', action='store_true', help='per-stage kernels instead of the persistent step')
     ap.add_argument('--no-gemv-chain', action='store_true', help='skip the GEMV-launches-alone comparison graph')
     ap.add_argument('--cpu-sample', type=int, default=3, help='timed CPU decode tokens (after one warm-up token)')
+    ap.add_argument('--workload', choices=['qwen3_1.7b', 'qwen3_8b'], default='qwen3_1.7b')
+    ap.add_argument('--replicas', action='store_true', help='N > 1: independent replicas instead of tensor parallelism')
     a = ap.parse_args()
     if a.warmup < 3:
         ap.error('--warmup must be >= 3')
@@ -256,11 +261,128 @@ def run_reference(a, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_tp(a, world, rank, local):
+    """Tensor-parallel decode over the `world` GPUs (world 1: the same engine on one GPU): K timed replays of a
+    graph holding one step, device time max over ranks; every rank builds the same seeded model and keeps its
+    shard."""
+    from efficientgpt_b200 import tp
+    from efficientgpt_b200.configs import qwen3_1p7b_config, qwen3_8b_config, random_model
+    from efficientgpt_b200.int8_linear import quantize_model
+    big = a.workload == 'qwen3_8b'
+    prompt_len = 4096 if big else PROMPT_LEN
+    cfg = qwen3_8b_config() if big else qwen3_1p7b_config()
+    dev = torch.device('cuda', local)
+    model = random_model(cfg, dev, seed=0)
+    quantize_model(model, scale_dtype=torch.bfloat16)
+    shape = tp.Qwen3Shape.from_config(model.config)
+    full = tp.full_weights(model)
+    weights = tp.shard(full, shape, rank, world) if world > 1 else full
+    if world > 1:
+        del full, model
+    torch.cuda.empty_cache()
+    eng = tp.TPQwen3Engine(shape, weights, rank, world, prompt_len + NEW_TOKENS)
+    prompt = torch.randint(0, shape.vocab, (1, prompt_len), generator=torch.Generator().manual_seed(0))
+    eng.feed(prompt.to(dev))
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        eng.step()
+        eng.step()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        eng.step()
+
+    def reset():
+        eng.position.fill_(prompt_len)
+
+    reset()
+    time_replays(graph, a.warmup)
+    reset()
+    sampler = ClockSampler()
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+    torch.cuda.synchronize(dev)
+    barrier(world)  # after the sampler's start-up: the ranks' kernels wait on one another with a bounded wait
+    ms = time_replays(graph, a.steps, reset)
+    clocks = sampler.stop(local) if rank == 0 else None
+    ms = max_over_ranks(ms, world)
+    barrier(world)
+    from efficientgpt_b200._lib import device_error
+    err = device_error()
+    tok_s = a.steps / (ms / 1e3)  # one token per step for the whole job (all ranks decode the same token)
+
+    ctxs = [prompt_len + 1 + (i % NEW_TOKENS) for i in range(a.steps)]
+    bytes_rank = eng.weight_bytes() + statistics.fmean(eng.kv_bytes_per_token(c) for c in ctxs)
+    peaks, peak_src = measured_peaks()
+    hbm = float(peaks['hbm_gbs'])
+    gbs = bytes_rank / (ms / 1e3 / a.steps) / 1e9
+    nvlink = 2 * shape.n_layers * shape.hidden * 8 * (world - 1) + 8 * (world - 1) if world > 1 else 0
+
+    # end to end through the engine's public API: pinned host prompt in, every token read back to the host
+    e2e = None
+    if not a.no_e2e:
+        host_prompt = prompt.pin_memory()
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        t0 = time.perf_counter()
+        eng.feed(host_prompt.to(dev, non_blocking=True))
+        host_tok = torch.empty(NEW_TOKENS, dtype=torch.int64).pin_memory()
+        host_tok[0:1].copy_(eng.token, non_blocking=True)
+        torch.cuda.synchronize(dev)
+        t1 = time.perf_counter()
+        for i in range(1, NEW_TOKENS):
+            graph.replay()
+            host_tok[i:i + 1].copy_(eng.token, non_blocking=True)
+        torch.cuda.synchronize(dev)
+        t2 = time.perf_counter()
+        dt = max_over_ranks(t2 - t1, world)
+        e2e = {'value': (NEW_TOKENS - 1) / dt, 'unit': 'tok/s', 'h2d_bytes_per_step': prompt_len * 8 / NEW_TOKENS,
+               'd2h_bytes_per_step': 8, 'ttft_ms': round((t1 - t0) * 1e3, 3),
+               'api': 'efficientgpt_b200.tp.TPQwen3Engine (pinned host prompt fed token by token, then one graph '
+                      'replay and one token read per step)'}
+    if rank == 0:
+        wl = ('qwen3_8b int8 decode, BASELINE config 5' if big else 'qwen3_1.7b int8 decode, BASELINE config 2')
+        line = {
+            'metric': METRIC if not big else METRIC.replace('Qwen3-1.7B', 'Qwen3-8B').replace('1 B200', f'{world} B200'),
+            'value': round(tok_s, 2), 'unit': 'tok/s', 'n_gpus': world, 'steps': a.steps, 'warmup': a.warmup,
+            'ms_per_step': round(ms / a.steps, 5), 'higher_is_better': True, 'scaling': 'strong',
+            'vs_baseline': None, 'dtype': 'int8-weight/bf16', 'data': 'synthetic',
+            'config': {'workload': wl, 'prompt': prompt_len, 'new_tokens': NEW_TOKENS, 'scale_dtype': 'bf16',
+                       'init': 'HF random init N(0,0.02) on the GPU, seed 0',
+                       'parallelism': f'tp{world}' if world > 1 else 'single',
+                       'l2': f'no flush: {bytes_rank / 1e9:.2f} GB streamed per step per GPU, larger than L2',
+                       'step': 'persistent' if eng.persistent else 'launch sequence'},
+            'roofline': {'bound': 'hbm', 'kernel': 'decode_step_kernel' if eng.persistent else 'gemv_i8_kernel',
+                         'achieved': round(gbs, 1), 'peak': hbm, 'unit': 'GB/s', 'frac': round(gbs / hbm, 4),
+                         'traffic': None, 'launches_per_step': 1 if eng.persistent else 5 * shape.n_layers + 1,
+                         'bytes_per_launch': round(bytes_rank), 'avg_launch_us': round(ms * 1e3 / a.steps, 3),
+                         'peak_source': peak_src, 'per': 'GPU (each rank streams its shard)'},
+            'nvlink_bytes_per_token_per_gpu': nvlink,
+            'device_error': err,
+            'e2e': e2e,
+            'cpu_baseline': None,
+            'gpu_launches': a.steps * (1 if eng.persistent else 5 * shape.n_layers + 1),
+            'clocks': clocks,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    eng.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def main():
     a = parse()
     world, rank, local = dist_setup()
     if a.impl == 'reference':
         run_reference(a, world, rank)
+        return
+    if a.workload == 'qwen3_8b' or (world > 1 and not a.replicas):
+        run_tp(a, world, rank, local)
         return
     model, dec, prompt = build('cuda', pdl=not a.no_pdl, persistent=False if a.launch_sequence else None)
     eng = dec.engine

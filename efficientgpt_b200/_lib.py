@@ -44,7 +44,8 @@ class Qwen3Plan(ctypes.Structure):
                 ('embed', P), ('final_norm', P), ('w_lm', P), ('s_lm', P), ('rope_cos', P), ('rope_sin', P),
                 ('token', P), ('position', P), ('h', P), ('qkv', P), ('attn', P), ('act', P), ('logits', P),
                 ('attn_ws', P), ('attn_ws_bytes', SZ), ('lm_ws', P), ('lm_ws_bytes', SZ),
-                ('layers_dev', P), ('sync_ws', P), ('trace', P)]
+                ('layers_dev', P), ('sync_ws', P), ('trace', P),
+                ('tp_rank', ctypes.c_int32), ('tp_world', ctypes.c_int32), ('tp_xchg', P * 8), ('h2', P)]
 
 
 # name -> (restype, argtypes)
@@ -71,6 +72,12 @@ SIGNATURES = {
     'egpt_step_sync_ws_bytes': (SZ, []),
     'egpt_decode_step_persistent': (I32, [ctypes.POINTER(Qwen3Plan), P]),
     'egpt_decode_step_persistent_check': (I32, [ctypes.POINTER(Qwen3Plan)]),
+    'egpt_tp_xchg_bytes': (SZ, [I64]),
+    'egpt_tp_xchg_alloc': (I32, [ctypes.POINTER(P), SZ]),
+    'egpt_tp_xchg_free': (I32, [P]),
+    'egpt_ipc_handle': (I32, [P, P]),
+    'egpt_ipc_open': (I32, [P, ctypes.POINTER(P)]),
+    'egpt_ipc_close': (I32, [P]),
 }
 
 _lib = None

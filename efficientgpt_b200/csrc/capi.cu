@@ -1,6 +1,7 @@
 // Library plumbing (error reporting, device queries) and the whole-token decode step of the Qwen3 family.
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 #include "common.cuh"
@@ -85,6 +86,8 @@ extern "C" int egpt_decode_step(const egpt_qwen3_plan *P, void *stream) {
   if (P->n_layers < 1 || P->hidden < 1 || P->n_q_heads < 1 || P->n_kv_heads < 1 || P->head_dim < 1 ||
       P->intermediate < 1 || P->vocab < 1 || P->cap < 1)
     return set_error(EGPT_ERR_SHAPE, "decode_step: bad model sizes");
+  if (P->tp_world > 1)
+    return set_error(EGPT_ERR_ARG, "decode_step: tensor parallelism runs on egpt_decode_step_persistent only");
   const unsigned pdl = P->flags & EGPT_FLAG_PDL;
   const int sdt = P->scale_dtype;
   const int64_t H = P->hidden, D = P->head_dim, NQ = P->n_q_heads, NKV = P->n_kv_heads, I = P->intermediate;
@@ -115,4 +118,61 @@ extern "C" int egpt_decode_step(const egpt_qwen3_plan *P, void *stream) {
   return egpt_lm_head_argmax(P->token, P->position, P->logits, P->h, P->w_lm, P->s_lm, sdt, P->vocab, H,
                              P->final_norm, P->eps, P->lm_ws, P->lm_ws_bytes,
                              EGPT_FLAG_RMSNORM | EGPT_FLAG_ADVANCE | pdl, stream);
+}
+
+// ---------------------------------------------------------------------------------------- tensor parallelism
+// Exchange region: u64 flags [3][8] at 0, i64 keys [8] at 256, fp64 partials [2][8][hidden] at 4096.
+extern "C" size_t egpt_tp_xchg_bytes(int64_t hidden) {
+  return hidden > 0 ? (size_t)4096 + (size_t)2 * 8 * (size_t)hidden * 8 : 0;
+}
+
+extern "C" int egpt_tp_xchg_alloc(void **ptr, size_t bytes) {
+  clear_error();
+  if (!ptr || bytes == 0) return set_error(EGPT_ERR_ARG, "tp_xchg_alloc: null pointer or zero size");
+  *ptr = nullptr;
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return set_error(EGPT_ERR_LAUNCH, "tp_xchg_alloc: cudaMalloc: %s", cudaGetErrorString(e));
+  e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return set_error(EGPT_ERR_LAUNCH, "tp_xchg_alloc: cudaMemset: %s", cudaGetErrorString(e));
+  }
+  *ptr = p;
+  return EGPT_OK;
+}
+
+extern "C" int egpt_tp_xchg_free(void *ptr) {
+  clear_error();
+  if (!ptr) return EGPT_OK;
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? EGPT_OK : set_error(EGPT_ERR_LAUNCH, "tp_xchg_free: %s", cudaGetErrorString(e));
+}
+
+extern "C" int egpt_ipc_handle(const void *ptr, void *handle64) {
+  clear_error();
+  if (!ptr || !handle64) return set_error(EGPT_ERR_ARG, "ipc_handle: null pointer");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void *>(ptr));
+  if (e != cudaSuccess) return set_error(EGPT_ERR_LAUNCH, "ipc_handle: %s", cudaGetErrorString(e));
+  memcpy(handle64, &h, sizeof(h));
+  return EGPT_OK;
+}
+
+extern "C" int egpt_ipc_open(const void *handle64, void **ptr) {
+  clear_error();
+  if (!ptr || !handle64) return set_error(EGPT_ERR_ARG, "ipc_open: null pointer");
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? EGPT_OK : set_error(EGPT_ERR_LAUNCH, "ipc_open: %s", cudaGetErrorString(e));
+}
+
+extern "C" int egpt_ipc_close(void *ptr) {
+  clear_error();
+  if (!ptr) return EGPT_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? EGPT_OK : set_error(EGPT_ERR_LAUNCH, "ipc_close: %s", cudaGetErrorString(e));
 }

@@ -23,7 +23,13 @@
 //     reference GPU kernel's softmax rounding; ranges exchange their maxima), the last range of each head
 //     combines;
 //   * the lm_head stage keeps (max, index) per CTA; the last CTA reduces them, writes the token and advances
-//     the position and the step epoch.
+//     the position and the step epoch;
+//   * tensor parallelism (TP instantiation, 2/4/8 GPUs, one process each): the stage sizes are this rank's
+//     shard; o_proj and down_proj CTAs store their rows' exact fp64 partial sums into every rank's exchange
+//     region over NVLink, the CTA completing the local barrier raises this rank's flag on every peer, and the
+//     next stage on every rank adds the g partials in rank order before the residual add and RMSNorm; the
+//     lm_head's per-rank (logit, index) keys are exchanged the same way. The collective lives inside the
+//     step kernel: no extra launch, no library call, no second pass over the vector.
 #include <algorithm>
 
 #include "common.cuh"
@@ -70,6 +76,11 @@ struct Params {
   unsigned *epoch;
   int part_bytes;            // shared memory for the layer stages' per-item row sums
   unsigned long long *trace;  // nullable: per-barrier %globaltimer stamps of CTA 0
+  // tensor parallelism (TP instantiation only)
+  int tp_rank, tp_world;
+  int64_t v_embed;            // embedding rows (the whole vocabulary; V above is this rank's lm_head rows)
+  char *xchg[8];              // exchange regions of all ranks, mapped in this process
+  uint16_t *h2;               // second residual buffer
 };
 
 // A GEMV stage: n logical rows in tiles of 16 (GATEUP: tile t = gate rows 8t..8t+7 then up rows 8t..8t+7),
@@ -272,6 +283,91 @@ __device__ bool grid_wait(const Params &P, unsigned long long base, unsigned lon
   return *s_ok != 0;
 }
 
+// ------------------------------------------------------------------------------------------------ TP exchange
+// Exchange region of a rank: u64 flags [3][8] (site kind 0 o_proj, 1 down_proj, 2 lm_head; source rank) holding
+// the sequence number of the last site the source rank completed, u64 lm_head keys [8], fp64 partials [2][8][H].
+constexpr int kXKeyOff = 256;
+constexpr int kXDataOff = 4096;
+__device__ __forceinline__ unsigned long long *xflag(char *x, int kind, int src) {
+  return (unsigned long long *)x + kind * 8 + src;
+}
+__device__ __forceinline__ unsigned long long *xkey(char *x, int src) {
+  return (unsigned long long *)(x + kXKeyOff) + src;
+}
+__device__ __forceinline__ double *xpart(char *x, int kind, int src, int H) {
+  return (double *)(x + kXDataOff) + ((int64_t)kind * 8 + src) * H;
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Sequence number of exchange site `site` (o_proj of layer l: 2l, down_proj: 2l + 1, lm_head: 2L) of step `epoch`:
+// strictly increasing per flag, so a flag at or past it means the site's data has landed.
+__device__ __forceinline__ unsigned long long tp_seq(const Params &P, unsigned epoch, int site) {
+  return (unsigned long long)epoch * (2ull * (unsigned long long)P.L + 1ull) + (unsigned long long)site + 1ull;
+}
+// Raise this rank's flag of `kind` to seq in every rank's region (its own included), after a system-scope fence
+// that orders the data stores (this thread's, or those of the CTAs whose arrivals it observed) before it.
+__device__ __forceinline__ void tp_signal(const Params &P, int kind, unsigned long long seq) {
+  __threadfence_system();
+  for (int q = 0; q < P.tp_world; ++q) st_release_sys_u64(xflag(P.xchg[q], kind, P.tp_rank), seq);
+}
+// One thread: bounded wait until the flag of `kind` of every rank in this rank's region reached seq.
+__device__ __forceinline__ bool tp_wait_flags(const Params &P, int kind, unsigned long long seq) {
+  char *own = P.xchg[P.tp_rank];
+  const uint64_t t0 = globaltimer_ns();
+  for (int r = 0; r < P.tp_world; ++r) {
+    for (int it = 0; ld_acquire_sys_u64(xflag(own, kind, r)) < seq; ++it) {
+      if ((it & 63) == 63) {
+        if (device_error_set()) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          set_device_error(EGPT_ERR_TIMEOUT);
+          return false;
+        }
+      }
+    }
+  }
+  return true;
+}
+// Barrier after an o_proj / down_proj stage. Every CTA makes its peer stores visible system-wide and counts in on
+// the local barrier counter; the CTA whose arrival completes the count raises this rank's flag on every rank.
+// tp_wait then waits for the flags of all ranks (this rank's own flag implies the local barrier).
+__device__ __forceinline__ void tp_arrive(const Params &P, unsigned long long base, unsigned long long idx, int kind,
+                                          unsigned long long seq) {
+  csync();
+  if (threadIdx.x == 0) {
+    if (P.trace && blockIdx.x == 0) P.trace[2 * idx - 1] = globaltimer_ns();
+    __threadfence_system();
+    const unsigned long long prev = atomicAdd(P.bar, 1ull);
+    if (prev + 1ull == (base + idx) * gridDim.x) tp_signal(P, kind, seq);
+  }
+}
+__device__ bool tp_wait(const Params &P, unsigned long long idx, int kind, unsigned long long seq, int *s_ok) {
+  if (threadIdx.x == 0) {
+    const int ok = tp_wait_flags(P, kind, seq) ? 1 : 0;
+    __threadfence();
+    if (P.trace && blockIdx.x == 0) P.trace[2 * idx] = globaltimer_ns();
+    *s_ok = ok;
+  }
+  csync();
+  return *s_ok != 0;
+}
+// lm_head key of a rank's best (logit, global index): larger key = larger logit, then lower index (NaN above
+// everything, -0 == +0), the order of argmax_better.
+__device__ __forceinline__ unsigned long long argmax_key(float v, long long idx) {
+  unsigned u = __float_as_uint(v);
+  if (v != v) u = 0xFFFFFFFFu;
+  else if (v == 0.f) u = 0x80000000u;
+  else u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)idx);
+}
+// 2^e as a double (e within the normal range, which every staged-input exponent is).
+__device__ __forceinline__ double pow2_f64(int e) { return __longlong_as_double((long long)(e + 1023) << 52); }
+
 // Trace: stamp k (CTA 0, thread 0) of the second trace region: the moment stage k's input is ready (GEMV
 // stages: staged and normalised; attention: this CTA's scores done).
 __device__ __forceinline__ void stamp(const Params &P, int k) {
@@ -343,20 +439,61 @@ __device__ __forceinline__ void digits4(int X, int (&d)[4]) {
 // planes xd[d][i] in [-128, 127], zero-padded to whole 256-column chunks. One CTA reduction gives both the sum
 // of squares and the bound (max |x w| * rsqrt(...) * (1 + 2^-8)^2 covers the two bf16 roundings of the norm).
 // copy_to (nullable) receives the raw values (layer 0: h = embedding row). Returns E.
+// TP (tin non-null): the input is the residual sum h' = bf16(src + bf16(fp32(sum_r part_r) * s)) of the previous
+// o_proj / down_proj, from its np ranks' exact partials (added in rank order) and row scales; copy_to gets h'.
+struct TpIn {
+  const double *parts;  // rank r's partials at parts + r * k
+  const void *s;        // row scales of the stage that produced them
+  int np, s_bf16;
+};
+template <bool TP>
 __device__ int stage_input(const uint16_t *src, int64_t k, const NormW *nw, float eps, int8_t *xd, float *red,
-                           uint16_t *copy_to) {
+                           uint16_t *copy_to, const TpIn *tin) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   float v[kMaxPerThread];
   float ss = 0.f, mx = 0.f;
+  if (TP && tin) {
 #pragma unroll
-  for (int j = 0; j < kGroups; ++j) {
-    const int64_t i = 4 * ((int64_t)t + (int64_t)j * kCT);
-    uint2 u = make_uint2(0u, 0u);
-    if (i < k) {
-      u = __ldcg((const uint2 *)(src + i));
-      if (copy_to) *(uint2 *)(copy_to + i) = u;
+    for (int j = 0; j < kGroups; ++j) {
+      const int64_t i = 4 * ((int64_t)t + (int64_t)j * kCT);
+      float o[4] = {0.f, 0.f, 0.f, 0.f};
+      if (i < k) {
+        const uint2 u = __ldcg((const uint2 *)(src + i));
+        float sc[4];
+        if (tin->s_bf16) {
+          const uint2 su = *(const uint2 *)((const uint16_t *)tin->s + i);
+          sc[0] = bf16_lo(su.x), sc[1] = bf16_hi(su.x), sc[2] = bf16_lo(su.y), sc[3] = bf16_hi(su.y);
+        } else {
+          const float4 sf = *(const float4 *)((const float *)tin->s + i);
+          sc[0] = sf.x, sc[1] = sf.y, sc[2] = sf.z, sc[3] = sf.w;
+        }
+        double a[4] = {0.0, 0.0, 0.0, 0.0};
+        for (int r = 0; r < tin->np; ++r) {
+          const double2 *pp = (const double2 *)(tin->parts + (int64_t)r * k + i);
+          const double2 p0 = __ldcg(pp), p1 = __ldcg(pp + 1);
+          a[0] += p0.x, a[1] += p0.y, a[2] += p1.x, a[3] += p1.y;
+        }
+        const float hs[4] = {bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y)};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) o[q] = round_bf16(hs[q] + round_bf16(__double2float_rn(a[q]) * sc[q]));
+        if (copy_to)
+          *(uint2 *)(copy_to + i) = make_uint2((uint32_t)f32_to_bf16_bits(o[0]) | ((uint32_t)f32_to_bf16_bits(o[1]) << 16),
+                                               (uint32_t)f32_to_bf16_bits(o[2]) | ((uint32_t)f32_to_bf16_bits(o[3]) << 16));
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[4 * j + q] = o[q];
     }
-    v[4 * j] = bf16_lo(u.x), v[4 * j + 1] = bf16_hi(u.x), v[4 * j + 2] = bf16_lo(u.y), v[4 * j + 3] = bf16_hi(u.y);
+  } else {
+#pragma unroll
+    for (int j = 0; j < kGroups; ++j) {
+      const int64_t i = 4 * ((int64_t)t + (int64_t)j * kCT);
+      uint2 u = make_uint2(0u, 0u);
+      if (i < k) {
+        u = __ldcg((const uint2 *)(src + i));
+        if (copy_to) *(uint2 *)(copy_to + i) = u;
+      }
+      v[4 * j] = bf16_lo(u.x), v[4 * j + 1] = bf16_hi(u.x), v[4 * j + 2] = bf16_lo(u.y), v[4 * j + 3] = bf16_hi(u.y);
+    }
   }
 #pragma unroll
   for (int e = 0; e < kMaxPerThread; ++e) {
@@ -466,6 +603,7 @@ __device__ __forceinline__ float load_scale(const Params &P, const void *s, int6
 struct EpiIn {
   float s0, s1, res;
 };
+template <bool TP>
 __device__ __forceinline__ void load_epi(const Params &P, int gs, EpiIn &in) {
   const Stage sd = stage_desc(P, gs);
   in.s0 = in.s1 = in.res = 0.f;
@@ -477,7 +615,7 @@ __device__ __forceinline__ void load_epi(const Params &P, int gs, EpiIn &in) {
   const int r = e % per_tile;
   in.s0 = load_scale(P, sd.s, tile_row(sd, tile, r));
   if (sd.kind == GATEUP) in.s1 = load_scale(P, sd.s, tile_row(sd, tile, r + 8));
-  if (sd.kind == OPROJ || sd.kind == DOWN) in.res = bf16_bits_to_f32(__ldcg(P.h + tile * kTileRows + r));
+  if (!TP && (sd.kind == OPROJ || sd.kind == DOWN)) in.res = bf16_bits_to_f32(__ldcg(P.h + tile * kTileRows + r));
 }
 
 // Consume this warp's items of stage s (the stream's cursor is at stage s or later). Per item and lane (g =
@@ -488,6 +626,8 @@ __device__ __forceinline__ void load_epi(const Params &P, int gs, EpiIn &in) {
 // after a CTA barrier, threads e < (CTA tiles) x 16 (x 8 for gate/up pairs) add a row's items in order and
 // apply the epilogue; their scales and residuals are fetched before the items stream. The lm_head epilogue
 // (bf16 logits, argmax) runs in the warp that owns the tile.
+// TP: o_proj / down_proj rows store their exact partial sum (fp64, before the scale) into every rank's region.
+template <bool TP>
 __device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, int E, long long *part,
                            const EpiIn &ein, Best &best) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -577,7 +717,15 @@ __device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, 
   switch (sd.kind) {
     case QKV: P.qkv[etile * kTileRows + er] = f32_to_bf16_bits(y0 * es0); break;
     case OPROJ:
-    case DOWN: P.h[etile * kTileRows + er] = f32_to_bf16_bits(eres + round_bf16(y0 * es0)); break;
+    case DOWN:
+      if (TP) {
+        const double y = __ll2double_rn(T0) * pow2_f64(E);  // exact: |T0| < 2^53
+        const int64_t row = etile * kTileRows + er;
+        for (int q = 0; q < P.tp_world; ++q) xpart(P.xchg[q], sd.kind == OPROJ ? 0 : 1, P.tp_rank, P.H)[row] = y;
+      } else {
+        P.h[etile * kTileRows + er] = f32_to_bf16_bits(eres + round_bf16(y0 * es0));
+      }
+      break;
     default: {  // GATEUP: act = bf16(bf16(silu(gate)) * up)
       const float gt = round_bf16(y0 * es0), up = round_bf16(mul_pow2(__ll2float_rn(T1), E) * es1);
       P.act[etile * 8 + er] = f32_to_bf16_bits(round_bf16(gt / (1.0f + expf(-gt))) * up);
@@ -741,7 +889,7 @@ __device__ void attention_task(const Params &P, const egpt_qwen3_layer &Ly, int 
 }
 
 // ------------------------------------------------------------------------------------------------ kernel
-template <int DPL, int GRP>
+template <int DPL, int GRP, bool TP>
 __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
   extern __shared__ __align__(128) uint8_t smem[];
   float *red = (float *)smem;                    // 64 floats
@@ -766,13 +914,14 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
   stream_start(P, S, ring + (size_t)warp * kRing * kSlot);
 
   const unsigned long long nb = 5ull * (unsigned long long)P.L;  // grid barriers per step
-  const unsigned long long base = (unsigned long long)(*(volatile unsigned *)P.epoch) * nb;
+  const unsigned epoch = *(volatile unsigned *)P.epoch;
+  const unsigned long long base = (unsigned long long)epoch * nb;
   unsigned long long bidx = 0;
   bool ok = true;
   Best best{-INFINITY, 0x7fffffff};
   const int64_t pos = *P.position;
   const int64_t tok = *P.token;
-  if (pos < 0 || pos >= P.cap || tok < 0 || tok >= P.V) {
+  if (pos < 0 || pos >= P.cap || tok < 0 || tok >= P.v_embed) {
     if (threadIdx.x == 0) set_device_error(EGPT_ERR_SHAPE);
     ok = false;
   }
@@ -807,25 +956,50 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
         const uint16_t *src = ph == 2 ? P.attn : ph == 4 ? P.act : (ph == 0 && l == 0) ? P.embed + (ok ? tok : 0) * P.H : P.h;
         const int64_t k = ph == 2 ? (int64_t)P.NQ * P.D : ph == 4 ? P.I : P.H;
         const bool norm = ph == 0 || ph == 3 || ph == 5;
-        const int E = stage_input(src, k, norm ? &nw : nullptr, P.eps, xd, red,
-                                  (st == 0 && blockIdx.x == 0) ? P.h : nullptr);
+        uint16_t *copy_to = (st == 0 && blockIdx.x == 0) ? P.h : nullptr;
+        TpIn tin;
+        const TpIn *tinp = nullptr;
+        if (TP && ((ph == 0 && l > 0) || ph == 3 || ph == 5)) {
+          // residual sums: q|k|v and lm_head read h2 + down_proj partials (q|k|v: CTA 0 stores the sum in h),
+          // gate|up reads h + o_proj partials (CTA 0 stores the sum in h2)
+          const bool after_o = ph == 3;
+          src = after_o ? P.h : P.h2;
+          tin.parts = xpart(P.xchg[P.tp_rank], after_o ? 0 : 1, 0, P.H);
+          tin.s = after_o ? Ly.s_o : layers[l - 1].s_down;
+          tin.np = P.tp_world;
+          tin.s_bf16 = P.scale_bf16;
+          tinp = &tin;
+          copy_to = blockIdx.x != 0 || ph == 5 ? nullptr : after_o ? P.h2 : P.h;
+        }
+        const int E = stage_input<TP>(src, k, norm ? &nw : nullptr, P.eps, xd, red, copy_to, tinp);
         stamp(P, st);
-        load_epi(P, ph == 5 ? 4 * P.L : 4 * l + (ph == 0 ? 0 : ph - 1), ein);  // consumed after the items
-        gemv_stage(P, ph == 5 ? 4 * P.L : 4 * l + (ph == 0 ? 0 : ph - 1), S, xd, E, part, ein, best);
+        load_epi<TP>(P, ph == 5 ? 4 * P.L : 4 * l + (ph == 0 ? 0 : ph - 1), ein);  // consumed after the items
+        gemv_stage<TP>(P, ph == 5 ? 4 * P.L : 4 * l + (ph == 0 ? 0 : ph - 1), S, xd, E, part, ein, best);
       }
     }
     if (st < 5 * P.L) {
+      // TP: the barriers after o_proj (xk 0) and down_proj (xk 1) also exchange the partial sums between ranks
+      const int xk = (TP && st >= 0) ? (st % 5 == 2 ? 0 : st % 5 == 4 ? 1 : -1) : -1;
+      const unsigned long long xseq = xk >= 0 ? tp_seq(P, epoch, 2 * (st / 5) + xk) : 0ull;
       // step-invariant inputs of stage st + 1, requested between arriving at the barrier that precedes it and
       // waiting there (after the arrival's fence, which would otherwise wait for them): norm weights, the
       // attention prologue's weights and RoPE row, KV ranges
-      if (st >= 0) grid_arrive(P, bidx + 1);
+      if (st >= 0) {
+        if (xk >= 0)
+          tp_arrive(P, base, bidx + 1, xk, xseq);
+        else
+          grid_arrive(P, bidx + 1);
+      }
       const int n = st + 1, ln = n / 5, pn = n == 5 * P.L ? 5 : n % 5;
       const egpt_qwen3_layer &Ln = layers[ln < P.L ? ln : P.L - 1];
       if (pn == 0 || pn == 3 || pn == 5)
         load_norm(pn == 5 ? P.final_norm : (const uint16_t *)(pn == 0 ? Ln.ln_in : Ln.ln_post), P.H, nw);
       if (pn == 1 && attn_cta) attn_preload<DPL, GRP>(P, Ln, blockIdx.x, nsplit, bps, pos, pre);
       if (pn == 0 && attn_cta) attn_prefetch_kv<DPL, GRP>(P, Ln, blockIdx.x, nsplit, bps, pos);
-      if (st >= 0) ok = grid_wait(P, base, ++bidx, &s_flag) && ok;
+      if (st >= 0) {
+        ++bidx;
+        ok = (xk >= 0 ? tp_wait(P, bidx, xk, xseq, &s_flag) : grid_wait(P, base, bidx, &s_flag)) && ok;
+      }
     }
   }
   if (P.trace && blockIdx.x == 0 && threadIdx.x == 0) P.trace[1 + 10 * P.L] = globaltimer_ns();
@@ -870,7 +1044,21 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
     if (threadIdx.x == 0) {
       for (int w = 1; w < kNC; ++w)
         if (argmax_better(s_bv[w], s_bi[w], bv, bi)) bv = s_bv[w], bi = s_bi[w];
-      *P.token = ok ? (int64_t)bi : 0;
+      int64_t next = bi;
+      if (TP) {  // every rank's best key to every rank, then the same maximum everywhere
+        const unsigned long long seq = tp_seq(P, epoch, 2 * P.L);
+        const unsigned long long key = argmax_key(bv, (long long)bi + (long long)P.tp_rank * P.V);
+        for (int q = 0; q < P.tp_world; ++q) *(volatile unsigned long long *)xkey(P.xchg[q], P.tp_rank) = key;
+        tp_signal(P, 2, seq);
+        if (!tp_wait_flags(P, 2, seq)) ok = false;
+        unsigned long long bk = 0ull;
+        for (int r = 0; r < P.tp_world; ++r) {
+          const unsigned long long kr = *(volatile unsigned long long *)xkey(P.xchg[P.tp_rank], r);
+          bk = kr > bk ? kr : bk;
+        }
+        next = (int64_t)(0xFFFFFFFFu - (unsigned)(bk & 0xFFFFFFFFull));
+      }
+      *P.token = ok ? next : 0;
       *P.position += 1;
       *P.lm_cnt = 0u;
       *P.epoch += 1u;
@@ -891,9 +1079,9 @@ static size_t part_bytes(const egpt_qwen3_plan *Pl, int G) {
   return (size_t)items * kTileRows * 8;
 }
 
-template <int DPL, int GRP>
+template <int DPL, int GRP, bool TP>
 static cudaError_t launch(const Params &P, size_t smem, cudaStream_t st) {
-  auto kern = decode_step_kernel<DPL, GRP>;
+  auto kern = decode_step_kernel<DPL, GRP, TP>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -938,6 +1126,18 @@ static int persistent_validate(const egpt_qwen3_plan *Pl, size_t *smem_out) {
                      "of 16 and at most %d", ps::kMaxPerThread * ps::kCT);
   const int G = num_sms();
   if (G > kArgmaxMaxCtas) return set_error(EGPT_ERR_SHAPE, "decode_step_persistent: too many SMs");
+  if (Pl->tp_world > 1) {
+    const int g = Pl->tp_world;
+    if (g != 2 && g != 4 && g != 8) return set_error(EGPT_ERR_ARG, "decode_step_persistent: tp_world must be 2, 4 or 8");
+    if (Pl->tp_rank < 0 || Pl->tp_rank >= g) return set_error(EGPT_ERR_ARG, "decode_step_persistent: tp_rank out of range");
+    if (!Pl->h2) return set_error(EGPT_ERR_ARG, "decode_step_persistent: tensor parallelism needs h2");
+    for (int r = 0; r < g; ++r)
+      if (!Pl->tp_xchg[r] || (uintptr_t)Pl->tp_xchg[r] % 256)
+        return set_error(EGPT_ERR_ARG, "decode_step_persistent: exchange region of rank %d missing or not 256-byte aligned", r);
+    if (Pl->vocab * g > 0x7fffffffLL) return set_error(EGPT_ERR_SHAPE, "decode_step_persistent: vocabulary too large");
+  } else if (Pl->tp_world < 0) {
+    return set_error(EGPT_ERR_ARG, "decode_step_persistent: negative tp_world");
+  }
   // weights and each tile's scales are copied in 16-byte pieces
   const size_t sal = 16;
   bool aligned = (uintptr_t)Pl->w_lm % 16 == 0 && (uintptr_t)Pl->s_lm % sal == 0;
@@ -1009,12 +1209,21 @@ extern "C" int egpt_decode_step_persistent(const egpt_qwen3_plan *Pl, void *stre
   P.epoch = (unsigned *)((char *)Pl->sync_ws + 8);
   P.part_bytes = (int)ps::part_bytes(Pl, num_sms());
   P.trace = (unsigned long long *)Pl->trace;
+  P.v_embed = Pl->vocab;
+  const bool tp = Pl->tp_world > 1;
+  if (tp) {
+    P.tp_rank = Pl->tp_rank, P.tp_world = Pl->tp_world;
+    P.v_embed = Pl->vocab * Pl->tp_world;
+    for (int r = 0; r < Pl->tp_world; ++r) P.xchg[r] = (char *)Pl->tp_xchg[r];
+    P.h2 = (uint16_t *)Pl->h2;
+  }
   cudaError_t e;
+  const cudaStream_t cs = (cudaStream_t)stream;
   if (D == 128 && grp == 2)
-    e = ps::launch<4, 2>(P, smem, (cudaStream_t)stream);
+    e = tp ? ps::launch<4, 2, true>(P, smem, cs) : ps::launch<4, 2, false>(P, smem, cs);
   else if (D == 128)
-    e = ps::launch<4, 4>(P, smem, (cudaStream_t)stream);
+    e = tp ? ps::launch<4, 4, true>(P, smem, cs) : ps::launch<4, 4, false>(P, smem, cs);
   else
-    e = ps::launch<1, 2>(P, smem, (cudaStream_t)stream);
+    e = tp ? ps::launch<1, 2, true>(P, smem, cs) : ps::launch<1, 2, false>(P, smem, cs);
   return check_launch(e, "decode_step_kernel");
 }

@@ -3,8 +3,9 @@
  *
  * Every entry point takes raw device pointers, sizes and a cudaStream_t passed as `void *` (NULL = the
  * legacy default stream), launches stream-ordered work and returns an int status (EGPT_OK = 0). Nothing
- * here allocates device memory: callers own weights, activations, KV cache and workspaces, so every call
- * can be captured in a CUDA graph. On a non-zero status egpt_last_error() returns a message for the
+ * here allocates device memory except egpt_tp_xchg_alloc (CUDA IPC exports whole allocations, so the
+ * tensor-parallel exchange region is one of its own): callers own weights, activations, KV cache and
+ * workspaces, so every call can be captured in a CUDA graph. On a non-zero status egpt_last_error() returns a message for the
  * calling thread.
  *
  * The "replaces" line above each function names the reference symbol (BagelsFun/efficientgpt, paths
@@ -211,22 +212,54 @@ typedef struct egpt_qwen3_plan {
                                    [1+2B] lm_head stage done, [2+2B] token written, [3+2B] unused,
                                    [4+2B+k] stage k's input ready (k < B: the stage before barrier k+1;
                                    k = B: lm_head) (B = 5 * n_layers barriers)                            */
+  /* tensor parallelism (egpt_decode_step_persistent only; tp_world 0 or 1 = one GPU). With tp_world > 1 the
+     sizes n_q_heads, n_kv_heads, intermediate and vocab, the layer weights, lm_head and KV caches are this
+     rank's shard (egpt_tp_* below); hidden, the embedding and the norms are whole.                        */
+  int32_t tp_rank, tp_world;    /* world 2, 4 or 8; every rank runs the same step at the same epoch        */
+  void *tp_xchg[8];             /* exchange region of every rank (egpt_tp_xchg_bytes(hidden) bytes, zero-
+                                   filled before the first step), mapped in this process; [tp_rank] is own */
+  void *h2;                     /* tp: second bf16 [hidden] residual buffer (the layer's two residual sums
+                                   alternate between h and h2)                                            */
 } egpt_qwen3_plan;
 
 EGPT_API int egpt_decode_step(const egpt_qwen3_plan *plan, void *stream);
 
 /* Persistent variant of egpt_decode_step: the whole token in ONE cooperative kernel with one CTA per SM.
- * Every warp streams its share of every weight matrix of the step (row pairs, 2048-column chunks) through
- * its own shared-memory ring (cp.async, 3 chunks in flight, plus L2 prefetch further ahead) across stage
- * boundaries, while the CTAs run the stages separated by bounded grid barriers; same arithmetic and results
- * as egpt_decode_step. Needs plan->layers_dev and plan->sync_ws; after a device error (egpt_device_error)
- * sync_ws and the workspaces must be zero-filled again. Built for head_dim 128 with 2 or 4 q heads per kv
- * head and head_dim 32 with 2; other shapes, and activations too wide for shared memory next to the ring
- * (max(hidden, intermediate, nq*d) above about 6400 on a 227 KB part), return EGPT_ERR_SHAPE.
+ * Every warp streams its share of every weight matrix of the step (16-row tiles in 256-column items)
+ * through its own shared-memory ring (cp.async, 2 items in flight) across stage boundaries, while the CTAs
+ * run the stages separated by bounded grid barriers. The GEMVs are exact: the stage input is staged as
+ * fixed point (x = X 2^E, |X| < 2^30, four int8 digit planes), int8 tensor-core MMAs give exact int64 row
+ * sums, and each row is rounded once (then scaled and rounded at the reference's bf16 points), so results
+ * can differ from egpt_decode_step's fp32 sums in the last bits. Needs plan->layers_dev and plan->sync_ws;
+ * after a device error (egpt_device_error) sync_ws and the workspaces must be zero-filled again. Built for
+ * head_dim 128 with 2 or 4 q heads per kv head and head_dim 32 with 2; hidden, intermediate and nq*d up to
+ * 6144 and multiples of 16, vocab a multiple of 16; other shapes return EGPT_ERR_SHAPE.
  * egpt_decode_step_persistent_check runs the same host-side checks without launching anything. */
 EGPT_API size_t egpt_step_sync_ws_bytes(void);
 EGPT_API int egpt_decode_step_persistent(const egpt_qwen3_plan *plan, void *stream);
 EGPT_API int egpt_decode_step_persistent_check(const egpt_qwen3_plan *plan);
+
+/* ---- tensor-parallel decode step (2, 4 or 8 GPUs of one NVLink/NVSwitch box, one process per GPU) ------
+ * No counterpart in the reference (its decode runs on one GPU): the Megatron-style split of the step.
+ * Rank r of g holds q heads [r nq/g, (r+1) nq/g) with their kv heads (q|k|v rows, KV cache), the matching
+ * columns of o_proj, gate/up rows and down_proj columns [r I/g, (r+1) I/g), and lm_head rows
+ * [r V/g, (r+1) V/g). egpt_decode_step_persistent with plan->tp_world = g runs the whole token in one kernel
+ * per GPU: after o_proj and down_proj every CTA stores its rows' exact partial sums (fp64, unscaled) into
+ * every rank's exchange region over NVLink (plain peer stores, no multicast), the CTA that completes the
+ * local barrier raises this rank's flag on every peer, and the next stage on every rank adds the g
+ * partials in rank order, scales, rounds and adds the residual as the one-GPU step does. The lm_head
+ * stage exchanges one (logit, index) key per rank the same way; every rank writes the same token. All
+ * flag waits are bounded (EGPT_ERR_TIMEOUT via egpt_device_error). The exchange region holds flags
+ * [3][8] (u64 sequence numbers), keys [8] and fp64 partials [2][8][hidden].
+ * egpt_tp_xchg_alloc: cudaMalloc + zero fill of one region on the current device (free with
+ * egpt_tp_xchg_free). egpt_ipc_handle writes the 64-byte CUDA IPC handle of such a region; egpt_ipc_open
+ * maps a peer's handle into this process (peer access enabled), egpt_ipc_close unmaps it. */
+EGPT_API size_t egpt_tp_xchg_bytes(int64_t hidden);
+EGPT_API int egpt_tp_xchg_alloc(void **ptr, size_t bytes);
+EGPT_API int egpt_tp_xchg_free(void *ptr);
+EGPT_API int egpt_ipc_handle(const void *ptr, void *handle64);
+EGPT_API int egpt_ipc_open(const void *handle64, void **ptr);
+EGPT_API int egpt_ipc_close(void *ptr);
 
 #ifdef __cplusplus
 }

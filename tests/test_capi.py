@@ -65,3 +65,37 @@ def test_ops_reject_cpu_tensors():
         quantize_weight(torch.randn(4, 4))
     with pytest.raises(ValueError, match='bf16'):
         int8_linear(torch.zeros(2, 32), torch.zeros(8, 32, dtype=torch.int8), torch.ones(8))
+
+
+def test_plan_struct_layout_matches_the_header(tmp_path):
+    """The ctypes mirror of egpt_qwen3_plan / egpt_qwen3_layer has the C compiler's size and field offsets."""
+    import shutil
+    import subprocess
+    cc = shutil.which('gcc') or shutil.which('cc')
+    if cc is None:
+        pytest.skip('no C compiler')
+    plan_fields = [f[0] for f in L.Qwen3Plan._fields_]
+    layer_fields = [f[0] for f in L.Qwen3Layer._fields_]
+    src = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{L.HEADER_PATH}"', 'int main(void) {',
+           'printf("%zu %zu\\n", sizeof(egpt_qwen3_plan), sizeof(egpt_qwen3_layer));']
+    src += [f'printf("%zu\\n", offsetof(egpt_qwen3_plan, {f}));' for f in plan_fields]
+    src += [f'printf("%zu\\n", offsetof(egpt_qwen3_layer, {f}));' for f in layer_fields]
+    src += ['return 0; }']
+    (tmp_path / 'layout.c').write_text('\n'.join(src))
+    subprocess.run([cc, '-o', str(tmp_path / 'layout'), str(tmp_path / 'layout.c')], check=True)
+    out = subprocess.run([str(tmp_path / 'layout')], check=True, capture_output=True, text=True).stdout.split()
+    vals = [int(v) for v in out]
+    assert vals[0] == ctypes.sizeof(L.Qwen3Plan) and vals[1] == ctypes.sizeof(L.Qwen3Layer)
+    got = vals[2:]
+    want = [getattr(L.Qwen3Plan, f).offset for f in plan_fields] + [getattr(L.Qwen3Layer, f).offset for f in layer_fields]
+    assert got == want
+
+
+def test_tp_exchange_size_and_guards():
+    lib = L.load()
+    assert lib.egpt_tp_xchg_bytes(4096) == 4096 + 2 * 8 * 4096 * 8
+    assert lib.egpt_tp_xchg_bytes(0) == 0
+    assert lib.egpt_tp_xchg_alloc(None, 64) == L.EGPT_ERR_ARG
+    assert lib.egpt_ipc_handle(None, None) == L.EGPT_ERR_ARG
+    assert lib.egpt_ipc_open(None, None) == L.EGPT_ERR_ARG
+    assert lib.egpt_ipc_close(None) == L.EGPT_OK
