@@ -121,9 +121,9 @@ extern "C" int egpt_decode_step(const egpt_qwen3_plan *P, void *stream) {
 }
 
 // ---------------------------------------------------------------------------------------- tensor parallelism
-// Exchange region: u64 flags [3][8] at 0, i64 keys [8] at 256, fp64 partials [2][8][hidden] at 4096.
+// Exchange region: 16-byte LL slots, lm_head keys [8] at 0, fp64 partial sums [2][8][hidden] at 4096.
 extern "C" size_t egpt_tp_xchg_bytes(int64_t hidden) {
-  return hidden > 0 ? (size_t)4096 + (size_t)2 * 8 * (size_t)hidden * 8 : 0;
+  return hidden > 0 ? (size_t)4096 + (size_t)2 * 8 * (size_t)hidden * 16 : 0;
 }
 
 extern "C" int egpt_tp_xchg_alloc(void **ptr, size_t bytes) {

@@ -26,10 +26,10 @@
 //     the position and the step epoch;
 //   * tensor parallelism (TP instantiation, 2/4/8 GPUs, one process each): the stage sizes are this rank's
 //     shard; o_proj and down_proj CTAs store their rows' exact fp64 partial sums into every rank's exchange
-//     region over NVLink, the CTA completing the local barrier raises this rank's flag on every peer, and the
-//     next stage on every rank adds the g partials in rank order before the residual add and RMSNorm; the
-//     lm_head's per-rank (logit, index) keys are exchanged the same way. The collective lives inside the
-//     step kernel: no extra launch, no library call, no second pass over the vector.
+//     region over NVLink as sequence-tagged LL slots, and the next stage on every rank waits for the slots it
+//     reads and adds the g partials in rank order before the residual add and RMSNorm; those two stages need
+//     no grid barrier. The lm_head's per-rank (logit, index) keys are exchanged the same way. The collective
+//     lives inside the step kernel: no extra launch, no library call, no fence or flag round trip.
 #include <algorithm>
 
 #include "common.cuh"
@@ -284,77 +284,47 @@ __device__ bool grid_wait(const Params &P, unsigned long long base, unsigned lon
 }
 
 // ------------------------------------------------------------------------------------------------ TP exchange
-// Exchange region of a rank: u64 flags [3][8] (site kind 0 o_proj, 1 down_proj, 2 lm_head; source rank) holding
-// the sequence number of the last site the source rank completed, u64 lm_head keys [8], fp64 partials [2][8][H].
-constexpr int kXKeyOff = 256;
+// Exchange region of a rank: LL slots of 16 bytes, each carrying a 64-bit payload as two 8-byte words
+// (sequence number << 32 | 32 payload bits). Every 8-byte word is written and read in one piece, so a reader that
+// finds the expected sequence number in both words has the payload of that exchange site: data and flag travel
+// together, with no fence, flag or barrier between producer and consumer. Layout: lm_head keys [8] at 0,
+// partial sums [2 = o_proj, down_proj][8 source ranks][H] at 4096.
 constexpr int kXDataOff = 4096;
-__device__ __forceinline__ unsigned long long *xflag(char *x, int kind, int src) {
-  return (unsigned long long *)x + kind * 8 + src;
+__device__ __forceinline__ char *xkey(char *x, int src) { return x + 16 * src; }
+__device__ __forceinline__ char *xpart(char *x, int kind, int src, int H) {
+  return x + kXDataOff + (((int64_t)kind * 8 + src) * H) * 16;
 }
-__device__ __forceinline__ unsigned long long *xkey(char *x, int src) {
-  return (unsigned long long *)(x + kXKeyOff) + src;
+__device__ __forceinline__ void ll_store(char *p, unsigned long long v, unsigned seq) {
+  const unsigned long long hi = (unsigned long long)seq << 32;
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(hi | (v & 0xFFFFFFFFull)), "l"(hi | (v >> 32))
+               : "memory");
 }
-__device__ __forceinline__ double *xpart(char *x, int kind, int src, int H) {
-  return (double *)(x + kXDataOff) + ((int64_t)kind * 8 + src) * H;
+__device__ __forceinline__ bool ll_load(const char *p, unsigned seq, unsigned long long &v) {
+  unsigned long long w0, w1;
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p) : "memory");
+  v = (w0 & 0xFFFFFFFFull) | (w1 << 32);
+  return (unsigned)(w0 >> 32) == seq && (unsigned)(w1 >> 32) == seq;
 }
-__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long *p) {
+// Sequence number of exchange site `site` (o_proj of layer l: 2l, down_proj: 2l + 1, lm_head: 2L) of step `epoch`,
+// never 0 (the value of a zero-filled region).
+__device__ __forceinline__ unsigned tp_seq(const Params &P, unsigned epoch, int site) {
+  const unsigned long long n = (unsigned long long)epoch * (2ull * (unsigned long long)P.L + 1ull) + (unsigned)site;
+  return (unsigned)(n % 0xFFFFFFFFull) + 1u;
+}
+// Bounded spin until slot p carries sequence number seq; on timeout (or another wait's error) records the error
+// and returns whatever the slot holds.
+__device__ __forceinline__ unsigned long long ll_wait(const char *p, unsigned seq, uint64_t t0) {
   unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys_u64(unsigned long long *p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-// Sequence number of exchange site `site` (o_proj of layer l: 2l, down_proj: 2l + 1, lm_head: 2L) of step `epoch`:
-// strictly increasing per flag, so a flag at or past it means the site's data has landed.
-__device__ __forceinline__ unsigned long long tp_seq(const Params &P, unsigned epoch, int site) {
-  return (unsigned long long)epoch * (2ull * (unsigned long long)P.L + 1ull) + (unsigned long long)site + 1ull;
-}
-// Raise this rank's flag of `kind` to seq in every rank's region (its own included), after a system-scope fence
-// that orders the data stores (this thread's, or those of the CTAs whose arrivals it observed) before it.
-__device__ __forceinline__ void tp_signal(const Params &P, int kind, unsigned long long seq) {
-  __threadfence_system();
-  for (int q = 0; q < P.tp_world; ++q) st_release_sys_u64(xflag(P.xchg[q], kind, P.tp_rank), seq);
-}
-// One thread: bounded wait until the flag of `kind` of every rank in this rank's region reached seq.
-__device__ __forceinline__ bool tp_wait_flags(const Params &P, int kind, unsigned long long seq) {
-  char *own = P.xchg[P.tp_rank];
-  const uint64_t t0 = globaltimer_ns();
-  for (int r = 0; r < P.tp_world; ++r) {
-    for (int it = 0; ld_acquire_sys_u64(xflag(own, kind, r)) < seq; ++it) {
-      if ((it & 63) == 63) {
-        if (device_error_set()) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          set_device_error(EGPT_ERR_TIMEOUT);
-          return false;
-        }
+  for (int it = 0; !ll_load(p, seq, v); ++it) {
+    if ((it & 63) == 63) {
+      if (device_error_set()) break;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        set_device_error(EGPT_ERR_TIMEOUT);
+        break;
       }
     }
   }
-  return true;
-}
-// Barrier after an o_proj / down_proj stage. Every CTA makes its peer stores visible system-wide and counts in on
-// the local barrier counter; the CTA whose arrival completes the count raises this rank's flag on every rank.
-// tp_wait then waits for the flags of all ranks (this rank's own flag implies the local barrier).
-__device__ __forceinline__ void tp_arrive(const Params &P, unsigned long long base, unsigned long long idx, int kind,
-                                          unsigned long long seq) {
-  csync();
-  if (threadIdx.x == 0) {
-    if (P.trace && blockIdx.x == 0) P.trace[2 * idx - 1] = globaltimer_ns();
-    __threadfence_system();
-    const unsigned long long prev = atomicAdd(P.bar, 1ull);
-    if (prev + 1ull == (base + idx) * gridDim.x) tp_signal(P, kind, seq);
-  }
-}
-__device__ bool tp_wait(const Params &P, unsigned long long idx, int kind, unsigned long long seq, int *s_ok) {
-  if (threadIdx.x == 0) {
-    const int ok = tp_wait_flags(P, kind, seq) ? 1 : 0;
-    __threadfence();
-    if (P.trace && blockIdx.x == 0) P.trace[2 * idx] = globaltimer_ns();
-    *s_ok = ok;
-  }
-  csync();
-  return *s_ok != 0;
+  return v;
 }
 // lm_head key of a rank's best (logit, global index): larger key = larger logit, then lower index (NaN above
 // everything, -0 == +0), the order of argmax_better.
@@ -442,9 +412,10 @@ __device__ __forceinline__ void digits4(int X, int (&d)[4]) {
 // TP (tin non-null): the input is the residual sum h' = bf16(src + bf16(fp32(sum_r part_r) * s)) of the previous
 // o_proj / down_proj, from its np ranks' exact partials (added in rank order) and row scales; copy_to gets h'.
 struct TpIn {
-  const double *parts;  // rank r's partials at parts + r * k
-  const void *s;        // row scales of the stage that produced them
+  const char *parts;  // LL slots of rank r's partials at parts + 16 (r k + i)
+  const void *s;      // row scales of the stage that produced them
   int np, s_bf16;
+  unsigned seq;       // sequence number of the exchange site
 };
 template <bool TP>
 __device__ int stage_input(const uint16_t *src, int64_t k, const NormW *nw, float eps, int8_t *xd, float *red,
@@ -467,11 +438,35 @@ __device__ int stage_input(const uint16_t *src, int64_t k, const NormW *nw, floa
           const float4 sf = *(const float4 *)((const float *)tin->s + i);
           sc[0] = sf.x, sc[1] = sf.y, sc[2] = sf.z, sc[3] = sf.w;
         }
+        // partials of two ranks per pass: eight slot loads in flight before the first check
         double a[4] = {0.0, 0.0, 0.0, 0.0};
-        for (int r = 0; r < tin->np; ++r) {
-          const double2 *pp = (const double2 *)(tin->parts + (int64_t)r * k + i);
-          const double2 p0 = __ldcg(pp), p1 = __ldcg(pp + 1);
-          a[0] += p0.x, a[1] += p0.y, a[2] += p1.x, a[3] += p1.y;
+        const uint64_t t0 = globaltimer_ns();
+        for (int r = 0; r < tin->np; r += 2) {
+          const char *p0 = tin->parts + ((int64_t)r * k + i) * 16;
+          const char *p1 = p0 + k * 16;
+          const bool two = r + 1 < tin->np;
+          unsigned long long v[8];
+          bool ok = true;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) ok = ll_load(p0 + 16 * q, tin->seq, v[q]) && ok;
+          if (two) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) ok = ll_load(p1 + 16 * q, tin->seq, v[4 + q]) && ok;
+          }
+          if (!ok) {  // not all there yet: wait slot by slot
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[q] = ll_wait(p0 + 16 * q, tin->seq, t0);
+            if (two) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) v[4 + q] = ll_wait(p1 + 16 * q, tin->seq, t0);
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) a[q] += __longlong_as_double((long long)v[q]);
+          if (two) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) a[q] += __longlong_as_double((long long)v[4 + q]);
+          }
         }
         const float hs[4] = {bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y)};
 #pragma unroll
@@ -626,10 +621,11 @@ __device__ __forceinline__ void load_epi(const Params &P, int gs, EpiIn &in) {
 // after a CTA barrier, threads e < (CTA tiles) x 16 (x 8 for gate/up pairs) add a row's items in order and
 // apply the epilogue; their scales and residuals are fetched before the items stream. The lm_head epilogue
 // (bf16 logits, argmax) runs in the warp that owns the tile.
-// TP: o_proj / down_proj rows store their exact partial sum (fp64, before the scale) into every rank's region.
+// TP: o_proj / down_proj rows store their exact partial sum (fp64, before the scale) into every rank's region,
+// tagged with the exchange site's sequence number tseq.
 template <bool TP>
 __device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, int E, long long *part,
-                           const EpiIn &ein, Best &best) {
+                           const EpiIn &ein, Best &best, unsigned tseq) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const Stage sd = stage_desc(P, s);
   const bool lm = sd.kind == LMHEAD;
@@ -721,7 +717,9 @@ __device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, 
       if (TP) {
         const double y = __ll2double_rn(T0) * pow2_f64(E);  // exact: |T0| < 2^53
         const int64_t row = etile * kTileRows + er;
-        for (int q = 0; q < P.tp_world; ++q) xpart(P.xchg[q], sd.kind == OPROJ ? 0 : 1, P.tp_rank, P.H)[row] = y;
+        const unsigned long long bits = (unsigned long long)__double_as_longlong(y);
+        for (int q = 0; q < P.tp_world; ++q)
+          ll_store(xpart(P.xchg[q], sd.kind == OPROJ ? 0 : 1, P.tp_rank, P.H) + row * 16, bits, tseq);
       } else {
         P.h[etile * kTileRows + er] = f32_to_bf16_bits(eres + round_bf16(y0 * es0));
       }
@@ -913,7 +911,7 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
   Stream S;
   stream_start(P, S, ring + (size_t)warp * kRing * kSlot);
 
-  const unsigned long long nb = 5ull * (unsigned long long)P.L;  // grid barriers per step
+  const unsigned long long nb = (TP ? 3ull : 5ull) * (unsigned long long)P.L;  // grid barriers per step
   const unsigned epoch = *(volatile unsigned *)P.epoch;
   const unsigned long long base = (unsigned long long)epoch * nb;
   unsigned long long bidx = 0;
@@ -968,38 +966,32 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
           tin.s = after_o ? Ly.s_o : layers[l - 1].s_down;
           tin.np = P.tp_world;
           tin.s_bf16 = P.scale_bf16;
+          tin.seq = tp_seq(P, epoch, after_o ? 2 * l : 2 * (l - 1) + 1);
           tinp = &tin;
           copy_to = blockIdx.x != 0 || ph == 5 ? nullptr : after_o ? P.h2 : P.h;
         }
         const int E = stage_input<TP>(src, k, norm ? &nw : nullptr, P.eps, xd, red, copy_to, tinp);
         stamp(P, st);
         load_epi<TP>(P, ph == 5 ? 4 * P.L : 4 * l + (ph == 0 ? 0 : ph - 1), ein);  // consumed after the items
-        gemv_stage<TP>(P, ph == 5 ? 4 * P.L : 4 * l + (ph == 0 ? 0 : ph - 1), S, xd, E, part, ein, best);
+        gemv_stage<TP>(P, ph == 5 ? 4 * P.L : 4 * l + (ph == 0 ? 0 : ph - 1), S, xd, E, part, ein, best,
+                       (TP && (ph == 2 || ph == 4)) ? tp_seq(P, epoch, 2 * l + (ph == 4)) : 0u);
       }
     }
     if (st < 5 * P.L) {
-      // TP: the barriers after o_proj (xk 0) and down_proj (xk 1) also exchange the partial sums between ranks
-      const int xk = (TP && st >= 0) ? (st % 5 == 2 ? 0 : st % 5 == 4 ? 1 : -1) : -1;
-      const unsigned long long xseq = xk >= 0 ? tp_seq(P, epoch, 2 * (st / 5) + xk) : 0ull;
+      // TP: no barrier after o_proj and down_proj: the next stage waits for the sequence-tagged partial sums of
+      // every rank (which every CTA of every rank stored), and that wait orders everything the barrier did
+      const bool bar = !(TP && st >= 0 && (st % 5 == 2 || st % 5 == 4));
       // step-invariant inputs of stage st + 1, requested between arriving at the barrier that precedes it and
       // waiting there (after the arrival's fence, which would otherwise wait for them): norm weights, the
       // attention prologue's weights and RoPE row, KV ranges
-      if (st >= 0) {
-        if (xk >= 0)
-          tp_arrive(P, base, bidx + 1, xk, xseq);
-        else
-          grid_arrive(P, bidx + 1);
-      }
+      if (st >= 0 && bar) grid_arrive(P, bidx + 1);
       const int n = st + 1, ln = n / 5, pn = n == 5 * P.L ? 5 : n % 5;
       const egpt_qwen3_layer &Ln = layers[ln < P.L ? ln : P.L - 1];
       if (pn == 0 || pn == 3 || pn == 5)
         load_norm(pn == 5 ? P.final_norm : (const uint16_t *)(pn == 0 ? Ln.ln_in : Ln.ln_post), P.H, nw);
       if (pn == 1 && attn_cta) attn_preload<DPL, GRP>(P, Ln, blockIdx.x, nsplit, bps, pos, pre);
       if (pn == 0 && attn_cta) attn_prefetch_kv<DPL, GRP>(P, Ln, blockIdx.x, nsplit, bps, pos);
-      if (st >= 0) {
-        ++bidx;
-        ok = (xk >= 0 ? tp_wait(P, bidx, xk, xseq, &s_flag) : grid_wait(P, base, bidx, &s_flag)) && ok;
-      }
+      if (st >= 0 && bar) ok = grid_wait(P, base, ++bidx, &s_flag) && ok;
     }
   }
   if (P.trace && blockIdx.x == 0 && threadIdx.x == 0) P.trace[1 + 10 * P.L] = globaltimer_ns();
@@ -1046,16 +1038,16 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
         if (argmax_better(s_bv[w], s_bi[w], bv, bi)) bv = s_bv[w], bi = s_bi[w];
       int64_t next = bi;
       if (TP) {  // every rank's best key to every rank, then the same maximum everywhere
-        const unsigned long long seq = tp_seq(P, epoch, 2 * P.L);
+        const unsigned seq = tp_seq(P, epoch, 2 * P.L);
         const unsigned long long key = argmax_key(bv, (long long)bi + (long long)P.tp_rank * P.V);
-        for (int q = 0; q < P.tp_world; ++q) *(volatile unsigned long long *)xkey(P.xchg[q], P.tp_rank) = key;
-        tp_signal(P, 2, seq);
-        if (!tp_wait_flags(P, 2, seq)) ok = false;
+        for (int q = 0; q < P.tp_world; ++q) ll_store(xkey(P.xchg[q], P.tp_rank), key, seq);
+        const uint64_t t0 = globaltimer_ns();
         unsigned long long bk = 0ull;
         for (int r = 0; r < P.tp_world; ++r) {
-          const unsigned long long kr = *(volatile unsigned long long *)xkey(P.xchg[P.tp_rank], r);
+          const unsigned long long kr = ll_wait(xkey(P.xchg[P.tp_rank], r), seq, t0);
           bk = kr > bk ? kr : bk;
         }
+        if (device_error_set()) ok = false;
         next = (int64_t)(0xFFFFFFFFu - (unsigned)(bk & 0xFFFFFFFFull));
       }
       *P.token = ok ? next : 0;

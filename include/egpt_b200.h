@@ -245,12 +245,13 @@ EGPT_API int egpt_decode_step_persistent_check(const egpt_qwen3_plan *plan);
  * columns of o_proj, gate/up rows and down_proj columns [r I/g, (r+1) I/g), and lm_head rows
  * [r V/g, (r+1) V/g). egpt_decode_step_persistent with plan->tp_world = g runs the whole token in one kernel
  * per GPU: after o_proj and down_proj every CTA stores its rows' exact partial sums (fp64, unscaled) into
- * every rank's exchange region over NVLink (plain peer stores, no multicast), the CTA that completes the
- * local barrier raises this rank's flag on every peer, and the next stage on every rank adds the g
- * partials in rank order, scales, rounds and adds the residual as the one-GPU step does. The lm_head
- * stage exchanges one (logit, index) key per rank the same way; every rank writes the same token. All
- * flag waits are bounded (EGPT_ERR_TIMEOUT via egpt_device_error). The exchange region holds flags
- * [3][8] (u64 sequence numbers), keys [8] and fp64 partials [2][8][hidden].
+ * every rank's exchange region over NVLink (plain peer stores, no multicast) as 16-byte LL slots (two
+ * 8-byte words, each a 32-bit sequence number above 32 payload bits), and the next stage on every rank
+ * waits for the slots it reads, adds the g partials in rank order, scales, rounds and adds the residual as
+ * the one-GPU step does (no grid barrier after those two stages). The lm_head stage exchanges one
+ * (logit, index) key per rank the same way; every rank writes the same token. All waits are bounded
+ * (EGPT_ERR_TIMEOUT via egpt_device_error). The exchange region holds key slots [8] and partial-sum slots
+ * [2][8][hidden]; trace stamps (plan->trace) then cover the 3 * n_layers grid barriers that remain.
  * egpt_tp_xchg_alloc: cudaMalloc + zero fill of one region on the current device (free with
  * egpt_tp_xchg_free). egpt_ipc_handle writes the 64-byte CUDA IPC handle of such a region; egpt_ipc_open
  * maps a peer's handle into this process (peer access enabled), egpt_ipc_close unmaps it. */

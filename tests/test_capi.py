@@ -93,7 +93,7 @@ def test_plan_struct_layout_matches_the_header(tmp_path):
 
 def test_tp_exchange_size_and_guards():
     lib = L.load()
-    assert lib.egpt_tp_xchg_bytes(4096) == 4096 + 2 * 8 * 4096 * 8
+    assert lib.egpt_tp_xchg_bytes(4096) == 4096 + 2 * 8 * 4096 * 16
     assert lib.egpt_tp_xchg_bytes(0) == 0
     assert lib.egpt_tp_xchg_alloc(None, 64) == L.EGPT_ERR_ARG
     assert lib.egpt_ipc_handle(None, None) == L.EGPT_ERR_ARG
