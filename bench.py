@@ -21,10 +21,12 @@ Printed JSON line (rank 0):
                replayed alone as one PDL-chained graph (gemv_i8_kernel).
   gemv_chain   the GEMV launches of the launch-sequence path replayed alone (for comparison)
   cpu_baseline the reference's CPU path (oracle/torch_ref.py) on this host's cores, bounded sample
-With N > 1 (torchrun, one rank per GPU) the same model is split tensor-parallel over the N GPUs (efficientgpt_b200.tp:
-one persistent kernel per GPU and token, o_proj / down_proj partial sums exchanged over NVLink inside it; scaling
-"strong"); --replicas runs N independent one-GPU replicas instead (scaling "weak"). --workload qwen3_8b runs
-BASELINE config 5 (Qwen3-8B shape, 4096-token prompt fed through the step, 256 greedy tokens) at any N.
+With N > 1 (torchrun, one rank per GPU) the default workload is BASELINE config 5, the model the reference's north
+star shards: Qwen3-8B shape, 4096-token prompt fed through the step, 256 greedy tokens, tensor-parallel over the N
+GPUs (efficientgpt_b200.tp: one persistent kernel per GPU and token, o_proj / down_proj partial sums exchanged over
+NVLink inside it; scaling "strong"). --workload selects either model at any N (qwen3_8b on one GPU runs the
+launch sequence: its 12288-wide MLP does not fit the persistent kernel's shared memory); --replicas runs N
+independent one-GPU replicas of config 2 instead (scaling "weak").
 """
 import argparse
 import json
@@ -57,11 +59,14 @@ def parse():
     ap.add_argument('--launch-sequence', action='store_true', help='per-stage kernels instead of the persistent step')
     ap.add_argument('--no-gemv-chain', action='store_true', help='skip the GEMV-launches-alone comparison graph')
     ap.add_argument('--cpu-sample', type=int, default=3, help='timed CPU decode tokens (after one warm-up token)')
-    ap.add_argument('--workload', choices=['qwen3_1.7b', 'qwen3_8b'], default='qwen3_1.7b')
+    ap.add_argument('--workload', choices=['qwen3_1.7b', 'qwen3_8b'], default=None,
+                    help='default: qwen3_1.7b (config 2) on one GPU, qwen3_8b (config 5, tensor-parallel) on N > 1')
     ap.add_argument('--replicas', action='store_true', help='N > 1: independent replicas instead of tensor parallelism')
     a = ap.parse_args()
     if a.warmup < 3:
         ap.error('--warmup must be >= 3')
+    if a.workload is None:
+        a.workload = 'qwen3_8b' if a.gpus > 1 and not a.replicas else 'qwen3_1.7b'
     return a
 
 
@@ -243,7 +248,63 @@ def cpu_baseline(dec, n_tokens):
                       f'bf16((x.float() @ q.float().T) * s) per linear'}
 
 
+class _CpuWeights:
+    """The attributes oracle/torch_ref.TorchCpuQwen3 reads, from tp.full_weights of a quantised model."""
+
+    def __init__(self, model):
+        from efficientgpt_b200 import tp
+        c = model.config
+        shape = tp.Qwen3Shape.from_config(c)
+        full = tp.full_weights(model)
+        self.nq, self.nkv, self.d, self.eps = shape.nq, shape.nkv, shape.d, shape.eps
+        self.hidden, self.inter = shape.hidden, shape.inter
+        self.layers = full['layers']
+        self.embed, self.final_norm, self.w_lm, self.s_lm = full['embed'], full['final_norm'], full['w_lm'], full['s_lm']
+        self.rope_cos, self.rope_sin = tp.rope_tables(shape, 4096 + NEW_TOKENS, model.device, full['rotary'])
+
+
+def run_reference_8b(a, world, rank):
+    """The reference's CPU decode path on the config-5 model: a bounded sample of decode steps at context
+    4097.. with the 4096 prompt positions of the KV cache filled from a seeded draw (a CPU prefill of 4096 tokens
+    through an 8B model would take far longer than the run allows)."""
+    if rank != 0:
+        return
+    from oracle.torch_ref import TorchCpuQwen3
+    from efficientgpt_b200.configs import qwen3_8b_config, random_model
+    from efficientgpt_b200.int8_linear import quantize_model
+    model = random_model(qwen3_8b_config(), 'cuda', seed=0)
+    quantize_model(model, scale_dtype=torch.bfloat16)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    n = max(1, min(a.steps, a.cpu_sample))
+    cpu = TorchCpuQwen3(_CpuWeights(model), 4096 + n + 2)
+    del model
+    g = torch.Generator().manual_seed(0)
+    cpu.k[:, :, :, :4096].copy_(torch.randn(cpu.k[:, :, :, :4096].shape, generator=g).to(torch.bfloat16))
+    cpu.v[:, :, :, :4096].copy_(torch.randn(cpu.v[:, :, :, :4096].shape, generator=g).to(torch.bfloat16))
+    tok = cpu.step(11, 4096)
+    t0 = time.perf_counter()
+    for i in range(n):
+        tok = cpu.step(tok, 4097 + i)
+    v = n / (time.perf_counter() - t0)
+    cb = {'value': v, 'unit': 'tok/s', 'cores': threads, 'kind': 'port',
+          'sample': f'{n} decode tokens (after 1 warm-up token) of the Qwen3-8B-shape int8 model at context '
+                    f'4098..{4097 + n}, KV of the 4096 prompt positions from a seeded draw, torch CPU ops, '
+                    f'bf16((x.float() @ q.float().T) * s) per linear'}
+    line = {'impl': 'reference', 'metric': METRIC.replace('Qwen3-1.7B', 'Qwen3-8B').replace('1 B200', f'{world} B200'),
+            'value': v, 'unit': 'tok/s', 'n_gpus': world, 'steps': n, 'warmup': 1, 'ms_per_step': 1e3 / v,
+            'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'int8-weight/bf16',
+            'data': 'synthetic',
+            'config': {'workload': 'qwen3_8b int8 decode, BASELINE config 5 (CPU port of the reference path)',
+                       'prompt': 4096, 'new_tokens': NEW_TOKENS, 'scale_dtype': 'bf16'},
+            'cpu_baseline': cb, 'e2e': {'value': v, 'unit': 'tok/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(a, world, rank):
+    if a.workload == 'qwen3_8b':
+        run_reference_8b(a, world, rank)
+        return
     if rank != 0:
         return
     _, dec, _ = build('cuda', pdl=True)
