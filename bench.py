@@ -59,7 +59,7 @@ def parse():
     ap.add_argument('--launch-sequence', action='store_true', help='per-stage kernels instead of the persistent step')
     ap.add_argument('--no-gemv-chain', action='store_true', help='skip the GEMV-launches-alone comparison graph')
     ap.add_argument('--cpu-sample', type=int, default=3, help='timed CPU decode tokens (after one warm-up token)')
-    ap.add_argument('--workload', choices=['qwen3_1.7b', 'qwen3_8b'], default=None,
+    ap.add_argument('--workload', choices=['qwen3_1.7b', 'qwen3_8b', 'nanogpt'], default=None,
                     help='default: qwen3_1.7b (config 2) on one GPU, qwen3_8b (config 5, tensor-parallel) on N > 1')
     ap.add_argument('--replicas', action='store_true', help='N > 1: independent replicas instead of tensor parallelism')
     a = ap.parse_args()
@@ -212,13 +212,13 @@ def gemv_chain_graph(eng):
     return g, nbytes, 4 * len(eng.layers) + 1
 
 
-def time_replays(graph, k, reset=None):
+def time_replays(graph, k, reset=None, window=NEW_TOKENS):
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record(st)
     for i in range(k):
-        if reset is not None and i and i % NEW_TOKENS == 0:
+        if reset is not None and i and i % window == 0:
             reset()
         graph.replay()
     e1.record(st)
@@ -436,9 +436,87 @@ def run_tp(a, world, rank, local):
         dist.destroy_process_group()
 
 
+def run_nanogpt(a, world, rank):
+    """the nanoGPT decode step (one CUDA graph per token) over the contexts 65..128 window, and
+    the oracle's numpy restatement of the reference CPU path for a bounded sample. Rank 0 only."""
+    if rank != 0:
+        return
+    from efficientgpt_b200.int8_linear import quantize_model
+    from efficientgpt_b200.nanogpt import GPT, GPTConfig, GraphDecoder
+    cfg = GPTConfig(block_size=256, vocab_size=50304, n_layer=6, n_head=6, n_embd=384, bias=True)
+    model = GPT(cfg, seed=0).cuda().eval()
+    params = {n: p.detach().cpu().numpy().copy() for n, p in model.named_parameters()}
+    quantize_model(model)
+    prompt = torch.randint(0, cfg.vocab_size, (1, 64), generator=torch.Generator().manual_seed(0))
+    dec = GraphDecoder(model, prompt.cuda())
+    eng = dec.engine.engine
+    dec.engine.reset(prompt.cuda())
+
+    def reset():
+        eng.position.fill_(64)
+
+    time_replays(dec.graph, a.warmup)
+    reset()
+    ms = time_replays(dec.graph, a.steps, reset, window=64)
+    bytes_tok = sum(b.numel() * b.element_size() for b in model.buffers() if b.dtype in (torch.int8, torch.float32))
+    peaks, peak_src = measured_peaks()
+    hbm = float(peaks['hbm_gbs'])
+    gbs = bytes_tok / (ms / 1e3 / a.steps) / 1e9
+    e2e = None
+    if not a.no_e2e:
+        host = prompt.pin_memory()
+        vals = []
+        for _ in range(3):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            dev_prompt = host.to('cuda', non_blocking=True)
+            dec.engine.reset(dev_prompt)
+            torch.cuda.synchronize()
+            t1 = time.perf_counter()
+            for _ in range(63):
+                dec.graph.replay()
+            out = dec.engine.finish(64).cpu()
+            t2 = time.perf_counter()
+            vals.append(63 / (t2 - t1))
+        e2e = {'value': statistics.median(vals), 'unit': 'tok/s', 'h2d_bytes_per_step': 64 * 8 / 64,
+               'd2h_bytes_per_step': out.numel() * 8 / 64, 'ttft_ms': round((t1 - t0) * 1e3, 3),
+               'api': 'efficientgpt_b200.nanogpt.GraphDecoder (pinned host prompt, 64 tokens, history read back)'}
+    cb = None
+    if not a.no_cpu_baseline:
+        from oracle.nanogpt_ref import NanoGPTRef
+        params['lm_head.weight'] = params['transformer.wte.weight']
+        ref = NanoGPTRef(params, {'block_size': 256, 'n_layer': 6, 'n_head': 6, 'n_embd': 384}, semantics='cuda')
+        lg = ref.forward(prompt[0].tolist(), 0)
+        n = max(1, a.cpu_sample)
+        t0 = time.perf_counter()
+        pos = 64
+        for _ in range(n):
+            lg = ref.forward([int(lg.argmax())], pos)
+            pos += 1
+        cb = {'value': n / (time.perf_counter() - t0), 'unit': 'tok/s', 'cores': os.cpu_count(), 'kind': 'port',
+              'sample': f'{n} decode tokens at context 65..{64 + n}, numpy restatement of the reference CPU path '
+                        '(oracle/nanogpt_ref.py: x @ (q * s).T + b per linear, fp32)'}
+    line = {'metric': 'batch-1 decode tok/s, nanoGPT 6x384 int8 (BASELINE config 1), 1 B200', 'value': round(a.steps / (ms / 1e3), 2),
+            'unit': 'tok/s', 'n_gpus': 1, 'steps': a.steps, 'warmup': a.warmup, 'ms_per_step': round(ms / a.steps, 5),
+            'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'int8-weight/fp32',
+            'data': 'synthetic',
+            'config': {'workload': 'nanogpt 6x384 int8 decode, BASELINE config 1', 'prompt': 64, 'new_tokens': 64,
+                       'scale_dtype': 'fp32', 'init': 'N(0,0.02), seed 0', 'parallelism': 'single',
+                       'l2': 'no flush: the 30 MB of weights are L2-resident by design (latency-bound step)'},
+            'roofline': {'bound': 'hbm', 'kernel': 'nanoGPT step (graph of per-op kernels)', 'achieved': round(gbs, 1),
+                         'peak': hbm, 'unit': 'GB/s', 'frac': round(gbs / hbm, 4), 'traffic': None,
+                         'note': 'weights fit in L2: launch/latency-bound, the fraction is not a bandwidth limit',
+                         'peak_source': peak_src},
+            'e2e': e2e, 'cpu_baseline': cb, 'gpu_launches': a.steps * (1 + 8 * 6 + 2)}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse()
     world, rank, local = dist_setup()
+    if a.workload == 'nanogpt':
+        run_nanogpt(a, world, rank)
+        return
     if a.impl == 'reference':
         run_reference(a, world, rank)
         return

@@ -970,11 +970,16 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
           tinp = &tin;
           copy_to = blockIdx.x != 0 || ph == 5 ? nullptr : after_o ? P.h2 : P.h;
         }
-        const int E = stage_input<TP>(src, k, norm ? &nw : nullptr, P.eps, xd, red, copy_to, tinp);
-        stamp(P, st);
-        load_epi<TP>(P, ph == 5 ? 4 * P.L : 4 * l + (ph == 0 ? 0 : ph - 1), ein);  // consumed after the items
-        gemv_stage<TP>(P, ph == 5 ? 4 * P.L : 4 * l + (ph == 0 ? 0 : ph - 1), S, xd, E, part, ein, best,
-                       (TP && (ph == 2 || ph == 4)) ? tp_seq(P, epoch, 2 * l + (ph == 4)) : 0u);
+        const int gs = ph == 5 ? 4 * P.L : 4 * l + (ph == 0 ? 0 : ph - 1);
+        // TP shards leave some CTAs without tiles in a stage: those skip it (and its partial-sum reads); CTA 0
+        // always has tile 0 and stores the residual sum
+        if (!TP || ph == 5 || cta_tiles(stage_desc(P, gs)) > 0) {
+          const int E = stage_input<TP>(src, k, norm ? &nw : nullptr, P.eps, xd, red, copy_to, tinp);
+          stamp(P, st);
+          load_epi<TP>(P, gs, ein);  // consumed after the items
+          gemv_stage<TP>(P, gs, S, xd, E, part, ein, best,
+                         (TP && (ph == 2 || ph == 4)) ? tp_seq(P, epoch, 2 * l + (ph == 4)) : 0u);
+        }
       }
     }
     if (st < 5 * P.L) {

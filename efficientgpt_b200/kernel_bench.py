@@ -1,7 +1,7 @@
 """Per-kernel sweeps of BASELINE configs 3 (int8 GEMV) and 4 (GQA decode attention) against the HBM roofline, and
 the config-1 nanoGPT decode rate.
 
-    python -m efficientgpt_b200.kernel_bench [--reps 50] [--skip-nanogpt]
+    python -m efficientgpt_b200.kernel_bench [--reps 50] [--skip-nanogpt] [--only lm_head]
 
 Each case replays a CUDA graph of `reps` launches (device time from CUDA events around the replays, so host launch
 cost is not counted) over enough weight / cache copies that one pass of the graph exceeds L2 (126 MB): every
@@ -9,8 +9,8 @@ launch reads from HBM. Algorithmic bytes: GEMV N*K + 2N (bf16 scales) + 2K (x) +
 4096*L + 8192 (K and V of 8 kv heads x d 128 in bf16, q and out). Peak: MEASURED_PEAKS.json hbm_gbs when present.
 nanoGPT (config 1: 6 layers, 384 dims, vocab 50304, block 256, int8 weights with fp32 scales, fp32 activations,
 N(0, 0.02) init, 64-token prompt, 64 greedy tokens): graph replays of the native decode step timed with CUDA events
-(its 30 MB of weights fit in L2, so the step is launch- and latency-bound, not HBM-bound), next to the oracle's
-numpy restatement of the reference CPU path for 3 tokens on this host. Prints one JSON line per case.
+(its 30 MB of weights fit in L2, so the step is launch- and latency-bound, not HBM-bound); the CPU baseline of
+config 1 is timed by `bench.py --workload nanogpt`. Prints one JSON line per case.
 """
 import argparse
 import json
@@ -52,10 +52,12 @@ def time_graph(fn, reps):
     return e0.elapsed_time(e1) / (5 * reps) * 1e3  # us per launch
 
 
-def gemv_cases(reps, peak, src):
+def gemv_cases(reps, peak, src, only=''):
     from . import ops
     for n, k, what in ((4096, 2048, 'qkv'), (2048, 2048, 'o'), (12288, 2048, 'gate_up'), (2048, 6144, 'down'),
                        (151936, 2048, 'lm_head')):
+        if only not in f'config 3 {what}':
+            continue
         g = torch.Generator(device='cuda').manual_seed(0)
         copies = max(1, math.ceil(2 * L2_BYTES / (n * k)))
         ws = [torch.randint(-127, 128, (n, k), dtype=torch.int8, device='cuda', generator=g) for _ in range(copies)]
@@ -71,10 +73,12 @@ def gemv_cases(reps, peak, src):
         del ws
 
 
-def attention_cases(reps, peak, src):
+def attention_cases(reps, peak, src, only=''):
     from . import ops
     nq, nkv, d = 16, 8, 128
     for length in (512, 2048, 8192, 32768):
+        if only not in f'config 4 L={length}':
+            continue
         g = torch.Generator(device='cuda').manual_seed(length)
         per = 2 * nkv * length * d * 2
         copies = max(1, math.ceil(2 * L2_BYTES / per))
@@ -96,10 +100,9 @@ def attention_cases(reps, peak, src):
         del ks, vs
 
 
-def nanogpt_case():
-    import os
-    import sys
-    import time
+def nanogpt_case(n_tokens=63):
+    """Config-1 decode rate: graph replays of the native nanoGPT decode step (64-token prompt, contexts 65..127).
+    Returns (line, model parameters as numpy arrays, prompt) so a caller can time a CPU baseline on the same model."""
     from .int8_linear import quantize_model
     from .nanogpt import GPT, GPTConfig, GraphDecoder
     cfg = GPTConfig(block_size=256, vocab_size=50304, n_layer=6, n_head=6, n_embd=384, bias=True)
@@ -116,43 +119,30 @@ def nanogpt_case():
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(63):
+    for _ in range(n_tokens):
         dec.graph.replay()
     e1.record()
     e1.synchronize()
-    ms = e0.elapsed_time(e1) / 63
+    ms = e0.elapsed_time(e1) / n_tokens
     line = {'kernel': 'nanoGPT decode step (one CUDA graph: 48 library kernels + history write)',
             'case': 'config 1 (6x384, vocab 50304), context 65..127', 'tok_s': round(1e3 / ms, 1),
             'ms_per_token': round(ms, 4), 'bound': 'latency (weights 30 MB, L2-resident)'}
-    root = Path(__file__).resolve().parent.parent
-    if (root / 'oracle').exists():
-        sys.path.insert(0, str(root))
-        from oracle.nanogpt_ref import NanoGPTRef
-        params['lm_head.weight'] = params['transformer.wte.weight']
-        ref = NanoGPTRef(params, {'block_size': 256, 'n_layer': 6, 'n_head': 6, 'n_embd': 384}, semantics='cuda')
-        lg = ref.forward(prompt[0].tolist(), 0)
-        t0 = time.perf_counter()
-        pos = 64
-        for _ in range(3):
-            lg = ref.forward([int(lg.argmax())], pos)
-            pos += 1
-        line['cpu_baseline'] = {'tok_s': round(3 / (time.perf_counter() - t0), 2), 'kind': 'port', 'cores': os.cpu_count(),
-                                'sample': '3 decode tokens at context 65..67, numpy restatement of the reference CPU path'}
-    return line
+    return line, params, prompt
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--reps', type=int, default=50)
     ap.add_argument('--skip-nanogpt', action='store_true')
+    ap.add_argument('--only', default='', help='run only the cases whose name contains this text (e.g. lm_head)')
     a = ap.parse_args()
     peak, src = peak_gbs()
-    for line in gemv_cases(a.reps, peak, src):
+    for line in gemv_cases(a.reps, peak, src, a.only):
         print(json.dumps(line), flush=True)
-    for line in attention_cases(a.reps, peak, src):
+    for line in attention_cases(a.reps, peak, src, a.only):
         print(json.dumps(line), flush=True)
     if not a.skip_nanogpt:
-        print(json.dumps(nanogpt_case()), flush=True)
+        print(json.dumps(nanogpt_case()[0]), flush=True)
 
 
 if __name__ == '__main__':
