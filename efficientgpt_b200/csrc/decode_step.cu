@@ -248,13 +248,13 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 // Grid barrier: arrivals accumulate on a monotonic counter; barrier idx (1-based) of the step with epoch
 // base completes when the counter reaches (base + idx) * G. Bounded: records EGPT_ERR_TIMEOUT, returns false.
 // Split in two so that work can go between arriving and waiting: grid_arrive publishes this CTA's writes and
-// counts it in (thread 0: fence, then one atomic add); grid_wait spins (thread 0) until every CTA arrived.
+// counts it in (thread 0: one release reduction); grid_wait spins (thread 0) until every CTA arrived.
 __device__ __forceinline__ void grid_arrive(const Params &P, unsigned long long idx) {
   csync();
   if (threadIdx.x == 0) {
     if (P.trace && blockIdx.x == 0) P.trace[2 * idx - 1] = globaltimer_ns();
-    __threadfence();
-    atomicAdd(P.bar, 1ull);
+    // release: the CTA's writes (ordered before by the CTA barrier) are visible before the count
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(P.bar) : "memory");
   }
 }
 __device__ bool grid_wait(const Params &P, unsigned long long base, unsigned long long idx, int *s_ok) {
@@ -531,6 +531,46 @@ __device__ int stage_input(const uint16_t *src, int64_t k, const NormW *nw, floa
 #pragma unroll
       for (int p = 0; p < 4; ++p) *(uint32_t *)(xd + (int64_t)p * xs + i) = word[p];
     }
+  }
+  csync();
+  return E;
+}
+
+// Inputs wider than kMaxPerThread * kCT values (no norm, no residual: the down_proj input of a 12288-wide MLP):
+// the same fixed point as stage_input in two passes over the vector, one for the bound and one (L2 hits) for the
+// digit planes, so no thread holds more than four values.
+__device__ int stage_input_wide(const uint16_t *src, int64_t k, int8_t *xd, float *red) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  float mx = 0.f;
+  for (int64_t i = 4 * (int64_t)t; i < k; i += 4 * kCT) {
+    const uint2 u = __ldcg((const uint2 *)(src + i));
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(bf16_lo(u.x)), fabsf(bf16_hi(u.x))), fmaxf(fabsf(bf16_lo(u.y)), fabsf(bf16_hi(u.y)))));
+  }
+  mx = warp_max(mx);
+  if (lane == 0) red[kNC + warp] = mx;
+  csync();
+  float bound = red[kNC];
+#pragma unroll
+  for (int w = 1; w < kNC; ++w) bound = fmaxf(bound, red[kNC + w]);
+  const int ex = bound > 0.f ? ((__float_as_int(bound) >> 23) & 0xFF) - 127 : 0;  // floor(log2 bound)
+  const int E = ex - 29;
+  const int xs = x_stride(k);
+  const int64_t kpad = xs - kXPad;
+  for (int64_t i = 4 * (int64_t)t; i < kpad; i += 4 * kCT) {
+    uint32_t word[4] = {0u, 0u, 0u, 0u};
+    if (i < k) {
+      const uint2 u = __ldcg((const uint2 *)(src + i));
+      const float v[4] = {bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y)};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        int d[4];
+        digits4(__float2int_rn(mul_pow2(v[q], -E)), d);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) word[p] |= ((uint32_t)d[p] & 0xFFu) << (8 * q);
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p) *(uint32_t *)(xd + (int64_t)p * xs + i) = word[p];
   }
   csync();
   return E;
@@ -887,7 +927,7 @@ __device__ void attention_task(const Params &P, const egpt_qwen3_layer &Ly, int 
 }
 
 // ------------------------------------------------------------------------------------------------ kernel
-template <int DPL, int GRP, bool TP>
+template <int DPL, int GRP, bool TP, bool WIDE>
 __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
   extern __shared__ __align__(128) uint8_t smem[];
   float *red = (float *)smem;                    // 64 floats
@@ -974,7 +1014,9 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
         // TP shards leave some CTAs without tiles in a stage: those skip it (and its partial-sum reads); CTA 0
         // always has tile 0 and stores the residual sum
         if (!TP || ph == 5 || cta_tiles(stage_desc(P, gs)) > 0) {
-          const int E = stage_input<TP>(src, k, norm ? &nw : nullptr, P.eps, xd, red, copy_to, tinp);
+          const int E = (WIDE && k > kMaxPerThread * kCT)
+                            ? stage_input_wide(src, k, xd, red)
+                            : stage_input<TP>(src, k, norm ? &nw : nullptr, P.eps, xd, red, copy_to, tinp);
           stamp(P, st);
           load_epi<TP>(P, gs, ein);  // consumed after the items
           gemv_stage<TP>(P, gs, S, xd, E, part, ein, best,
@@ -1076,9 +1118,9 @@ static size_t part_bytes(const egpt_qwen3_plan *Pl, int G) {
   return (size_t)items * kTileRows * 8;
 }
 
-template <int DPL, int GRP, bool TP>
+template <int DPL, int GRP, bool TP, bool WIDE = false>
 static cudaError_t launch(const Params &P, size_t smem, cudaStream_t st) {
-  auto kern = decode_step_kernel<DPL, GRP, TP>;
+  auto kern = decode_step_kernel<DPL, GRP, TP, WIDE>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -1117,10 +1159,15 @@ static int persistent_validate(const egpt_qwen3_plan *Pl, size_t *smem_out) {
   const int grp = NQ / NKV;
   const bool shape_ok = (D == 128 && (grp == 2 || grp == 4)) || (D == 32 && grp == 2);
   if (!shape_ok) return set_error(EGPT_ERR_SHAPE, "decode_step_persistent: head_dim %d / group %d not built", D, grp);
-  if (H % 16 || I % 16 || ((int64_t)NQ * D) % 16 || Pl->vocab % 16 ||
-      std::max<int64_t>({H, I, (int64_t)NQ * D}) > (int64_t)ps::kMaxPerThread * ps::kCT)
+  // inputs staged in registers: hidden and nq*d up to kMaxPerThread * kCT; the intermediate (down_proj input,
+  // no norm) up to twice that on the one-GPU head_dim-128 / group-4 instantiation (two-pass staging)
+  const int64_t reg_max = (int64_t)ps::kMaxPerThread * ps::kCT;
+  const bool wide_ok = D == 128 && grp == 4 && Pl->tp_world <= 1;
+  if (H % 16 || I % 16 || ((int64_t)NQ * D) % 16 || Pl->vocab % 16 || std::max<int64_t>(H, (int64_t)NQ * D) > reg_max ||
+      I > (wide_ok ? 2 * reg_max : reg_max))
     return set_error(EGPT_ERR_SHAPE, "decode_step_persistent: hidden, intermediate, nq*d and vocab must be multiples "
-                     "of 16 and at most %d", ps::kMaxPerThread * ps::kCT);
+                     "of 16, hidden and nq*d at most %lld, intermediate at most %lld", (long long)reg_max,
+                     (long long)(wide_ok ? 2 * reg_max : reg_max));
   const int G = num_sms();
   if (G > kArgmaxMaxCtas) return set_error(EGPT_ERR_SHAPE, "decode_step_persistent: too many SMs");
   if (Pl->tp_world > 1) {
@@ -1218,6 +1265,8 @@ extern "C" int egpt_decode_step_persistent(const egpt_qwen3_plan *Pl, void *stre
   const cudaStream_t cs = (cudaStream_t)stream;
   if (D == 128 && grp == 2)
     e = tp ? ps::launch<4, 2, true>(P, smem, cs) : ps::launch<4, 2, false>(P, smem, cs);
+  else if (D == 128 && !tp && I > ps::kMaxPerThread * ps::kCT)
+    e = ps::launch<4, 4, false, true>(P, smem, cs);  // the 12288-wide MLP of the 8B shape on one GPU
   else if (D == 128)
     e = tp ? ps::launch<4, 4, true>(P, smem, cs) : ps::launch<4, 4, false>(P, smem, cs);
   else

@@ -232,8 +232,9 @@ EGPT_API int egpt_decode_step(const egpt_qwen3_plan *plan, void *stream);
  * sums, and each row is rounded once (then scaled and rounded at the reference's bf16 points), so results
  * can differ from egpt_decode_step's fp32 sums in the last bits. Needs plan->layers_dev and plan->sync_ws;
  * after a device error (egpt_device_error) sync_ws and the workspaces must be zero-filled again. Built for
- * head_dim 128 with 2 or 4 q heads per kv head and head_dim 32 with 2; hidden, intermediate and nq*d up to
- * 6144 and multiples of 16, vocab a multiple of 16; other shapes return EGPT_ERR_SHAPE.
+ * head_dim 128 with 2 or 4 q heads per kv head and head_dim 32 with 2; hidden and nq*d up to 6144, the
+ * intermediate size up to 6144 (12288 with head_dim 128, 4 q heads per kv head and one GPU: the 8B shape), all
+ * multiples of 16, vocab a multiple of 16; other shapes return EGPT_ERR_SHAPE.
  * egpt_decode_step_persistent_check runs the same host-side checks without launching anything. */
 EGPT_API size_t egpt_step_sync_ws_bytes(void);
 EGPT_API int egpt_decode_step_persistent(const egpt_qwen3_plan *plan, void *stream);

@@ -143,6 +143,41 @@ def test_persistent_step_matches_launch_sequence(cuda, scale_dtype):
     assert _lib.device_error() == 0
 
 
+def test_persistent_wide_mlp_matches_launch_sequence(cuda):
+    """An intermediate wider than the persistent kernel's register staging (the 8B shape's 12288; here 8192 with
+    head_dim 128 and 4 q heads per kv head) takes the two-pass staging of the down_proj input; teacher-forced
+    against the launch sequence under the same rules as above."""
+    from transformers import Qwen3Config
+    from efficientgpt_b200 import _lib
+    from efficientgpt_b200.engine import Qwen3Engine
+    cfg = Qwen3Config(vocab_size=1024, hidden_size=256, intermediate_size=8192, num_hidden_layers=2,
+                      num_attention_heads=8, num_key_value_heads=2, head_dim=128, max_position_embeddings=256,
+                      tie_word_embeddings=True, initializer_range=0.05)
+    model = gi.build_model(cfg, seed=5).cuda()
+    _quantize(model, torch.bfloat16, 'cuda')
+    a = Qwen3Engine(model, 160, keep_logits=True, persistent=False)
+    b = Qwen3Engine(model, 160, keep_logits=True, persistent=True)
+    assert b.persistent
+    x = gi.tiny_prompts()[5].cuda()
+    a.prefill(x)
+    b.prefill(x)
+    same = 0
+    for i in range(120):
+        b.token.copy_(a.token)
+        a.step()
+        b.step()
+        la, lb = from_torch(a.logits), from_torch(b.logits)
+        ok, detail = parity.logits_close(lb, la)
+        assert ok, (i, detail)
+        if int(a.token) != int(b.token):
+            top = np.sort(la)[-2:]
+            assert top[1] - top[0] <= parity.near_tie_threshold(top[1]), i
+        else:
+            same += 1
+    assert same >= 115
+    assert _lib.device_error() == 0
+
+
 def test_logits_past_one_softmax_block_match_oracle(cuda):
     """Teacher-forced decode from position 120 to 140 (crossing the reference kernel's first 128-key softmax
     block) vs the oracle's block-walk rounding, under the long-sequence logit rule (parity.logits_close: 99%
