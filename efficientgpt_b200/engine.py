@@ -25,6 +25,9 @@ from . import ops
 from .int8_linear import Int8Linear
 
 
+PREFILL_GEMM_MIN = 256  # prompts longer than this take the GEMM prefill
+
+
 def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
@@ -172,11 +175,21 @@ class Qwen3Engine:
     @torch.no_grad()
     def prefill(self, input_ids):
         """Run the prompt (int64 [p] or [1, p] on the device) from position 0; leaves token = first generated id
-        and position = p. Returns the token tensor (device)."""
+        and position = p. Returns the token tensor (device). Prompts longer than PREFILL_GEMM_MIN tokens fill the
+        KV cache with the GEMM prefill (efficientgpt_b200.prefill) and run their last token through the decode
+        step; shorter ones run the per-stage kernels on 16-row blocks."""
         ids = input_ids.reshape(-1).to(device=self.device, dtype=torch.int64).contiguous()
         p = ids.numel()
         if p < 1 or p > self.cap:
             raise ValueError('prompt length must be in [1, max_cache_len]')
+        if p > PREFILL_GEMM_MIN:
+            from .prefill import fill_kv
+            fill_kv(ids[:-1], self.layers, self.embed, self.kv, self.rope_cos, self.rope_sin, self.nq, self.nkv,
+                    self.d, self.eps)
+            self.position.fill_(p - 1)
+            self.token.copy_(ids[-1:])
+            self.step()
+            return self.token
         self.position.zero_()
         h = ops.embed(ids, self.embed)
         ws = ops.attn_ws(p, self.nq, self.nkv, self.d, self.attn_max_split, self.device)

@@ -65,10 +65,15 @@ def gemv_cases(reps, peak, src, only=''):
         x = torch.randn(1, k, device='cuda', generator=g).to(torch.bfloat16)
         out = torch.empty(1, n, dtype=torch.bfloat16, device='cuda')
         us = time_graph(lambda i: ops.gemv_i8(x, ws[i % copies], s, out=out), reps)
+        # chained with programmatic dependent launch, as the launch-sequence decode path runs it: a launch streams
+        # its first weights while the previous one drains
+        us_pdl = time_graph(lambda i: ops.gemv_i8(x, ws[i % copies], s, out=out, pdl=True), reps)
         nbytes = n * k + 2 * n + 2 * k + 2 * n
         gbs = nbytes / (us * 1e-6) / 1e9
+        gbs_pdl = nbytes / (us_pdl * 1e-6) / 1e9
         yield {'kernel': 'gemv_i8_kernel', 'case': f'config 3 {what} N={n} K={k}', 'us': round(us, 3),
                'bytes': nbytes, 'achieved_gbs': round(gbs, 1), 'peak_gbs': peak, 'frac': round(gbs / peak, 4),
+               'us_pdl_chain': round(us_pdl, 3), 'frac_pdl_chain': round(gbs_pdl / peak, 4),
                'peak_source': src, 'l2': f'{copies} weight copies rotated'}
         del ws
 

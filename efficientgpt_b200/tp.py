@@ -261,14 +261,29 @@ class TPQwen3Engine:
             L.check(self.lib.egpt_decode_step(ctypes.byref(self.plan), stream), 'decode_step')
 
     @torch.no_grad()
-    def feed(self, ids):
-        """Run the prompt token by token from position 0 through the decode step (KV appended per token); leaves
-        token = the first generated id and position = len(ids)."""
+    def feed(self, ids, gemm_min=64):
+        """Run the prompt from position 0; leaves token = the first generated id and position = len(ids). Prompts
+        longer than gemm_min tokens fill the KV cache of all but the last token with the GEMM prefill
+        (efficientgpt_b200.prefill; o_proj / down_proj partial products summed over the group) and run the last
+        token through the decode step; shorter ones go token by token through the decode step."""
         ids = ids.reshape(-1).to(device=self.device, dtype=torch.int64)
-        if ids.numel() < 1 or ids.numel() > self.cap:
+        p = ids.numel()
+        if p < 1 or p > self.cap:
             raise ValueError('prompt length must be in [1, max_cache_len]')
         self.position.zero_()
-        for i in range(ids.numel()):
+        if p > gemm_min:
+            from .prefill import fill_kv
+            allreduce = None
+            if self.world > 1:
+                import torch.distributed as dist
+                allreduce = lambda y: dist.all_reduce(y, group=self.group)
+            fill_kv(ids[:-1].contiguous(), self.w['layers'], self.w['embed'], self.kv, self.rope_cos, self.rope_sin,
+                    self.nq, self.nkv, self.shape.d, self.shape.eps, allreduce)
+            self.position.fill_(p - 1)
+            self.token.copy_(ids[-1:])
+            self.step()
+            return self.token
+        for i in range(p):
             self.token.copy_(ids[i:i + 1])
             self.step()
         return self.token
