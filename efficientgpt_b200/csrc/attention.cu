@@ -458,8 +458,13 @@ struct AttnOut {
   void *out;          // this row's output; head h at element offset h * D
   float *part;        // this row's split partials: head h, split s at (h * max_split + s) * (D + 2)
   unsigned *cnt;      // combine counter of this (row, kv head)
+  unsigned long long *done;  // nullable: +1 (release) once this kv head's output is written
   int g, split, nsplit, max_split, busy;
 };
+
+__device__ __forceinline__ void red_release_add_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 
 template <bool BF16>
 __device__ __forceinline__ void store_out(void *out, int64_t i, float v) {
@@ -499,7 +504,13 @@ __device__ void attn_finish(AttnScratch<DPL, GRP> &S, const AttnOut &o) {
       }
     }
   }
-  if (single) return;
+  if (single) {
+    if (o.done) {
+      nt_sync<NT>();
+      if (threadIdx.x == 0) red_release_add_u64(o.done, 1ull);
+    }
+    return;
+  }
   __threadfence();
   nt_sync<NT>();
   if (threadIdx.x == 0) {
@@ -525,6 +536,10 @@ __device__ void attn_finish(AttnScratch<DPL, GRP> &S, const AttnOut &o) {
       a += __ldcg(base + s * (D + 2) + 2 + dd) * f;
     }
     store_out<BF16>(o.out, (int64_t)h * D + dd, a / lsum);
+  }
+  if (o.done) {
+    nt_sync<NT>();
+    if (threadIdx.x == 0) red_release_add_u64(o.done, 1ull);
   }
 }
 
@@ -593,6 +608,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
   o.out = (char *)p.out + row * p.ldo * esz;
   o.part = p.ws_f ? p.ws_f + row * p.nq * p.max_split * (D + 2) : nullptr;
   o.cnt = p.ws_cnt ? p.ws_cnt + row * p.nkv + g : nullptr;
+  o.done = nullptr;
   o.g = g;
   o.split = split;
   o.nsplit = nsplit;

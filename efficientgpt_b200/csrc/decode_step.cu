@@ -74,6 +74,8 @@ struct Params {
   unsigned *lm_cnt;
   unsigned long long *bar;
   unsigned *epoch;
+  unsigned long long *qcnt;  // one-GPU step: q|k|v tiles written, per kv group (monotonic over steps and layers)
+  unsigned long long *acnt;  // one-GPU step: kv heads whose attention output is written (monotonic)
   int part_bytes;            // shared memory for the layer stages' per-item row sums
   unsigned long long *trace;  // nullable: per-barrier %globaltimer stamps of CTA 0
   // tensor parallelism (TP instantiation only)
@@ -337,6 +339,32 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, long long idx)
 }
 // 2^e as a double (e within the normal range, which every staged-input exponent is).
 __device__ __forceinline__ double pow2_f64(int e) { return __longlong_as_double((long long)(e + 1023) << 52); }
+
+// Dependency wait (one-GPU step): thread 0 spins (bounded) until the monotonic counter c reaches target, then
+// the CTA proceeds; replaces a grid barrier where only some producers matter (q|k|v tiles of one kv group before
+// its attention, the kv heads' outputs before o_proj).
+__device__ bool dep_wait(const unsigned long long *c, unsigned long long target, int *s_ok) {
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    for (int it = 0; ld_acquire_u64(c) < target; ++it) {
+      if ((it & 63) == 63) {
+        if (device_error_set()) {
+          ok = 0;
+          break;
+        }
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          set_device_error(EGPT_ERR_TIMEOUT);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    *s_ok = ok;
+  }
+  csync();
+  return *s_ok != 0;
+}
 
 // Trace: stamp k (CTA 0, thread 0) of the second trace region: the moment stage k's input is ready (GEMV
 // stages: staged and normalised; attention: this CTA's scores done).
@@ -923,6 +951,7 @@ __device__ void attention_task(const Params &P, const egpt_qwen3_layer &Ly, int 
   o.nsplit = nsplit;
   o.max_split = P.max_split;
   o.busy = min(kAttnWarps, ntiles);
+  o.done = P.acnt;  // read by the one-GPU step's o_proj; the tensor-parallel step keeps a grid barrier instead
   attn_finish<DPL, GRP, true, kCT>(S, o);
 }
 
@@ -951,7 +980,7 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
   Stream S;
   stream_start(P, S, ring + (size_t)warp * kRing * kSlot);
 
-  const unsigned long long nb = (TP ? 3ull : 5ull) * (unsigned long long)P.L;  // grid barriers per step
+  const unsigned long long nb = 3ull * (unsigned long long)P.L;  // grid barriers per step
   const unsigned epoch = *(volatile unsigned *)P.epoch;
   const unsigned long long base = (unsigned long long)epoch * nb;
   unsigned long long bidx = 0;
@@ -985,9 +1014,17 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
       const int l = st / 5, ph = st == 5 * P.L ? 5 : st % 5;
       const egpt_qwen3_layer &Ly = layers[l < P.L ? l : P.L - 1];
       if (ph == 1) {
-        // ---- attention (q/k norm + RoPE + KV append + split-K softmax . V + combine)
+        // ---- attention (q/k norm + RoPE + KV append + split-K softmax . V + combine); one GPU: starts once the
+        //      q|k|v tiles of its kv group are written (no grid barrier after q|k|v)
+        if (!TP && attn_cta)
+          ok = dep_wait(P.qcnt + blockIdx.x / nsplit,
+                        ((unsigned long long)epoch * P.L + l + 1) * (unsigned long long)((GRP + 2) * P.D / kTileRows),
+                        &s_flag) && ok;
         if (ok && attn_cta) attention_task<DPL, GRP>(P, Ly, blockIdx.x, nsplit, bps, pos, u, pre, st);
       } else {
+        // one GPU: o_proj starts once every kv head's attention output is written (no grid barrier after attention)
+        if (!TP && ph == 2)
+          ok = dep_wait(P.acnt, ((unsigned long long)epoch * P.L + l + 1) * (unsigned long long)P.NKV, &s_flag) && ok;
         // ---- GEMV stages: q|k|v = Wqkv . RMSNorm(h) (layer 0: h = embed[token], CTA 0 stores it);
         //      h += Wo . attn;  act = silu(Wg . RMSNorm(h)) * (Wu . RMSNorm(h));  h += Wdown . act;
         //      token = argmax(lm_head . RMSNorm(h))
@@ -1021,13 +1058,25 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
           load_epi<TP>(P, gs, ein);  // consumed after the items
           gemv_stage<TP>(P, gs, S, xd, E, part, ein, best,
                          (TP && (ph == 2 || ph == 4)) ? tp_seq(P, epoch, 2 * l + (ph == 4)) : 0u);
+          if (!TP && ph == 0) {  // count this CTA's q|k|v tiles in, per kv group, once their rows are written
+            csync();
+            if (threadIdx.x == 0) {
+              const int ntl = (int)cta_tiles(stage_desc(P, gs));
+              for (int tl = 0; tl < ntl; ++tl) {
+                const int hd = (int)((((int64_t)blockIdx.x + (int64_t)gridDim.x * tl) * kTileRows) / P.D);
+                const int g = hd < P.NQ ? hd / GRP : hd < P.NQ + P.NKV ? hd - P.NQ : hd - P.NQ - P.NKV;
+                red_release_add_u64(P.qcnt + g, 1ull);
+              }
+            }
+          }
         }
       }
     }
     if (st < 5 * P.L) {
       // TP: no barrier after o_proj and down_proj: the next stage waits for the sequence-tagged partial sums of
       // every rank (which every CTA of every rank stored), and that wait orders everything the barrier did
-      const bool bar = !(TP && st >= 0 && (st % 5 == 2 || st % 5 == 4));
+      // one GPU: no barrier after q|k|v and attention either: dependency counters order those stages
+      const bool bar = TP ? !(st >= 0 && (st % 5 == 2 || st % 5 == 4)) : !(st >= 0 && (st % 5 == 0 || st % 5 == 1));
       // step-invariant inputs of stage st + 1, requested between arriving at the barrier that precedes it and
       // waiting there (after the arrival's fence, which would otherwise wait for them): norm weights, the
       // attention prologue's weights and RoPE row, KV ranges
@@ -1144,7 +1193,10 @@ static cudaError_t launch(const Params &P, size_t smem, cudaStream_t st) {
 
 using namespace egpt;
 
-extern "C" size_t egpt_step_sync_ws_bytes(void) { return 64; }
+// Step synchronisation words: u64 barrier counter at 0, u32 epoch at 8, u64 attention-done counter at 64, u64
+// q|k|v-tile counters per kv group from 72.
+constexpr int kMaxSyncGroups = 240;
+extern "C" size_t egpt_step_sync_ws_bytes(void) { return 72 + 8 * kMaxSyncGroups; }
 
 // Host-side checks of a plan for the persistent kernel; on success *smem is its dynamic shared memory.
 static int persistent_validate(const egpt_qwen3_plan *Pl, size_t *smem_out) {
@@ -1157,6 +1209,7 @@ static int persistent_validate(const egpt_qwen3_plan *Pl, size_t *smem_out) {
   if (Pl->n_layers < 1 || H < 16 || I < 16 || NQ < 1 || NKV < 1 || NQ % NKV || Pl->vocab < 2 || Pl->cap < 1)
     return set_error(EGPT_ERR_SHAPE, "decode_step_persistent: bad model sizes");
   const int grp = NQ / NKV;
+  if (NKV > kMaxSyncGroups) return set_error(EGPT_ERR_SHAPE, "decode_step_persistent: more than %d kv heads", kMaxSyncGroups);
   const bool shape_ok = (D == 128 && (grp == 2 || grp == 4)) || (D == 32 && grp == 2);
   if (!shape_ok) return set_error(EGPT_ERR_SHAPE, "decode_step_persistent: head_dim %d / group %d not built", D, grp);
   // inputs staged in registers: hidden and nq*d up to kMaxPerThread * kCT; the intermediate (down_proj input,
@@ -1251,6 +1304,8 @@ extern "C" int egpt_decode_step_persistent(const egpt_qwen3_plan *Pl, void *stre
   P.lm_cnt = (unsigned *)((char *)Pl->lm_ws + kArgmaxMaxCtas * 8);
   P.bar = (unsigned long long *)Pl->sync_ws;
   P.epoch = (unsigned *)((char *)Pl->sync_ws + 8);
+  P.acnt = (unsigned long long *)((char *)Pl->sync_ws + 64);
+  P.qcnt = (unsigned long long *)((char *)Pl->sync_ws + 72);
   P.part_bytes = (int)ps::part_bytes(Pl, num_sms());
   P.trace = (unsigned long long *)Pl->trace;
   P.v_embed = Pl->vocab;
