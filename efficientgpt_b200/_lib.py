@@ -19,6 +19,7 @@ EPI_NONE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_GELU = 0, 1, 2, 3
 FLAG_DOUBLE_ROUND, FLAG_RMSNORM, FLAG_PDL, FLAG_EMBED, FLAG_ADVANCE, FLAG_APPEND, FLAG_NO_TMA = 1, 2, 4, 8, 16, 32, 64
 FLAG_REF_SOFTMAX = 128
 FLAG_X_F32 = 256
+FLAG_EXACT = 512
 
 _VALUE_ERRORS = {EGPT_ERR_SHAPE, EGPT_ERR_DTYPE, EGPT_ERR_ALIGN, EGPT_ERR_ARG, EGPT_ERR_WORKSPACE}
 

@@ -5,3 +5,4 @@
 #include "gemv_i8.cu"
 #include "attention.cu"
 #include "decode_step.cu"
+#include "gemv_tc.cu"

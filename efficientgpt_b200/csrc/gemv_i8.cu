@@ -471,6 +471,8 @@ static cudaError_t launch_gemv(const GemvParams &p, int grid, size_t smem, cudaS
   return launch_kernel((const void *)kern, dim3(grid), dim3(kGemvThreads), smem, st, pdl, p);
 }
 
+int gemv_tc_launch(const GemvParams &gp, cudaStream_t st);  // gemv_tc.cu
+
 int gemv_launch(GemvParams p, cudaStream_t st) {
   const bool pdl = (p.flags & EGPT_FLAG_PDL) != 0;
   if (p.m > kMaxMT) {  // the kernel holds up to 8 activation rows: split larger M into row blocks
@@ -565,6 +567,7 @@ extern "C" int egpt_gemv_i8(void *out, const void *x, int x_dtype, int64_t m, in
   p.token = token;
   p.flags = flags;
   p.epilogue = epilogue;
+  if (flags & EGPT_FLAG_EXACT) return gemv_tc_launch(p, (cudaStream_t)stream);
   return gemv_launch(p, (cudaStream_t)stream);
 }
 

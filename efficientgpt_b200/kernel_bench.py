@@ -68,12 +68,17 @@ def gemv_cases(reps, peak, src, only=''):
         # chained with programmatic dependent launch, as the launch-sequence decode path runs it: a launch streams
         # its first weights while the previous one drains
         us_pdl = time_graph(lambda i: ops.gemv_i8(x, ws[i % copies], s, out=out, pdl=True), reps)
+        # the exact int8 tensor-core kernel (EGPT_FLAG_EXACT), alone and PDL-chained
+        us_tc = time_graph(lambda i: ops.gemv_i8(x, ws[i % copies], s, out=out, exact=True), reps)
+        us_tc_pdl = time_graph(lambda i: ops.gemv_i8(x, ws[i % copies], s, out=out, exact=True, pdl=True), reps)
         nbytes = n * k + 2 * n + 2 * k + 2 * n
+        f = lambda t: round(nbytes / (t * 1e-6) / 1e9 / peak, 4)
         gbs = nbytes / (us * 1e-6) / 1e9
-        gbs_pdl = nbytes / (us_pdl * 1e-6) / 1e9
         yield {'kernel': 'gemv_i8_kernel', 'case': f'config 3 {what} N={n} K={k}', 'us': round(us, 3),
                'bytes': nbytes, 'achieved_gbs': round(gbs, 1), 'peak_gbs': peak, 'frac': round(gbs / peak, 4),
-               'us_pdl_chain': round(us_pdl, 3), 'frac_pdl_chain': round(gbs_pdl / peak, 4),
+               'us_pdl_chain': round(us_pdl, 3), 'frac_pdl_chain': f(us_pdl),
+               'exact_tc': {'kernel': 'gemv_tc_kernel', 'us': round(us_tc, 3), 'frac': f(us_tc),
+                            'us_pdl_chain': round(us_tc_pdl, 3), 'frac_pdl_chain': f(us_tc_pdl)},
                'peak_source': src, 'l2': f'{copies} weight copies rotated'}
         del ws
 

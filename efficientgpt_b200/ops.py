@@ -58,10 +58,11 @@ def quantize_rows(w, scale_dtype=torch.float32):
 
 
 def gemv_i8(x, w, s, *, out=None, epilogue=L.EPI_NONE, bias=None, residual=None, norm_w=None, eps=1e-6,
-            double_round=False, pdl=False, no_tma=False):
+            double_round=False, pdl=False, no_tma=False, exact=False):
     """out[m, :] = epilogue(s * (x[m] @ q.T)) for x [M <= 16, K] (bf16 or fp32), q int8 [N, K].
 
-    EPI_SILU_MUL takes q = cat(gate, up) rows ([2I, K]) and returns [M, I]."""
+    EPI_SILU_MUL takes q = cat(gate, up) rows ([2I, K]) and returns [M, I]. exact (one bf16 row): the int8
+    tensor-core kernel with exact row sums, rounded once (EGPT_FLAG_EXACT)."""
     _cuda(x, w, s, bias, residual, norm_w, out)
     _contig_rows(x, 'x')
     m, k = x.shape
@@ -77,7 +78,7 @@ def gemv_i8(x, w, s, *, out=None, epilogue=L.EPI_NONE, bias=None, residual=None,
     if residual is not None and (residual.stride() != out.stride() or residual.shape != out.shape):
         raise ValueError('gemv_i8: residual must have the output layout')
     flags = (L.FLAG_DOUBLE_ROUND if double_round else 0) | (L.FLAG_RMSNORM if norm_w is not None else 0) \
-        | (L.FLAG_PDL if pdl else 0) | (L.FLAG_NO_TMA if no_tma else 0)
+        | (L.FLAG_PDL if pdl else 0) | (L.FLAG_NO_TMA if no_tma else 0) | (L.FLAG_EXACT if exact else 0)
     L.check(L.load().egpt_gemv_i8(_p(out), _p(x), _dt(x), m, x.stride(0), out.stride(0), _p(w), _p(s), _dt(s), n, k,
                                   _p(bias), _p(residual), epilogue, _p(norm_w), float(eps), None, flags, _stream()),
             'gemv_i8')

@@ -57,6 +57,7 @@ extern "C" {
 #define EGPT_FLAG_NO_TMA 64u      /* GEMV: force the plain-load kernel (any K)                            */
 #define EGPT_FLAG_REF_SOFTMAX 128u /* attention: bf16 probabilities rounded as the reference GPU kernel does */
 #define EGPT_FLAG_X_F32 256u      /* lm_head argmax: x and logits are fp32 (nanoGPT), no bf16 rounding      */
+#define EGPT_FLAG_EXACT 512u      /* GEMV, one bf16 row: exact int8 tensor-core sums, one rounding per row    */
 
 /* ---- library ---------------------------------------------------------------------------------------- */
 EGPT_API const char *egpt_version(void);
@@ -81,7 +82,10 @@ EGPT_API int egpt_quantize_rows(int8_t *q, void *scale, int scale_dtype, const v
  * dtype x_dtype (bf16 for the Qwen path, fp32 for the nanoGPT path), s has scale_dtype.
  * Leading dimensions: x ldx, out/residual ldo (elements). EGPT_EPI_SILU_MUL writes n/2 outputs per row.
  * token (int64, device) is read with EGPT_FLAG_EMBED, in which case x points at the embedding table
- * [vocab, K], ldx is vocab (the token is bounds-checked against it) and residual receives the selected row. */
+ * [vocab, K], ldx is vocab (the token is bounds-checked against it) and residual receives the selected row.
+ * EGPT_FLAG_EXACT (m = 1, bf16 x, epilogue none / residual / SiLU*up, optional RMSNorm prologue, n and k
+ * multiples of 16, k up to 12288 or 6144 with RMSNorm): the int8 tensor-core kernel of the persistent decode
+ * step; the row sums are exact (fixed-point input, int64 sums) and rounded once, out = bf16(fp32(sum) * s). */
 EGPT_API int egpt_gemv_i8(void *out, const void *x, int x_dtype, int64_t m, int64_t ldx, int64_t ldo, const int8_t *w,
                  const void *scale, int scale_dtype, int64_t n, int64_t k, const void *bias, void *residual,
                  int epilogue, const void *norm_w, float eps, const int64_t *token, unsigned flags, void *stream);

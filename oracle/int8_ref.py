@@ -54,6 +54,14 @@ def int8_linear(x, q, s):
     return y.reshape(*x.shape[:-1], q.shape[0])
 
 
+def int8_exact(x, q, s):
+    """The exact-sum GEMV of the persistent decode step and EGPT_FLAG_EXACT: bf16(fp32(x . q) * s) with the dot
+    product exact (fp64 holds these bf16 x int8 sums exactly) and rounded once to fp32 (the rounding points of
+    int8_linear.py:37, `bf16(acc * s)`, with an exact acc)."""
+    acc = (np.asarray(x, np.float64) @ q.astype(np.float64).T).astype(np.float32)
+    return round_bf16(acc * np.asarray(s, np.float32)[None, :])
+
+
 def int8_truth(x, q, s):
     """fp64 ground truth of x @ (q * s).T (research/kernelagent/tasks.py:150-158, chunking irrelevant in numpy)."""
     return np.asarray(x, np.float64) @ (q.astype(np.float64) * np.asarray(s, np.float64)[:, None]).T

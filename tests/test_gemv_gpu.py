@@ -67,6 +67,50 @@ def test_gemv_sweep_vs_oracle_and_fp64(cuda, n, k, seed, edge):
     assert err <= max(2 * np.abs(naive - truth).max(), 1e-3), (n, k, err)
 
 
+@pytest.mark.parametrize('n,k', SWEEP + [(2048, 12288), (48, 32)])
+@pytest.mark.parametrize('seed,edge', [(0, None), (1, None), (0, 'large'), (0, 'extreme_w')])
+def test_exact_gemv_sweep_is_the_exact_sum_rounded_once(cuda, n, k, seed, edge):
+    """EGPT_FLAG_EXACT: the tensor-core kernel's output is bf16(fp32(exact x . q) * s) (oracle int8_exact) bit for
+    bit, except where an x value falls below the fixed-point grid (2^-29 of the largest |x|): allowed on 0.1%
+    of the outputs, one bf16 ulp at most. Covers the split-chunk mode (few tiles per CTA), the whole-tile mode
+    (lm_head) and the two-pass staging of inputs wider than 6144."""
+    L, ops = _lib()
+    x, q, s = int8_ref.gemv_inputs(n, k, seed, edge=edge)
+    xd, qd, sd = _to_dev(x, q, s, cuda)
+    y = from_torch(ops.gemv_i8(xd, qd, sd, exact=True))
+    ref = int8_ref.int8_exact(x, q, s)
+    same = np.mean(y == ref)
+    assert same >= 0.999, (n, k, same)
+    assert _bf16_ulps(y, ref).max() <= 1.0
+
+
+def test_exact_gemv_epilogues(cuda):
+    """Residual (in place), SiLU*up over cat(gate, up) and the fused RMSNorm prologue of the exact kernel against the
+    same rounding points on the oracle's exact sums."""
+    L, ops = _lib()
+    k, n = 2048, 1024
+    x, q, s = int8_ref.gemv_inputs(n, k, 3)
+    xd, qd, sd = _to_dev(x, q, s, cuda)
+    base = int8_ref.int8_exact(x, q, s)
+    rng = np.random.default_rng(5)
+    r0 = round_bf16(rng.standard_normal((1, n)).astype(np.float32))
+    r = torch.from_numpy(r0).to(cuda, torch.bfloat16)
+    ops.gemv_i8(xd, qd, sd, epilogue=L.EPI_RESIDUAL, residual=r, exact=True)
+    assert np.mean(from_torch(r) == round_bf16(r0 + base)) >= 0.999
+    y = from_torch(ops.gemv_i8(xd, qd, sd, epilogue=L.EPI_SILU_MUL, exact=True))
+    g, u = base[:, :n // 2], base[:, n // 2:]
+    want = round_bf16(round_bf16(g / (np.float32(1) + np.exp(-g))) * u)
+    assert y.shape == (1, n // 2) and _bf16_ulps(y, want).max() <= 1.0 and np.mean(y == want) >= 0.99
+    w = torch.from_numpy(round_bf16(rng.standard_normal(k).astype(np.float32))).to(cuda, torch.bfloat16)
+    fused = from_torch(ops.gemv_i8(xd, qd, sd, norm_w=w, eps=1e-6, exact=True))
+    sep = from_torch(ops.gemv_i8(ops.rmsnorm(xd, w, 1e-6), qd, sd, exact=True))
+    assert np.mean(fused == sep) >= 0.99 and _bf16_ulps(fused, sep).max() <= 2.0
+    with pytest.raises(ValueError):
+        ops.gemv_i8(xd.repeat(2, 1), qd, sd, exact=True)  # one row only
+    with pytest.raises(ValueError):
+        ops.gemv_i8(xd.float(), qd, sd, exact=True)  # bf16 only
+
+
 @pytest.mark.parametrize('m,k,n', [(1, 2048, 6144), (4, 6144, 2048), (16, 2048, 1024), (3, 100, 70), (17, 2048, 512),
                                    (64, 512, 256), (2, 2048, 1024), (1, 6144, 2048)])
 def test_op_matches_oracle_and_fp64(cuda, m, k, n):
