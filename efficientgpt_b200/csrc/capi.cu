@@ -90,12 +90,24 @@ extern "C" int egpt_decode_step(const egpt_qwen3_plan *P, void *stream) {
     return set_error(EGPT_ERR_ARG, "decode_step: tensor parallelism runs on egpt_decode_step_persistent only");
   const unsigned pdl = P->flags & EGPT_FLAG_PDL;
   const int sdt = P->scale_dtype;
+  // GEMVs on the exact int8 tensor-core kernel (the persistent step's arithmetic) where the shapes allow it
+  const int64_t reg_max = 12 * 512;
+  bool exact_ok = P->hidden % 16 == 0 && P->intermediate % 16 == 0 && (P->n_q_heads * P->head_dim) % 16 == 0 &&
+                  P->hidden <= reg_max && (int64_t)P->n_q_heads * P->head_dim <= 2 * reg_max &&
+                  P->intermediate <= 2 * reg_max && (uintptr_t)P->embed % 16 == 0 && (uintptr_t)P->h % 16 == 0 &&
+                  (uintptr_t)P->attn % 16 == 0 && (uintptr_t)P->act % 16 == 0;
+  for (int l = 0; exact_ok && l < P->n_layers; ++l) {
+    const egpt_qwen3_layer &L = P->layers[l];
+    exact_ok = (uintptr_t)L.w_qkv % 16 == 0 && (uintptr_t)L.w_o % 16 == 0 && (uintptr_t)L.w_gu % 16 == 0 &&
+               (uintptr_t)L.w_down % 16 == 0;
+  }
+  const unsigned gx = exact_ok ? EGPT_FLAG_EXACT : 0u;
   const int64_t H = P->hidden, D = P->head_dim, NQ = P->n_q_heads, NKV = P->n_kv_heads, I = P->intermediate;
   const int64_t nqkv = (NQ + 2 * NKV) * D;
   for (int l = 0; l < P->n_layers; ++l) {
     const egpt_qwen3_layer &L = P->layers[l];
     const void *x = l == 0 ? P->embed : P->h;
-    const unsigned f0 = EGPT_FLAG_RMSNORM | pdl | (l == 0 ? EGPT_FLAG_EMBED : 0u);
+    const unsigned f0 = EGPT_FLAG_RMSNORM | pdl | gx | (l == 0 ? EGPT_FLAG_EMBED : 0u);
     const int64_t ldx = l == 0 ? P->vocab : H;  // embedding mode: ldx = table rows
     int rc = egpt_gemv_i8(P->qkv, x, EGPT_BF16, 1, ldx, nqkv, L.w_qkv, L.s_qkv, sdt, nqkv, H, nullptr, P->h,
                           EGPT_EPI_NONE, L.ln_in, P->eps, P->token, f0, stream);
@@ -106,13 +118,13 @@ extern "C" int egpt_decode_step(const egpt_qwen3_plan *P, void *stream) {
                           EGPT_FLAG_APPEND | EGPT_FLAG_REF_SOFTMAX | pdl, stream);
     if (rc) return rc;
     rc = egpt_gemv_i8(P->h, P->attn, EGPT_BF16, 1, NQ * D, H, L.w_o, L.s_o, sdt, H, NQ * D, nullptr, P->h,
-                      EGPT_EPI_RESIDUAL, nullptr, 0.f, nullptr, pdl, stream);
+                      EGPT_EPI_RESIDUAL, nullptr, 0.f, nullptr, pdl | gx, stream);
     if (rc) return rc;
     rc = egpt_gemv_i8(P->act, P->h, EGPT_BF16, 1, H, I, L.w_gu, L.s_gu, sdt, 2 * I, H, nullptr, nullptr,
-                      EGPT_EPI_SILU_MUL, L.ln_post, P->eps, nullptr, EGPT_FLAG_RMSNORM | pdl, stream);
+                      EGPT_EPI_SILU_MUL, L.ln_post, P->eps, nullptr, EGPT_FLAG_RMSNORM | pdl | gx, stream);
     if (rc) return rc;
     rc = egpt_gemv_i8(P->h, P->act, EGPT_BF16, 1, I, H, L.w_down, L.s_down, sdt, H, I, nullptr, P->h,
-                      EGPT_EPI_RESIDUAL, nullptr, 0.f, nullptr, pdl, stream);
+                      EGPT_EPI_RESIDUAL, nullptr, 0.f, nullptr, pdl | gx, stream);
     if (rc) return rc;
   }
   return egpt_lm_head_argmax(P->token, P->position, P->logits, P->h, P->w_lm, P->s_lm, sdt, P->vocab, H,

@@ -25,6 +25,9 @@ using ps::kTileRows;
 struct TcParams {
   uint16_t *out;
   const uint16_t *x, *residual, *norm_w;
+  const int64_t *token;  // embedding prologue: x is the table [table_rows, k], row *token; CTA 0 copies it to
+  uint16_t *embed_to;    // embed_to (the residual stream)
+  int64_t table_rows;
   const int8_t *w;
   const void *s;
   int s_bf16, epi, nk, ring, whole;
@@ -121,9 +124,19 @@ __global__ void __launch_bounds__(kCT, 1) gemv_tc_kernel(const TcParams p) {
   pdl_wait();
   pdl_launch_dependents();
   if (epi && p.epi == EGPT_EPI_RESIDUAL) eres = bf16_bits_to_f32(__ldcg(p.residual + etile * kTileRows + er));
+  const uint16_t *xrow = p.x;
+  if (p.token) {  // embedding row of the current token (bounds-checked), stored by CTA 0 as the residual stream
+    int64_t tok = *p.token;
+    if (tok < 0 || tok >= p.table_rows) {
+      if (threadIdx.x == 0) set_device_error(EGPT_ERR_SHAPE);
+      tok = 0;
+    }
+    xrow = p.x + tok * p.k;
+  }
   const int E = p.k > ps::kMaxPerThread * kCT
-                    ? ps::stage_input_wide(p.x, p.k, xd, red)
-                    : ps::stage_input<false>(p.x, p.k, p.norm_w ? &nw : nullptr, p.eps, xd, red, nullptr, nullptr);
+                    ? ps::stage_input_wide(xrow, p.k, xd, red)
+                    : ps::stage_input<false>(xrow, p.k, p.norm_w ? &nw : nullptr, p.eps, xd, red,
+                                             (p.token && blockIdx.x == 0) ? p.embed_to : nullptr, nullptr);
 
   const int xs = ps::x_stride(p.k);
   int c4[4] = {0, 0, 0, 0};
@@ -194,8 +207,12 @@ __global__ void __launch_bounds__(kCT, 1) gemv_tc_kernel(const TcParams p) {
 
 // Host side (called by egpt_gemv_i8 with EGPT_FLAG_EXACT; p already validated for the general GEMV).
 int gemv_tc_launch(const GemvParams &gp, cudaStream_t st) {
-  if (gp.m != 1 || !gp.x_bf16 || gp.bias || (gp.flags & (EGPT_FLAG_DOUBLE_ROUND | EGPT_FLAG_EMBED)))
-    return set_error(EGPT_ERR_ARG, "gemv exact: one bf16 row, no bias, double rounding or embedding prologue");
+  if (gp.m != 1 || !gp.x_bf16 || gp.bias || (gp.flags & EGPT_FLAG_DOUBLE_ROUND))
+    return set_error(EGPT_ERR_ARG, "gemv exact: one bf16 row, no bias, no double rounding");
+  const bool embed = (gp.flags & EGPT_FLAG_EMBED) != 0;
+  if (embed && (gp.epilogue == EGPT_EPI_RESIDUAL || gp.k > (int64_t)ps::kMaxPerThread * ps::kCT))
+    return set_error(EGPT_ERR_ARG, "gemv exact: the embedding prologue takes k up to %d and no residual epilogue",
+                     ps::kMaxPerThread * ps::kCT);
   if (gp.epilogue != EGPT_EPI_NONE && gp.epilogue != EGPT_EPI_RESIDUAL && gp.epilogue != EGPT_EPI_SILU_MUL)
     return set_error(EGPT_ERR_ARG, "gemv exact: epilogue must be none, residual or SiLU*up");
   const int64_t n = gp.n, k = gp.k;
@@ -211,6 +228,11 @@ int gemv_tc_launch(const GemvParams &gp, cudaStream_t st) {
   p.x = (const uint16_t *)gp.x;
   p.residual = (const uint16_t *)gp.residual;
   p.norm_w = (gp.flags & EGPT_FLAG_RMSNORM) ? (const uint16_t *)gp.norm_w : nullptr;
+  if (embed) {
+    p.token = gp.token;
+    p.embed_to = (uint16_t *)gp.residual;
+    p.table_rows = gp.ldx;  // embedding mode: ldx holds the table's row count
+  }
   p.w = gp.w;
   p.s = gp.scale;
   p.s_bf16 = gp.scale_bf16;

@@ -83,9 +83,10 @@ EGPT_API int egpt_quantize_rows(int8_t *q, void *scale, int scale_dtype, const v
  * Leading dimensions: x ldx, out/residual ldo (elements). EGPT_EPI_SILU_MUL writes n/2 outputs per row.
  * token (int64, device) is read with EGPT_FLAG_EMBED, in which case x points at the embedding table
  * [vocab, K], ldx is vocab (the token is bounds-checked against it) and residual receives the selected row.
- * EGPT_FLAG_EXACT (m = 1, bf16 x, epilogue none / residual / SiLU*up, optional RMSNorm prologue, n and k
- * multiples of 16, k up to 12288 or 6144 with RMSNorm): the int8 tensor-core kernel of the persistent decode
- * step; the row sums are exact (fixed-point input, int64 sums) and rounded once, out = bf16(fp32(sum) * s). */
+ * EGPT_FLAG_EXACT (m = 1, bf16 x, epilogue none / residual / SiLU*up, optional RMSNorm and embedding
+ * prologues, n and k multiples of 16, k up to 12288 or 6144 with a prologue): the int8 tensor-core kernel of
+ * the persistent decode step; the row sums are exact (fixed-point input, int64 sums) and rounded once,
+ * out = bf16(fp32(sum) * s). */
 EGPT_API int egpt_gemv_i8(void *out, const void *x, int x_dtype, int64_t m, int64_t ldx, int64_t ldo, const int8_t *w,
                  const void *scale, int scale_dtype, int64_t n, int64_t k, const void *bias, void *residual,
                  int epilogue, const void *norm_w, float eps, const int64_t *token, unsigned flags, void *stream);
@@ -169,7 +170,8 @@ EGPT_API int egpt_argmax_rows(int64_t *out, const void *logits, int64_t rows, in
 /* ---- whole decode step (Qwen3 family) ---------------------------------------------------------------
  * replaces: research/realmodel/fast_decode.py:45-49 GraphGreedyDecoder._step (HF Qwen3 forward with
  *           StaticCache + argmax + position += 1), captured into one CUDA graph by the caller.
- * Launches 5 kernels per layer + the lm_head/argmax kernel. Reads *token and *position on the device,
+ * Launches 5 kernels per layer + the lm_head/argmax kernel (the GEMVs on the exact tensor-core kernel,
+ * EGPT_FLAG_EXACT, when the shapes and pointers allow it). Reads *token and *position on the device,
  * writes the next token to *token and increments *position. */
 typedef struct egpt_qwen3_layer {
   const int8_t *w_qkv;  /* [(nq + 2 nkv) d, hidden]: q_proj, k_proj, v_proj rows concatenated          */
