@@ -1018,7 +1018,7 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
         //      q|k|v tiles of its kv group are written (no grid barrier after q|k|v)
         if (!TP && attn_cta)
           ok = dep_wait(P.qcnt + blockIdx.x / nsplit,
-                        ((unsigned long long)epoch * P.L + l + 1) * (unsigned long long)((GRP + 2) * P.D / kTileRows),
+                        ((unsigned long long)epoch * P.L + l + 1) * (unsigned long long)((GRP + 2) * DPL * 32 / kTileRows),
                         &s_flag) && ok;
         if (ok && attn_cta) attention_task<DPL, GRP>(P, Ly, blockIdx.x, nsplit, bps, pos, u, pre, st);
       } else {
@@ -1061,9 +1061,10 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
           if (!TP && ph == 0) {  // count this CTA's q|k|v tiles in, per kv group, once their rows are written
             csync();
             if (threadIdx.x == 0) {
-              const int ntl = (int)cta_tiles(stage_desc(P, gs));
-              for (int tl = 0; tl < ntl; ++tl) {
-                const int hd = (int)((((int64_t)blockIdx.x + (int64_t)gridDim.x * tl) * kTileRows) / P.D);
+              constexpr int kTilesPerHead = DPL * 32 / kTileRows;
+              const int tiles = (P.NQ + 2 * P.NKV) * kTilesPerHead;
+              for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+                const int hd = t / kTilesPerHead;
                 const int g = hd < P.NQ ? hd / GRP : hd < P.NQ + P.NKV ? hd - P.NQ : hd - P.NQ - P.NKV;
                 red_release_add_u64(P.qcnt + g, 1ull);
               }
