@@ -94,6 +94,7 @@ struct Stage {
   const void *s;
   int64_t n, k, tiles;
   int kind, nk;
+  int ntl;  // tiles of this stage that belong to this CTA
 };
 
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"r"(kCT) : "memory"); }
@@ -104,13 +105,13 @@ struct StageT {
   const int8_t *w;
   const void *s;
   int64_t n, k;
-  int kind, pad;
+  int kind, ntl;  // ntl: this CTA's tiles of the stage (computed once per launch)
 };
 constexpr int kStabOffset = 256;  // after the 64-float reduction scratch
 
 __device__ __forceinline__ StageT stage_from_layers(const Params &P, int s) {
   StageT st;
-  st.pad = 0;
+  st.ntl = 0;
   if (s == 4 * P.L) {
     st.w = P.w_lm, st.s = P.s_lm, st.n = P.V, st.k = P.H, st.kind = LMHEAD;
     return st;
@@ -136,14 +137,12 @@ __device__ __forceinline__ Stage stage_desc(const Params &P, int s) {
   st.w = t.w, st.s = t.s, st.n = t.n, st.k = t.k, st.kind = t.kind;
   st.tiles = st.n / kTileRows;
   st.nk = (int)((st.k + kChunkCols - 1) / kChunkCols);
+  st.ntl = t.ntl;
   return st;
 }
 
-// Tiles of a stage that belong to this CTA.
-__device__ __forceinline__ int64_t cta_tiles(const Stage &st) {
-  const int64_t b = blockIdx.x;
-  return b < st.tiles ? (st.tiles - b + gridDim.x - 1) / gridDim.x : 0;
-}
+// Tiles of a stage that belong to this CTA (tile t belongs to CTA t % G; counted once per launch).
+__device__ __forceinline__ int cta_tiles(const Stage &st) { return st.ntl; }
 
 // Physical weight row of row r (< 16) of tile t.
 __device__ __forceinline__ int64_t tile_row(const Stage &st, int64_t t, int r) {
@@ -674,8 +673,9 @@ __device__ __forceinline__ void load_epi(const Params &P, int gs, EpiIn &in) {
   const int per_tile = sd.kind == GATEUP ? 8 : kTileRows;
   const int e = threadIdx.x;
   if (e >= cta_tiles(sd) * per_tile) return;
-  const int64_t tile = blockIdx.x + (int64_t)gridDim.x * (e / per_tile);
-  const int r = e % per_tile;
+  const int sh = per_tile == 8 ? 3 : 4;
+  const int64_t tile = blockIdx.x + (int64_t)gridDim.x * (e >> sh);
+  const int r = e & (per_tile - 1);
   in.s0 = load_scale(P, sd.s, tile_row(sd, tile, r));
   if (sd.kind == GATEUP) in.s1 = load_scale(P, sd.s, tile_row(sd, tile, r + 8));
   if (!TP && (sd.kind == OPROJ || sd.kind == DOWN)) in.res = bf16_bits_to_f32(__ldcg(P.h + tile * kTileRows + r));
@@ -700,8 +700,9 @@ __device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, 
   const int per_tile = sd.kind == GATEUP ? 8 : kTileRows;
   const int e = threadIdx.x;
   const bool epi = !lm && e < cta_tiles(sd) * per_tile;
-  const int64_t etile = blockIdx.x + (int64_t)gridDim.x * (e / per_tile);
-  const int er = e % per_tile;
+  const int esh = per_tile == 8 ? 3 : 4;
+  const int64_t etile = blockIdx.x + (int64_t)gridDim.x * (e >> esh);
+  const int er = e & (per_tile - 1);
   const float es0 = ein.s0, es1 = ein.s1, eres = ein.res;
   const int xs = x_stride(sd.k);
   int c4[4] = {0, 0, 0, 0};
@@ -771,7 +772,7 @@ __device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, 
   if (lm) return;
   csync();  // all items' sums are in `part`
   if (!epi) return;
-  const int64_t tl = e / per_tile;
+  const int64_t tl = e >> esh;
   long long T0 = 0, T1 = 0;
   for (int c = 0; c < sd.nk; ++c) {
     T0 += part[(tl * sd.nk + c) * kTileRows + er];
@@ -964,7 +965,12 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
   const int stab_bytes = ((4 * P.L + 1) * (int)sizeof(StageT) + 127) / 128 * 128;
   const int lay_bytes = (P.L * (int)sizeof(egpt_qwen3_layer) + 127) / 128 * 128;
   egpt_qwen3_layer *layers = (egpt_qwen3_layer *)(smem + kStabOffset + stab_bytes);
-  for (int i = threadIdx.x; i <= 4 * P.L; i += kCT) stage_table()[i] = stage_from_layers(P, i);
+  for (int i = threadIdx.x; i <= 4 * P.L; i += kCT) {
+    StageT t = stage_from_layers(P, i);
+    const int tiles = (int)(t.n / kTileRows), b = blockIdx.x;
+    t.ntl = b < tiles ? (tiles - b + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+    stage_table()[i] = t;
+  }
   for (int i = threadIdx.x; i < P.L; i += kCT) layers[i] = P.layers[i];
   csync();
   uint8_t *ring = smem + kStabOffset + stab_bytes + lay_bytes;  // kNC x kRing weight slots

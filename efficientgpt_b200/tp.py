@@ -7,15 +7,16 @@ matching columns of o_proj, gate/up rows and down_proj columns [r I/g, (r+1) I/g
 row over the whole row), so a shard's int8 values and scales are slices of the one-GPU tensors.
 
 Each token is ONE launch per GPU of the persistent step (egpt_decode_step_persistent with tp_world = g): the
-o_proj / down_proj partial sums cross NVLink inside the kernel (peer stores into every rank's exchange region,
-bounded flag waits), with no collective call on the path. The exchange regions are allocated by the library
+o_proj / down_proj partial sums cross NVLink inside the kernel (peer stores of sequence-tagged slots into every
+rank's exchange region; the consuming stage waits, bounded, on the slots themselves), with no collective call on
+the path. Prompts longer than 64 tokens fill the KV cache with the GEMM prefill (efficientgpt_b200.prefill). The exchange regions are allocated by the library
 (cudaMalloc: CUDA IPC exports whole allocations) and mapped into every rank with CUDA IPC handles passed
 over the process group. torch.distributed is only the plumbing that moves those handles and the barriers
 around set-up and tear-down.
 
 HBM layout per rank: the shard's fused weights (`w_qkv` [(nq/g + 2 nkv/g) d, H], `w_o` [H, nq d / g],
 `w_gu` [2 I/g, H], `w_down` [H, I/g], `w_lm` [V/g, H]), KV cache [L, 2, nkv/g, cap, d] bf16, two bf16 [H]
-residual buffers, the exchange region (4 KB flags/keys + fp64 partials [2][8][H]).
+residual buffers, the exchange region (4 KB of lm_head key slots + fp64 partial-sum slots [2][8][H], 16 bytes each).
 """
 import ctypes
 from dataclasses import dataclass
@@ -249,7 +250,7 @@ class TPQwen3Engine:
         """One decode token on the current stream, on every rank in lockstep: token <- argmax(model(token,
         position)) (the same token on every rank); position += 1."""
         if self.world > 1 and not self._started:
-            # the ranks' first kernels must start within the flag waits' bound of one another: line up first
+            # the ranks' first kernels must start within the slot waits' bound of one another: line up first
             import torch.distributed as dist
             torch.cuda.synchronize(self.device)
             dist.barrier(group=self.group)
