@@ -250,14 +250,16 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 // base completes when the counter reaches (base + idx) * G. Bounded: records EGPT_ERR_TIMEOUT, returns false.
 // Split in two so that work can go between arriving and waiting: grid_arrive publishes this CTA's writes and
 // counts it in (thread 0: one release reduction); grid_wait spins (thread 0) until every CTA arrived.
+template <bool TRACE>
 __device__ __forceinline__ void grid_arrive(const Params &P, unsigned long long idx) {
   csync();
   if (threadIdx.x == 0) {
-    if (P.trace && blockIdx.x == 0) P.trace[2 * idx - 1] = globaltimer_ns();
+    if (TRACE && P.trace && blockIdx.x == 0) P.trace[2 * idx - 1] = globaltimer_ns();
     // release: the CTA's writes (ordered before by the CTA barrier) are visible before the count
     asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(P.bar) : "memory");
   }
 }
+template <bool TRACE>
 __device__ bool grid_wait(const Params &P, unsigned long long base, unsigned long long idx, int *s_ok) {
   const unsigned long long target = (base + idx) * gridDim.x;
   if (threadIdx.x == 0) {
@@ -277,7 +279,7 @@ __device__ bool grid_wait(const Params &P, unsigned long long base, unsigned lon
       }
     }
     __threadfence();
-    if (P.trace && blockIdx.x == 0) P.trace[2 * idx] = globaltimer_ns();
+    if (TRACE && P.trace && blockIdx.x == 0) P.trace[2 * idx] = globaltimer_ns();
     *s_ok = ok;
   }
   csync();
@@ -367,8 +369,9 @@ __device__ bool dep_wait(const unsigned long long *c, unsigned long long target,
 
 // Trace: stamp k (CTA 0, thread 0) of the second trace region: the moment stage k's input is ready (GEMV
 // stages: staged and normalised; attention: this CTA's scores done).
+template <bool TRACE>
 __device__ __forceinline__ void stamp(const Params &P, int k) {
-  if (P.trace && blockIdx.x == 0 && threadIdx.x == 0) P.trace[4 + 10 * P.L + k] = globaltimer_ns();
+  if (TRACE && P.trace && blockIdx.x == 0 && threadIdx.x == 0) P.trace[4 + 10 * P.L + k] = globaltimer_ns();
 }
 
 // CTA-wide sum in a fixed order: per-warp butterfly, then every thread adds the warp partials in order.
@@ -856,7 +859,7 @@ __device__ __forceinline__ void attn_prefetch_kv(const Params &P, const egpt_qwe
   }
 }
 
-template <int DPL, int GRP>
+template <int DPL, int GRP, bool TRACE>
 __device__ void attention_task(const Params &P, const egpt_qwen3_layer &Ly, int task, int nsplit, int bps, int64_t pos,
                                float *u, const AttnPre<DPL> &pre, int tslot) {
   constexpr int D = DPL * 32;
@@ -904,7 +907,7 @@ __device__ void attention_task(const Params &P, const egpt_qwen3_layer &Ly, int 
   t.k1 = k1;
   t.scale = P.scale;
   attn_pass_a<DPL, GRP, true>(t, S);
-  stamp(P, tslot);
+  stamp<TRACE>(P, tslot);
   const int ntiles = (int)((k1 - k0 + kKeyTile - 1) / kKeyTile);
   if (nsplit > 1) {
     csync();
@@ -957,7 +960,7 @@ __device__ void attention_task(const Params &P, const egpt_qwen3_layer &Ly, int 
 }
 
 // ------------------------------------------------------------------------------------------------ kernel
-template <int DPL, int GRP, bool TP, bool WIDE>
+template <int DPL, int GRP, bool TP, bool WIDE, bool TRACE>
 __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
   extern __shared__ __align__(128) uint8_t smem[];
   float *red = (float *)smem;                    // 64 floats
@@ -1004,7 +1007,7 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
     if (threadIdx.x == 0) set_device_error(EGPT_ERR_SHAPE);
     ok = false;
   }
-  if (P.trace && blockIdx.x == 0 && threadIdx.x == 0) P.trace[0] = globaltimer_ns();
+  if (TRACE && P.trace && blockIdx.x == 0 && threadIdx.x == 0) P.trace[0] = globaltimer_ns();
 
   // Everything a stage reads that does not depend on the step (norm weights, the attention prologue's norm
   // weights and RoPE row, the KV ranges) is requested before the barrier that precedes the stage.
@@ -1026,7 +1029,7 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
           ok = dep_wait(P.qcnt + blockIdx.x / nsplit,
                         ((unsigned long long)epoch * P.L + l + 1) * (unsigned long long)((GRP + 2) * DPL * 32 / kTileRows),
                         &s_flag) && ok;
-        if (ok && attn_cta) attention_task<DPL, GRP>(P, Ly, blockIdx.x, nsplit, bps, pos, u, pre, st);
+        if (ok && attn_cta) attention_task<DPL, GRP, TRACE>(P, Ly, blockIdx.x, nsplit, bps, pos, u, pre, st);
       } else {
         // one GPU: o_proj starts once every kv head's attention output is written (no grid barrier after attention)
         if (!TP && ph == 2)
@@ -1060,7 +1063,7 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
           const int E = (WIDE && k > kMaxPerThread * kCT)
                             ? stage_input_wide(src, k, xd, red)
                             : stage_input<TP>(src, k, norm ? &nw : nullptr, P.eps, xd, red, copy_to, tinp);
-          stamp(P, st);
+          stamp<TRACE>(P, st);
           load_epi<TP>(P, gs, ein);  // consumed after the items
           gemv_stage<TP>(P, gs, S, xd, E, part, ein, best,
                          (TP && (ph == 2 || ph == 4)) ? tp_seq(P, epoch, 2 * l + (ph == 4)) : 0u);
@@ -1087,17 +1090,17 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
       // step-invariant inputs of stage st + 1, requested between arriving at the barrier that precedes it and
       // waiting there (after the arrival's fence, which would otherwise wait for them): norm weights, the
       // attention prologue's weights and RoPE row, KV ranges
-      if (st >= 0 && bar) grid_arrive(P, bidx + 1);
+      if (st >= 0 && bar) grid_arrive<TRACE>(P, bidx + 1);
       const int n = st + 1, ln = n / 5, pn = n == 5 * P.L ? 5 : n % 5;
       const egpt_qwen3_layer &Ln = layers[ln < P.L ? ln : P.L - 1];
       if (pn == 0 || pn == 3 || pn == 5)
         load_norm(pn == 5 ? P.final_norm : (const uint16_t *)(pn == 0 ? Ln.ln_in : Ln.ln_post), P.H, nw);
       if (pn == 1 && attn_cta) attn_preload<DPL, GRP>(P, Ln, blockIdx.x, nsplit, bps, pos, pre);
       if (pn == 0 && attn_cta) attn_prefetch_kv<DPL, GRP>(P, Ln, blockIdx.x, nsplit, bps, pos);
-      if (st >= 0 && bar) ok = grid_wait(P, base, ++bidx, &s_flag) && ok;
+      if (st >= 0 && bar) ok = grid_wait<TRACE>(P, base, ++bidx, &s_flag) && ok;
     }
   }
-  if (P.trace && blockIdx.x == 0 && threadIdx.x == 0) P.trace[1 + 10 * P.L] = globaltimer_ns();
+  if (TRACE && P.trace && blockIdx.x == 0 && threadIdx.x == 0) P.trace[1 + 10 * P.L] = globaltimer_ns();
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, best.v, o);
@@ -1158,7 +1161,7 @@ __global__ void __launch_bounds__(kCT, 1) decode_step_kernel(const Params P) {
       *P.lm_cnt = 0u;
       *P.epoch += 1u;
       __threadfence();
-      if (P.trace) P.trace[2 + 10 * P.L] = globaltimer_ns();
+      if (TRACE && P.trace) P.trace[2 + 10 * P.L] = globaltimer_ns();
     }
   }
 }
@@ -1174,9 +1177,11 @@ static size_t part_bytes(const egpt_qwen3_plan *Pl, int G) {
   return (size_t)items * kTileRows * 8;
 }
 
+// The %globaltimer stamps of plan->trace live in their own instantiation: the production kernel carries no
+// trace code (its instruction footprint is on the critical path of every stage).
 template <int DPL, int GRP, bool TP, bool WIDE = false>
 static cudaError_t launch(const Params &P, size_t smem, cudaStream_t st) {
-  auto kern = decode_step_kernel<DPL, GRP, TP, WIDE>;
+  auto kern = P.trace ? decode_step_kernel<DPL, GRP, TP, WIDE, true> : decode_step_kernel<DPL, GRP, TP, WIDE, false>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;

@@ -214,6 +214,32 @@ def test_gemm_prefill_matches_block_prefill(cuda, monkeypatch):
     assert ok, detail
 
 
+def test_trace_stamps_and_same_tokens(cuda):
+    """plan->trace runs the traced instantiation of the persistent kernel: %globaltimer stamps in order (start,
+    barrier arrivals and releases, token written) and the same tokens as the untraced kernel."""
+    from efficientgpt_b200 import _lib
+    from efficientgpt_b200.engine import Qwen3Engine
+    model = gi.build_model(_cfg05(), seed=3).cuda()
+    _quantize(model, torch.bfloat16, 'cuda')
+    a = Qwen3Engine(model, 96, persistent=True)
+    b = Qwen3Engine(model, 96, persistent=True)
+    L = a.n_layers
+    tr = torch.zeros(5 + 15 * L, dtype=torch.int64, device=cuda)
+    b.plan.trace = tr.data_ptr()
+    x = gi.tiny_prompts()[5].cuda()
+    a.prefill(x)
+    b.prefill(x)
+    for _ in range(8):
+        tr.zero_()
+        a.step()
+        b.step()
+        assert int(a.token) == int(b.token)
+        t = tr.cpu().tolist()
+        stamps = [t[0]] + [t[2 * i - 1] for i in range(1, 3 * L + 1)] + [t[2 + 10 * L]]
+        assert all(v > 0 for v in stamps) and stamps == sorted(stamps)
+    assert _lib.device_error() == 0
+
+
 def test_logits_past_one_softmax_block_match_oracle(cuda):
     """Teacher-forced decode from position 120 to 140 (crossing the reference kernel's first 128-key softmax
     block) vs the oracle's block-walk rounding, under the long-sequence logit rule (parity.logits_close: 99%
