@@ -402,8 +402,8 @@ def run_tp(a, world, rank, local):
         dt = max_over_ranks(t2 - t1, world)
         e2e = {'value': (NEW_TOKENS - 1) / dt, 'unit': 'tok/s', 'h2d_bytes_per_step': prompt_len * 8 / NEW_TOKENS,
                'd2h_bytes_per_step': 8, 'ttft_ms': round((t1 - t0) * 1e3, 3),
-               'api': 'efficientgpt_b200.tp.TPQwen3Engine (pinned host prompt fed token by token, then one graph '
-                      'replay and one token read per step)'}
+               'api': 'efficientgpt_b200.tp.TPQwen3Engine.feed (pinned host prompt: GEMM prefill beyond 64 tokens, '
+                      'token by token below), then one graph replay and one token read per step'}
     if rank == 0:
         wl = ('qwen3_8b int8 decode, BASELINE config 5' if big else 'qwen3_1.7b int8 decode, BASELINE config 2')
         line = {
