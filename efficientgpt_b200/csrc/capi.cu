@@ -127,9 +127,10 @@ extern "C" int egpt_decode_step(const egpt_qwen3_plan *P, void *stream) {
                       EGPT_EPI_RESIDUAL, nullptr, 0.f, nullptr, pdl | gx, stream);
     if (rc) return rc;
   }
+  const unsigned gl = (gx && P->vocab % 16 == 0 && (uintptr_t)P->w_lm % 16 == 0) ? EGPT_FLAG_EXACT : 0u;
   return egpt_lm_head_argmax(P->token, P->position, P->logits, P->h, P->w_lm, P->s_lm, sdt, P->vocab, H,
                              P->final_norm, P->eps, P->lm_ws, P->lm_ws_bytes,
-                             EGPT_FLAG_RMSNORM | EGPT_FLAG_ADVANCE | pdl, stream);
+                             EGPT_FLAG_RMSNORM | EGPT_FLAG_ADVANCE | pdl | gl, stream);
 }
 
 // ---------------------------------------------------------------------------------------- tensor parallelism

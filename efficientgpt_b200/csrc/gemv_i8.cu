@@ -610,5 +610,6 @@ extern "C" int egpt_lm_head_argmax(int64_t *token, int64_t *position, void *logi
   p.ws_val = (float *)ws;
   p.ws_idx = (int *)((char *)ws + kArgmaxMaxCtas * 4);
   p.ws_counter = (unsigned *)((char *)ws + kArgmaxMaxCtas * 8);
+  if (flags & EGPT_FLAG_EXACT) return gemv_tc_launch(p, (cudaStream_t)stream);
   return gemv_launch(p, (cudaStream_t)stream);
 }

@@ -34,6 +34,14 @@ struct TcParams {
   int64_t n, k, tiles;
   float eps;
   int part_bytes;
+  // lm_head argmax (out unused, logits nullable): each CTA's best (logit, row) into ws, the last CTA to finish
+  // writes the token (first index on ties) and, with advance, position + 1
+  int argmax, advance;
+  int64_t *tok_out, *position;
+  uint16_t *logits;
+  float *ws_val;
+  int *ws_idx;
+  unsigned *ws_counter;
 };
 
 __device__ __forceinline__ int64_t tc_row(const TcParams &p, int64_t t, int r) {
@@ -86,6 +94,63 @@ __device__ __forceinline__ void tc_emit(const TcParams &p, int64_t tile, int r, 
     p.out[tile * kTileRows + r] = f32_to_bf16_bits(res + round_bf16(y0 * s0));
   } else {
     p.out[tile * kTileRows + r] = f32_to_bf16_bits(y0 * s0);
+  }
+}
+
+// lm_head logit of one row from its exact sum: bf16(fp32(T) 2^E * s), kept if it beats the thread's best.
+__device__ __forceinline__ void tc_best(const TcParams &p, int64_t row, long long T, int E, float s, float &bv, int &bi) {
+  const float y = round_bf16(ps::mul_pow2(__ll2float_rn(T), E) * s);
+  if (p.logits) p.logits[row] = f32_to_bf16_bits(y);
+  if (argmax_better(y, (int)row, bv, bi)) bv = y, bi = (int)row;
+}
+
+// All threads: the CTA's best (warps, then thread 0) into ws; the last CTA to arrive reduces every CTA's best.
+__device__ void tc_argmax_finish(const TcParams &p, float bv, int bi) {
+  __shared__ float s_bv[kNC];
+  __shared__ int s_bi[kNC];
+  __shared__ int s_last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (argmax_better(ov, oi, bv, bi)) bv = ov, bi = oi;
+  }
+  if (lane == 0) s_bv[warp] = bv, s_bi[warp] = bi;
+  ps::csync();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kNC; ++w)
+      if (argmax_better(s_bv[w], s_bi[w], bv, bi)) bv = s_bv[w], bi = s_bi[w];
+    p.ws_val[blockIdx.x] = bv;
+    p.ws_idx[blockIdx.x] = bi;
+    __threadfence();
+    s_last = atomicAdd(p.ws_counter, 1u) == gridDim.x - 1;
+  }
+  ps::csync();
+  if (!s_last) return;
+  __threadfence();
+  bv = -INFINITY;
+  bi = 0x7fffffff;
+  for (unsigned b = threadIdx.x; b < gridDim.x; b += kCT) {
+    const float v = __ldcg(&p.ws_val[b]);
+    const int i = __ldcg(&p.ws_idx[b]);
+    if (argmax_better(v, i, bv, bi)) bv = v, bi = i;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (argmax_better(ov, oi, bv, bi)) bv = ov, bi = oi;
+  }
+  ps::csync();
+  if (lane == 0) s_bv[warp] = bv, s_bi[warp] = bi;
+  ps::csync();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kNC; ++w)
+      if (argmax_better(s_bv[w], s_bi[w], bv, bi)) bv = s_bv[w], bi = s_bi[w];
+    *p.tok_out = (int64_t)bi;
+    if (p.advance && p.position) *p.position += 1;
+    *p.ws_counter = 0u;
   }
 }
 
@@ -142,6 +207,8 @@ __global__ void __launch_bounds__(kCT, 1) gemv_tc_kernel(const TcParams p) {
   int c4[4] = {0, 0, 0, 0};
   float ws0 = 0.f, ws1 = 0.f, wr0 = 0.f, wr1 = 0.f;  // whole mode: the tile's scales / residuals (lanes t == 0)
   int slot = 0;
+  float bv = -INFINITY;  // argmax: this thread's best logit and its row
+  int bi = 0x7fffffff;
   for (int j = 0; tc_item(p, ntl, j, tl, c); ++j) {
     const int64_t tile = blockIdx.x + (int64_t)G * tl;
     if (!p.whole || c == 0) c4[0] = c4[1] = c4[2] = c4[3] = 0;
@@ -184,23 +251,32 @@ __global__ void __launch_bounds__(kCT, 1) gemv_tc_kernel(const TcParams p) {
       part[(tl * p.nk + c) * kTileRows + g + 8] = T1;
       continue;
     }
-    if (p.epi == EGPT_EPI_SILU_MUL) {
+    if (p.argmax) {
+      tc_best(p, tile * kTileRows + g, T0, E, ws0, bv, bi);
+      tc_best(p, tile * kTileRows + g + 8, T1, E, ws1, bv, bi);
+    } else if (p.epi == EGPT_EPI_SILU_MUL) {
       tc_emit(p, tile, g, T0, T1, E, ws0, ws1, 0.f);
     } else {
       tc_emit(p, tile, g, T0, 0, E, ws0, 0.f, wr0);
       tc_emit(p, tile, g + 8, T1, 0, E, ws1, 0.f, wr1);
     }
   }
-  if (p.whole) return;
-  ps::csync();  // all items' sums are in `part`
-  if (!epi) return;
-  const int64_t tle = e / per_tile;
-  long long T0 = 0, T1 = 0;
-  for (int cc = 0; cc < p.nk; ++cc) {
-    T0 += part[(tle * p.nk + cc) * kTileRows + er];
-    if (p.epi == EGPT_EPI_SILU_MUL) T1 += part[(tle * p.nk + cc) * kTileRows + er + 8];
+  if (!p.whole) {
+    ps::csync();  // all items' sums are in `part`
+    if (epi) {
+      const int64_t tle = e / per_tile;
+      long long T0 = 0, T1 = 0;
+      for (int cc = 0; cc < p.nk; ++cc) {
+        T0 += part[(tle * p.nk + cc) * kTileRows + er];
+        if (p.epi == EGPT_EPI_SILU_MUL) T1 += part[(tle * p.nk + cc) * kTileRows + er + 8];
+      }
+      if (p.argmax)
+        tc_best(p, etile * kTileRows + er, T0, E, es0, bv, bi);
+      else
+        tc_emit(p, etile, er, T0, T1, E, es0, es1, eres);
+    }
   }
-  tc_emit(p, etile, er, T0, T1, E, es0, es1, eres);
+  if (p.argmax) tc_argmax_finish(p, bv, bi);
 }
 
 }  // namespace tc
@@ -215,6 +291,8 @@ int gemv_tc_launch(const GemvParams &gp, cudaStream_t st) {
                      ps::kMaxPerThread * ps::kCT);
   if (gp.epilogue != EGPT_EPI_NONE && gp.epilogue != EGPT_EPI_RESIDUAL && gp.epilogue != EGPT_EPI_SILU_MUL)
     return set_error(EGPT_ERR_ARG, "gemv exact: epilogue must be none, residual or SiLU*up");
+  if (gp.argmax && (gp.epilogue != EGPT_EPI_NONE || embed || gp.n > 0x7fffffff))
+    return set_error(EGPT_ERR_ARG, "lm_head argmax exact: plain rows only");
   const int64_t n = gp.n, k = gp.k;
   if (n % 16 || k % 16) return set_error(EGPT_ERR_SHAPE, "gemv exact: n and k must be multiples of 16");
   const int64_t reg_max = (int64_t)ps::kMaxPerThread * ps::kCT;
@@ -237,6 +315,16 @@ int gemv_tc_launch(const GemvParams &gp, cudaStream_t st) {
   p.s = gp.scale;
   p.s_bf16 = gp.scale_bf16;
   p.epi = gp.epilogue;
+  if (gp.argmax) {
+    p.argmax = 1;
+    p.advance = (gp.flags & EGPT_FLAG_ADVANCE) != 0;
+    p.tok_out = gp.tok_out;
+    p.position = gp.position;
+    p.logits = (uint16_t *)gp.logits;
+    p.ws_val = gp.ws_val;
+    p.ws_idx = gp.ws_idx;
+    p.ws_counter = gp.ws_counter;
+  }
   p.n = n;
   p.k = k;
   p.eps = gp.eps;

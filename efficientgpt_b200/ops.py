@@ -104,7 +104,7 @@ def lm_head_ws(n, device):
 
 
 def lm_head_argmax(x, w, s, ws, *, norm_w=None, eps=1e-6, logits=None, token=None, position=None, advance=False,
-                   pdl=False):
+                   pdl=False, exact=False):
     """token = argmax(bf16(s * (RMSNorm(x) @ q.T))) on the device; x bf16 [K] (one row). fp32 x (nanoGPT): the
     logits are fp32 s * (x @ q.T) without rounding, written fp32 to `logits`."""
     _cuda(x, w, s, ws, norm_w, logits, token, position)
@@ -116,7 +116,8 @@ def lm_head_argmax(x, w, s, ws, *, norm_w=None, eps=1e-6, logits=None, token=Non
     if token is None:
         token = torch.empty(1, dtype=torch.int64, device=x.device)
     flags = (L.FLAG_RMSNORM if norm_w is not None else 0) | (L.FLAG_ADVANCE if advance else 0) \
-        | (L.FLAG_PDL if pdl else 0) | (L.FLAG_X_F32 if x.dtype == torch.float32 else 0)
+        | (L.FLAG_PDL if pdl else 0) | (L.FLAG_X_F32 if x.dtype == torch.float32 else 0) \
+        | (L.FLAG_EXACT if exact else 0)
     L.check(L.load().egpt_lm_head_argmax(_p(token), _p(position), _p(logits), _p(x), _p(w), _p(s), _dt(s), n, k,
                                          _p(norm_w), float(eps), _p(ws), ws.numel(), flags, _stream()),
             'lm_head_argmax')

@@ -96,7 +96,8 @@ EGPT_API int egpt_gemv_i8(void *out, const void *x, int x_dtype, int64_t m, int6
  *           research/realmodel/fast_decode.py:48 (argmax(-1), first index on ties) and :49 (position += 1)
  * token[0] = argmax_n bf16(s[n] * sum_k xn[k] q[n, k]) where xn = RMSNorm(x)*norm_w if EGPT_FLAG_RMSNORM.
  * logits ([n], nullable; bf16, or fp32 with EGPT_FLAG_X_F32) receives the logits. ws must hold egpt_lm_head_ws_bytes(n) bytes,
- * zero-filled once before first use (the kernel leaves its counter at zero). */
+ * zero-filled once before first use (the kernel leaves its counter at zero). EGPT_FLAG_EXACT (bf16 x, n and k
+ * multiples of 16): the logits come from the exact int8 tensor-core kernel, bf16(fp32(exact sum) * s). */
 EGPT_API size_t egpt_lm_head_ws_bytes(int64_t n);
 EGPT_API int egpt_lm_head_argmax(int64_t *token, int64_t *position, void *logits, const void *x, const int8_t *w,
                         const void *scale, int scale_dtype, int64_t n, int64_t k, const void *norm_w, float eps,

@@ -251,6 +251,26 @@ def test_epilogues_vs_torch(cuda):
 
 
 @pytest.mark.parametrize('n,k', [(151936, 2048), (50304, 384), (512, 128)])
+def test_exact_lm_head_argmax(cuda, n, k):
+    """EGPT_FLAG_EXACT on the lm_head: logits bf16(fp32(exact sum) * s) (oracle int8_exact), token = first index
+    of the maximum, position advanced; whole-tile mode (151936, 50304) and split mode (512), two calls in a row
+    (the workspace counter is left at zero)."""
+    L, ops = _lib()
+    x, q, s = int8_ref.gemv_inputs(n, k, 2)
+    xd, qd, sd = _to_dev(x, q, s, cuda)
+    ws = ops.lm_head_ws(n, cuda)
+    want = int8_ref.int8_exact(x, q, s)[0]
+    pos = torch.zeros(1, dtype=torch.int64, device=cuda)
+    for it in range(2):
+        logits = torch.empty(n, dtype=torch.bfloat16, device=cuda)
+        tok = ops.lm_head_argmax(xd[0], qd, sd, ws, logits=logits, position=pos, advance=True, exact=True)
+        got = from_torch(logits)
+        assert np.mean(got == want) >= 0.999 and _bf16_ulps(got, want).max() <= 1.0
+        assert int(tok) == int(np.argmax(got))  # first index of the maximum of its own logits
+        assert int(pos) == it + 1
+
+
+@pytest.mark.parametrize('n,k', [(151936, 2048), (50304, 384), (512, 128)])
 def test_lm_head_argmax_vs_oracle(cuda, n, k):
     L, ops = _lib()
     x, q, s = int8_ref.gemv_inputs(n, k, seed=3)
