@@ -393,16 +393,21 @@ constexpr int kGroups = kMaxPerThread / 4;  // a thread stages groups of 4 conse
 // RMSNorm weights of a stage input, loaded into registers BEFORE the grid barrier that precedes the stage
 // (they do not depend on the step), so their latency hides behind the barrier instead of adding to it.
 // Thread t holds elements 4 (t + 512 j) .. + 3, j < kGroups.
+// The weights stay as the loaded bf16 pairs and are widened where they are used: an instruction that consumed the
+// loads here would stall the thread on their latency right away.
 struct NormW {
-  float w[kMaxPerThread];
+  uint2 u[kGroups];
+  __device__ __forceinline__ float w(int e) const {
+    const uint32_t x = (e & 2) ? u[e >> 2].y : u[e >> 2].x;
+    return (e & 1) ? bf16_hi(x) : bf16_lo(x);
+  }
 };
 __device__ __forceinline__ void load_norm(const uint16_t *nw, int64_t k, NormW &n) {
 #pragma unroll
   for (int j = 0; j < kGroups; ++j) {
     const int64_t i = 4 * ((int64_t)threadIdx.x + (int64_t)j * kCT);
-    uint2 u = make_uint2(0u, 0u);
-    if (i < k) u = *(const uint2 *)(nw + i);
-    n.w[4 * j] = bf16_lo(u.x), n.w[4 * j + 1] = bf16_hi(u.x), n.w[4 * j + 2] = bf16_lo(u.y), n.w[4 * j + 3] = bf16_hi(u.y);
+    n.u[j] = make_uint2(0u, 0u);
+    if (i < k) n.u[j] = *(const uint2 *)(nw + i);
   }
 }
 
@@ -523,7 +528,7 @@ __device__ int stage_input(const uint16_t *src, int64_t k, const NormW *nw, floa
 #pragma unroll
   for (int e = 0; e < kMaxPerThread; ++e) {
     ss = fmaf(v[e], v[e], ss);
-    mx = fmaxf(mx, fabsf(nw ? v[e] * nw->w[e] : v[e]));
+    mx = fmaxf(mx, fabsf(nw ? v[e] * nw->w(e) : v[e]));
   }
   ss = warp_sum(ss);
   mx = warp_max(mx);
@@ -537,7 +542,7 @@ __device__ int stage_input(const uint16_t *src, int64_t k, const NormW *nw, floa
   if (nw) {
     const float inv = rsqrtf(tot / (float)k + eps);
 #pragma unroll
-    for (int e = 0; e < kMaxPerThread; ++e) v[e] = round_bf16(round_bf16(v[e] * inv) * nw->w[e]);
+    for (int e = 0; e < kMaxPerThread; ++e) v[e] = round_bf16(round_bf16(v[e] * inv) * nw->w(e));
     bound = bound * inv * 1.0079f;
   }
   const int ex = bound > 0.f ? ((__float_as_int(bound) >> 23) & 0xFF) - 127 : 0;  // floor(log2 bound)
@@ -665,13 +670,21 @@ __device__ __forceinline__ float load_scale(const Params &P, const void *s, int6
 
 // Epilogue inputs of a layer stage for thread e (< this CTA's tiles x 16, or x 8 for gate/up pairs): its rows'
 // scales and (o, down) the residual row, requested when the stage starts and consumed after its items.
+// Raw bits as loaded (bf16 in the low half, or fp32 scales), widened in the epilogue: converting at the load would
+// stall the thread on the load's latency at the start of the stage.
 struct EpiIn {
-  float s0, s1, res;
+  uint32_t s0, s1, res;
 };
+__device__ __forceinline__ uint32_t raw_scale(const Params &P, const void *s, int64_t row) {
+  return P.scale_bf16 ? (uint32_t)((const uint16_t *)s)[row] : __float_as_uint(((const float *)s)[row]);
+}
+__device__ __forceinline__ float scale_of(const Params &P, uint32_t raw) {
+  return P.scale_bf16 ? __uint_as_float(raw << 16) : __uint_as_float(raw);
+}
 template <bool TP>
 __device__ __forceinline__ void load_epi(const Params &P, int gs, EpiIn &in) {
   const Stage sd = stage_desc(P, gs);
-  in.s0 = in.s1 = in.res = 0.f;
+  in.s0 = in.s1 = in.res = 0u;
   if (sd.kind == LMHEAD) return;
   const int per_tile = sd.kind == GATEUP ? 8 : kTileRows;
   const int e = threadIdx.x;
@@ -679,9 +692,9 @@ __device__ __forceinline__ void load_epi(const Params &P, int gs, EpiIn &in) {
   const int sh = per_tile == 8 ? 3 : 4;
   const int64_t tile = blockIdx.x + (int64_t)gridDim.x * (e >> sh);
   const int r = e & (per_tile - 1);
-  in.s0 = load_scale(P, sd.s, tile_row(sd, tile, r));
-  if (sd.kind == GATEUP) in.s1 = load_scale(P, sd.s, tile_row(sd, tile, r + 8));
-  if (!TP && (sd.kind == OPROJ || sd.kind == DOWN)) in.res = bf16_bits_to_f32(__ldcg(P.h + tile * kTileRows + r));
+  in.s0 = raw_scale(P, sd.s, tile_row(sd, tile, r));
+  if (sd.kind == GATEUP) in.s1 = raw_scale(P, sd.s, tile_row(sd, tile, r + 8));
+  if (!TP && (sd.kind == OPROJ || sd.kind == DOWN)) in.res = (uint32_t)__ldcg(P.h + tile * kTileRows + r);
 }
 
 // Consume this warp's items of stage s (the stream's cursor is at stage s or later). Per item and lane (g =
@@ -706,7 +719,7 @@ __device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, 
   const int esh = per_tile == 8 ? 3 : 4;
   const int64_t etile = blockIdx.x + (int64_t)gridDim.x * (e >> esh);
   const int er = e & (per_tile - 1);
-  const float es0 = ein.s0, es1 = ein.s1, eres = ein.res;
+  const EpiIn er_raw = ein;  // widened after the items (scale_of, bf16 residual)
   const int xs = x_stride(sd.k);
   int c4[4] = {0, 0, 0, 0};
   while (S.cur.s == s) {
@@ -783,7 +796,7 @@ __device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, 
   }
   const float y0 = mul_pow2(__ll2float_rn(T0), E);
   switch (sd.kind) {
-    case QKV: P.qkv[etile * kTileRows + er] = f32_to_bf16_bits(y0 * es0); break;
+    case QKV: P.qkv[etile * kTileRows + er] = f32_to_bf16_bits(y0 * scale_of(P, er_raw.s0)); break;
     case OPROJ:
     case DOWN:
       if (TP) {
@@ -793,11 +806,13 @@ __device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, 
         for (int q = 0; q < P.tp_world; ++q)
           ll_store(xpart(P.xchg[q], sd.kind == OPROJ ? 0 : 1, P.tp_rank, P.H) + row * 16, bits, tseq);
       } else {
-        P.h[etile * kTileRows + er] = f32_to_bf16_bits(eres + round_bf16(y0 * es0));
+        P.h[etile * kTileRows + er] =
+            f32_to_bf16_bits(__uint_as_float(er_raw.res << 16) + round_bf16(y0 * scale_of(P, er_raw.s0)));
       }
       break;
     default: {  // GATEUP: act = bf16(bf16(silu(gate)) * up)
-      const float gt = round_bf16(y0 * es0), up = round_bf16(mul_pow2(__ll2float_rn(T1), E) * es1);
+      const float gt = round_bf16(y0 * scale_of(P, er_raw.s0)),
+                  up = round_bf16(mul_pow2(__ll2float_rn(T1), E) * scale_of(P, er_raw.s1));
       P.act[etile * 8 + er] = f32_to_bf16_bits(round_bf16(gt / (1.0f + expf(-gt))) * up);
     }
   }
