@@ -3,21 +3,20 @@
 // Replaces the launch sequence of egpt_decode_step (5 kernels per layer + lm_head), whose kernel boundaries
 // (launch, ramp-up, tail, activation reload) cost several microseconds each and dominate the 1.7 GB weight
 // stream of a Qwen3-1.7B token (~265 us at the measured HBM bandwidth). Inside one kernel:
-//   * every GEMV stage (QKV, O, gate/up, down of each layer, then lm_head) is cut into row pairs; pair q of a
-//     stage belongs to CTA q % G and, inside the CTA, to warp (q / G) % 16, so at any moment the whole GPU
-//     reads a narrow, contiguous window of the matrix (all DRAM channels busy);
-//   * each warp walks ONE flattened stream of (stage, pair, 2048-column chunk) items across all stages of
-//     the token. Weights do not depend on activations, so each warp keeps kRing items in flight in its own
-//     shared-memory ring (cp.async, 8 x 16 B per lane and item, plus the rows' scales) and an L2 prefetch
-//     cursor (prefetch.global.L2::evict_last) kAhead items further: HBM keeps streaming the next stages'
-//     weights while the warps wait at a barrier or run attention;
-//   * the int8 x fp32 math is the exact packed-f32x2 dot product of gemv_i8.cu (same summation order per row);
-//   * per stage the CTA stages its input vector in shared memory (fused RMSNorm, or the embedding row for
-//     layer 0) and the lanes owning a reduced pair apply the fused epilogue (scale, residual add, SiLU*up,
-//     lm_head argmax);
-//   * stages that consume a whole vector produced by other CTAs are separated by a grid barrier: a monotonic
-//     64-bit arrival counter with release/acquire ordering and a per-step epoch; every wait is bounded and
-//     records EGPT_ERR_TIMEOUT instead of hanging;
+//   * every GEMV stage (q|k|v, o, gate|up, down of each layer, then lm_head) is cut into 16-row tiles (tile t
+//     belongs to CTA t % G) and 256-column items of 4 KB;
+//   * each warp walks ONE flattened stream of (stage, tile, chunk) items across all stages of the token. Weights
+//     do not depend on activations, so each warp keeps kRing items in flight in its own shared-memory ring
+//     (cp.async, XOR-swizzled rows): HBM keeps streaming the next stages' weights while the warps wait at a
+//     barrier or run attention;
+//   * the GEMVs are exact: the stage input is staged once per CTA as fixed point (four int8 digit planes),
+//     mma.sync.m16n8k32.s8 gives exact int32 per item, the planes fold into exact int64 row sums, and each row is
+//     rounded once, then scaled and rounded at the reference's bf16 points (fused RMSNorm prologue; residual,
+//     SiLU*up, lm_head argmax epilogues);
+//   * three grid barriers per layer (after o_proj, gate|up and down_proj: a monotonic 64-bit arrival counter with
+//     release/acquire ordering and a per-step epoch); after q|k|v and attention, dependency counters (q|k|v tiles
+//     per kv group, kv heads done) replace them. Every wait is bounded and records EGPT_ERR_TIMEOUT instead of
+//     hanging;
 //   * attention runs as a stage: CTA t < nkv * nsplit takes kv head t / nsplit and key range t % nsplit of
 //     whole 128-key blocks (q/k RMSNorm + RoPE + KV append, then the attention core of attention.cu with the
 //     reference GPU kernel's softmax rounding; ranges exchange their maxima), the last range of each head
@@ -46,11 +45,7 @@ constexpr int kItemBytes = kTileRows * kChunkCols;
 #ifndef EGPT_PS_RING
 #define EGPT_PS_RING 2
 #endif
-#ifndef EGPT_PS_AHEAD
-#define EGPT_PS_AHEAD 0
-#endif
 constexpr int kRing = EGPT_PS_RING;    // stream items in flight per warp (shared-memory ring filled by cp.async)
-constexpr int kAhead = EGPT_PS_AHEAD;  // items prefetched into L2 beyond the ring (0: none)
 constexpr int kSlot = kItemBytes + 64; // ring slot: the item, then its tile's 16 scales (up to 64 bytes)
 constexpr int kXPad = 64;              // bytes between the digit planes of the staged input (bank spread)
 
@@ -619,21 +614,9 @@ struct Best {
 
 struct Stream {
   Cursor cur, fill;  // consumption and ring-fill (kRing items ahead of cur) cursors
-  Cursor pf;         // L2 prefetch cursor (kAhead items ahead of fill)
   int slot;          // ring slot holding cur's item
   uint8_t *ring;     // this warp's kRing slots
 };
-
-// L2 prefetch of one item: lane l takes 128-byte line l of the 16 x 256-byte tile (pieces past the row end skipped).
-__device__ __forceinline__ void prefetch_item(const Cursor &cu) {
-  const int lane = threadIdx.x & 31, r = lane >> 1, half = lane & 1;
-  const Stage &st = cu.st;
-  const int64_t col0 = (int64_t)cu.c * kChunkCols + half * 128;
-  if (col0 < st.k) {
-    const int8_t *a = st.w + tile_row(st, cu.tile, r) * st.k + col0;
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
-  }
-}
 
 // Start the stream: kRing items in flight (one commit group each, empty past the end).
 __device__ __forceinline__ void stream_start(const Params &P, Stream &S, uint8_t *ring) {
@@ -648,11 +631,6 @@ __device__ __forceinline__ void stream_start(const Params &P, Stream &S, uint8_t
       cur_next(P, S.fill);
     }
     cp_async_commit();
-  }
-  S.pf = S.fill;
-  for (int i = 0; i < kAhead && !cur_end(P, S.pf); ++i) {
-    prefetch_item(S.pf);
-    cur_next(P, S.pf);
   }
 }
 
@@ -758,10 +736,6 @@ __device__ void gemv_stage(const Params &P, int s, Stream &S, const int8_t *xd, 
       cur_next(P, S.fill);
     }
     cp_async_commit();
-    if (kAhead > 0 && !cur_end(P, S.pf)) {
-      prefetch_item(S.pf);
-      cur_next(P, S.pf);
-    }
     S.slot = S.slot + 1 == kRing ? 0 : S.slot + 1;
     cur_next(P, S.cur);
     if (lm && !last) continue;
