@@ -62,6 +62,31 @@ def int8_exact(x, q, s):
     return round_bf16(acc * np.asarray(s, np.float32)[None, :])
 
 
+def fixed_point_stage(x):
+    """The exact GEMV's input staging in numpy (the arithmetic of the product's stage_input, not a reference
+    function): bound = max |x|, E = floor(log2 bound) - 29, X = rint(x 2^-E) with |X| < 2^30, and X's balanced
+    base-256 digits d0..d3 in [-128, 127] (X = sum d_i 256^i). Returns (E, X int64, digits int64 [4, ...])."""
+    x = np.asarray(x, np.float32)
+    bound = float(np.max(np.abs(x))) if x.size else 0.0
+    ex = int(np.floor(np.log2(bound))) if bound > 0 else 0
+    e = ex - 29
+    big = np.rint(x.astype(np.float64) * 2.0 ** -e).astype(np.int64)
+    digits, rest = [], big.copy()
+    for _ in range(3):
+        d = ((rest + 128) & 0xFF) - 128  # balanced digit: the low byte read as int8
+        digits.append(d)
+        rest = (rest - d) >> 8
+    digits.append(rest)
+    return e, big, np.stack(digits)
+
+
+def int8_fixed_point(x, q, s):
+    """bf16(fp32(sum_k X_k q_nk 2^E) * s): the exact GEMV on the staged fixed-point input (int64 sums)."""
+    e, big, _ = fixed_point_stage(np.asarray(x, np.float32)[0])
+    acc = (big[None, :] @ q.astype(np.int64).T).astype(np.float64) * 2.0 ** e
+    return round_bf16(acc.astype(np.float32) * np.asarray(s, np.float32)[None, :])
+
+
 def int8_truth(x, q, s):
     """fp64 ground truth of x @ (q * s).T (research/kernelagent/tasks.py:150-158, chunking irrelevant in numpy)."""
     return np.asarray(x, np.float64) @ (q.astype(np.float64) * np.asarray(s, np.float64)[:, None]).T

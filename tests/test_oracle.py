@@ -157,3 +157,17 @@ def test_nanogpt_oracle_matches_reference_golden():
         assert toks == run['tokens']
         lg = NanoGPTRef(params, meta['config']).forward(run['prompt'], 0)
         np.testing.assert_allclose(lg, z[f"logits_first_{len(run['prompt'])}"], atol=1e-6, rtol=0)
+
+
+@pytest.mark.parametrize('n,k,edge', [(512, 2048, None), (256, 6144, 'large'), (128, 12288, 'extreme_w')])
+def test_fixed_point_staging_is_exact(n, k, edge):
+    """The exact GEMV's staging: balanced digits rebuild X, |X| < 2^30 and every digit in [-128, 127] (digit 3 too),
+    and the int64 dot product on X rounded once equals the exact-sum oracle int8_exact (x values of N(0, 1) sit on
+    the fixed-point grid: bf16 values at least 2^-29 of the largest)."""
+    x, q, s = int8_ref.gemv_inputs(n, k, 4, edge=edge)
+    e, big, d = int8_ref.fixed_point_stage(x[0])
+    assert np.all(np.abs(big) < 2 ** 30)
+    assert d.min() >= -128 and d.max() <= 127
+    assert np.array_equal(d[0] + 256 * d[1] + 65536 * d[2] + 16777216 * d[3], big)
+    assert np.array_equal(big.astype(np.float64) * 2.0 ** e, x[0].astype(np.float64))  # on the grid
+    np.testing.assert_array_equal(int8_ref.int8_fixed_point(x, q, s), int8_ref.int8_exact(x, q, s))
