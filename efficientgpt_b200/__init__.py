@@ -1,7 +1,8 @@
 """efficientgpt_b200: batch-1 int8 decode engine for NVIDIA B200 (sm_100a).
 
 Drop-in for the research/realmodel path of BagelsFun/efficientgpt: `int8_linear` (op, Int8Linear, quantize_model),
-`fast_decode.GraphGreedyDecoder`, with the arithmetic in hand-written CUDA (libegpt_b200.so, C-ABI in
+`fast_decode.GraphGreedyDecoder`, plus `tp.TPQwen3Engine` (tensor parallelism) and `nanogpt` (config 1), with the
+arithmetic in hand-written CUDA (libegpt_b200.so, C-ABI in
 include/egpt_b200.h). Submodules import lazily so the package imports without a GPU.
 """
 from . import _lib  # noqa: F401
@@ -19,4 +20,10 @@ def __getattr__(name):
     if name == 'Qwen3Engine':
         from .engine import Qwen3Engine
         return Qwen3Engine
+    if name == 'TPQwen3Engine':  # tensor parallelism over 2/4/8 GPUs of one box
+        from .tp import TPQwen3Engine
+        return TPQwen3Engine
+    if name in ('GPT', 'GPTConfig', 'NanoGPTEngine'):  # nanoGPT
+        from . import nanogpt as m
+        return getattr(m, name)
     raise AttributeError(name)
