@@ -1,37 +1,40 @@
 #!/usr/bin/env python
 """Batch-1 greedy decode throughput of the Qwen3-1.7B-shape int8 model on B200 (BASELINE.json metric).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ...]
 
 A step is one decode token: one replay of the CUDA graph that holds the native decode step (one persistent
-cooperative kernel per token; 141 kernels per token on the launch-sequence path). Workload = BASELINE config 2: random-init weights (seed 0), int8 per-row weights with bf16 scales,
-a 32-token uniform prompt, then 256 greedy tokens; the timed loop replays that 256-token window (position reset
-to 32 every 256 steps), so contexts run 33..288 as in the config. The 1.72 GB of weights streamed per token are
-far larger than L2 (126 MB), so no flush is needed between steps.
+cooperative kernel per token). Workload = BASELINE config 2: random-init weights (seed 0), int8 per-row weights
+with bf16 scales, a 32-token uniform prompt, then 256 greedy tokens (contexts 33..288). Before the timed region the
+whole 256-token window runs once (every KV row of the window written); the K timed steps are then spread evenly
+over the window's positions (K >= 256: whole windows in order; K < 256: position 32 + floor(256 i / K) for step i,
+set on the device before the replay when it does not follow from the previous step), so any K measures the
+config's context mix. The 1.72 GB of weights streamed per token are far larger than L2 (126 MB), so no flush is
+needed between steps.
 
 Printed JSON line (rank 0):
   value        decode tok/s over all ranks, device-timed (CUDA events around the K replays, max over ranks)
   e2e          the same metric through GraphGreedyDecoder.generate with a pinned host prompt: H2D prompt copy,
                per-token D2H token reads, (n - 1) / (total - ttft) as research/realmodel/bench_int8.py
-  step_roofline  algorithmic bytes per token (weights + scales + norms + embedding row + KV at each step's
-               context) / step time, against the measured HBM copy bandwidth
-  roofline     the dominant kernel. Persistent step (default on this shape): decode_step_kernel, one launch
-               per token, so achieved = algorithmic bytes per token / (device time / K); traffic = its ncu
-               dram bytes per launch from the committed summary. Launch sequence: the step's GEMV launches
-               replayed alone as one PDL-chained graph (gemv_i8_kernel).
-  gemv_chain   the GEMV launches of the launch-sequence path replayed alone (for comparison)
+  roofline     decode_step_kernel, one launch per token: achieved = algorithmic bytes per token (weights, scales,
+               norms, embedding row, KV at each timed step's context) / (device time / K) against the measured
+               HBM copy bandwidth; traffic = its ncu dram bytes per launch (profiles/decode_step_kernel_traffic.json)
   cpu_baseline the reference's CPU path (oracle/torch_ref.py) on this host's cores, bounded sample
-With N > 1 (torchrun, one rank per GPU) the default workload is BASELINE config 5, the model the reference's north
-star shards: Qwen3-8B shape, 4096-token prompt fed through the step, 256 greedy tokens, tensor-parallel over the N
-GPUs (efficientgpt_b200.tp: one persistent kernel per GPU and token, o_proj / down_proj partial sums exchanged over
-NVLink inside it; scaling "strong"). --workload selects either model at any N (qwen3_8b on one GPU runs the
-launch sequence: its 12288-wide MLP does not fit the persistent kernel's shared memory); --replicas runs N
-independent one-GPU replicas of config 2 instead (scaling "weak").
+With N > 1 (torchrun, one rank per GPU) the same workload runs as N independent replicas (scaling "weak": the value
+is the tokens of all ranks per second), so every N measures the same thing; the line adds `tensor_parallel`, BASELINE
+config 5 (Qwen3-8B shape, 4096-token prompt, 256 tokens) sharded over the N GPUs (efficientgpt_b200.tp: one
+persistent kernel per GPU and token, o_proj / down_proj partial sums exchanged over NVLink inside it).
+
+--impl reference times the reference's CPU decode path (oracle/torch_ref.py: the seeded model built, quantised
+and prefilled on the CPU, no GPU and no library of this package) for the same K steps on rank 0.
+
+Other workloads: --workload qwen3_8b (config 5 at any N), nanogpt (config 1), gemv_sweep / attn_sweep (configs 3
+and 4, one JSON line per case), profile_step (a small engine for ncu captures: --layers, --steps).
 """
 import argparse
 import json
+import math
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -44,29 +47,32 @@ ROOT = Path(__file__).resolve().parent
 METRIC = 'batch-1 decode tok/s and % of HBM roofline, Qwen3-1.7B-shape int8, 1 B200'
 PROMPT_LEN, NEW_TOKENS = 32, 256
 FALLBACK_PEAKS = {'hbm_gbs': 6650.0}
-PROFILE_SUMMARY = ROOT / 'profiles' / 'decode_step_kernel_qwen3_1p7b.md'
+TRAFFIC_FILE = ROOT / 'profiles' / 'decode_step_kernel_traffic.json'
+L2_BYTES = 126 * 2 ** 20
+REF_MAX_STEPS = 512  # the reference arm's CPU steps are ~0.3 s each: bound the run to a few minutes
 
 
-def parse():
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=2048)
-    ap.add_argument('--warmup', type=int, default=16)
+    ap.add_argument('--steps', type=int, default=256)
+    ap.add_argument('--warmup', type=int, default=8)
     ap.add_argument('--impl', choices=['ours', 'reference'], default='ours')
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-cpu-baseline', action='store_true')
-    ap.add_argument('--no-pdl', action='store_true')
+    ap.add_argument('--no-tp', action='store_true', help='N > 1: skip the config-5 tensor-parallel measurement')
     ap.add_argument('--launch-sequence', action='store_true', help='per-stage kernels instead of the persistent step')
-    ap.add_argument('--no-gemv-chain', action='store_true', help='skip the GEMV-launches-alone comparison graph')
-    ap.add_argument('--cpu-sample', type=int, default=3, help='timed CPU decode tokens (after one warm-up token)')
-    ap.add_argument('--workload', choices=['qwen3_1.7b', 'qwen3_8b', 'nanogpt'], default=None,
-                    help='default: qwen3_1.7b (config 2) on one GPU, qwen3_8b (config 5, tensor-parallel) on N > 1')
-    ap.add_argument('--replicas', action='store_true', help='N > 1: independent replicas instead of tensor parallelism')
-    a = ap.parse_args()
+    ap.add_argument('--cpu-sample', type=int, default=16, help='timed CPU decode tokens of cpu_baseline')
+    ap.add_argument('--workload', default='qwen3_1.7b',
+                    choices=['qwen3_1.7b', 'qwen3_8b', 'nanogpt', 'gemv_sweep', 'attn_sweep', 'profile_step'])
+    ap.add_argument('--layers', type=int, default=4, help='profile_step: decoder layers')
+    ap.add_argument('--reps', type=int, default=50, help='gemv_sweep / attn_sweep: launches per graph')
+    ap.add_argument('--only', default='', help='gemv_sweep / attn_sweep: cases whose name contains this text')
+    a = ap.parse_args(argv)
     if a.warmup < 3:
         ap.error('--warmup must be >= 3')
-    if a.workload is None:
-        a.workload = 'qwen3_8b' if a.gpus > 1 and not a.replicas else 'qwen3_1.7b'
+    if a.steps < 1:
+        ap.error('--steps must be >= 1')
     return a
 
 
@@ -115,7 +121,6 @@ class ClockSampler:
 
     def __init__(self):
         self.proc = None
-        self.out = None
 
     def start(self):
         try:
@@ -153,15 +158,87 @@ class ClockSampler:
         return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': smax, 'reasons': sorted(reasons), 'samples': len(sm)}
 
 
-def profile_traffic():
-    """dram bytes read+write per launch of the dominant kernel, from the committed ncu summary (or None)."""
-    if not PROFILE_SUMMARY.exists():
+def traffic_per_launch():
+    """ncu dram bytes (read + write) per launch of decode_step_kernel at config 2, from the machine-readable
+    capture record (None when absent)."""
+    if not TRAFFIC_FILE.exists():
         return None
-    m = re.search(r'traffic_bytes_per_launch\s*[:=]\s*([0-9.eE+]+)', PROFILE_SUMMARY.read_text())
-    return float(m.group(1)) if m else None
+    rec = json.loads(TRAFFIC_FILE.read_text())
+    return rec.get('traffic_bytes_per_launch')
 
 
-def build(device, pdl, persistent=None):
+def window_positions(k, start=PROMPT_LEN, window=NEW_TOKENS):
+    """Decode positions of the K timed steps: whole windows in order when K >= window, else spread evenly."""
+    if k >= window:
+        return [start + (i % window) for i in range(k)]
+    return [start + (i * window) // k for i in range(k)]
+
+
+def time_replays(graph, k, positions=None, set_pos=None):
+    """Device time (ms) of k replays; `positions` (length k) puts the step at that position first whenever it does
+    not follow from the previous replay (set_pos runs on the same stream, inside the timed region)."""
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for i in range(k):
+        if positions is not None and (i == 0 or positions[i] != positions[i - 1] + 1):
+            set_pos(positions[i])
+        graph.replay()
+    e1.record(st)
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
+# --------------------------------------------------------------------------------------------- reference arm
+def run_reference(a, rank):
+    """The reference's CPU decode path (oracle/torch_ref.py) on this host's cores, rank 0 only: the seeded model
+    built and quantised on the CPU, the prompt prefilled on the CPU (the op's > 16-row branch), W untimed and K timed
+    decode tokens (at most REF_MAX_STEPS). Neither the product package nor its library is loaded."""
+    if rank != 0:
+        return
+    from oracle.torch_ref import TorchCpuQwen3, cpu_model_weights, qwen3_config
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    big = a.workload == 'qwen3_8b'
+    prompt_len = 4096 if big else PROMPT_LEN
+    steps = min(a.steps, REF_MAX_STEPS)
+    t_build = time.perf_counter()
+    w = cpu_model_weights(qwen3_config('qwen3_8b' if big else 'qwen3_1.7b'), seed=0,
+                          cap=prompt_len + NEW_TOKENS + a.warmup + steps)
+    cpu = TorchCpuQwen3(w, prompt_len + NEW_TOKENS + a.warmup + steps)
+    prompt = torch.randint(0, 151936, (prompt_len,), generator=torch.Generator().manual_seed(0)).tolist()
+    tok = cpu.prefill(prompt)
+    build_s = time.perf_counter() - t_build
+    pos = prompt_len
+    for _ in range(a.warmup):
+        tok = cpu.step(tok, pos)
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        tok = cpu.step(tok, pos)
+        pos += 1
+    dt = time.perf_counter() - t0
+    v = steps / dt
+    sample = (f'{steps} decode tokens after {a.warmup} untimed ones, contexts {prompt_len + a.warmup + 2}..'
+              f'{prompt_len + a.warmup + steps + 1}; seeded model built, quantised and prefilled on the CPU '
+              f'({build_s:.0f} s, untimed); torch CPU ops, bf16((x.float() @ q.float().T) * s) per linear')
+    cb = {'value': v, 'unit': 'tok/s', 'cores': threads, 'kind': 'port', 'sample': sample}
+    metric = METRIC if not big else METRIC.replace('Qwen3-1.7B', 'Qwen3-8B').replace('1 B200', f'{a.gpus} B200')
+    line = {'impl': 'reference', 'metric': metric, 'value': v, 'unit': 'tok/s', 'n_gpus': a.gpus, 'steps': steps,
+            'warmup': a.warmup, 'ms_per_step': 1e3 / v, 'higher_is_better': True,
+            'scaling': 'strong' if big else 'weak', 'vs_baseline': None, 'dtype': 'int8-weight/bf16',
+            'data': 'synthetic',
+            'config': {'workload': ('qwen3_8b int8 decode, BASELINE config 5' if big else
+                                    'qwen3_1.7b int8 decode, BASELINE config 2') + ' (CPU port of the reference path)',
+                       'prompt': prompt_len, 'new_tokens': NEW_TOKENS, 'scale_dtype': 'bf16',
+                       'init': 'HF random init N(0,0.02) on the CPU, seed 0'},
+            'cpu_baseline': cb, 'e2e': {'value': v, 'unit': 'tok/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------------------------- config 2
+def build(device, pdl=True, persistent=None):
     from efficientgpt_b200.configs import qwen3_1p7b_config, random_model
     from efficientgpt_b200.fast_decode import GraphGreedyDecoder
     from efficientgpt_b200.int8_linear import quantize_model
@@ -173,70 +250,15 @@ def build(device, pdl, persistent=None):
     return model, dec, prompt
 
 
-def gemv_chain_graph(eng):
-    """A graph with only the step's GEMV launches (same shapes, weights and buffers, PDL-chained)."""
-    from efficientgpt_b200 import _lib as L, ops
-    H, I = eng.hidden, eng.inter
-    x_h = eng.h.view(1, H)
-    qkv = eng.qkv.view(1, -1)
-    attn = eng.attn.view(1, -1)
-    act = eng.act.view(1, I)
-
-    def chain():
-        for lay in eng.layers:
-            ops.gemv_i8(x_h, lay['w_qkv'], lay['s_qkv'], out=qkv, norm_w=lay['ln_in'], eps=eng.eps, pdl=True)
-            ops.gemv_i8(attn, lay['w_o'], lay['s_o'], epilogue=L.EPI_RESIDUAL, residual=x_h, pdl=True)
-            ops.gemv_i8(x_h, lay['w_gu'], lay['s_gu'], out=act, epilogue=L.EPI_SILU_MUL, norm_w=lay['ln_post'],
-                        eps=eng.eps, pdl=True)
-            ops.gemv_i8(act, lay['w_down'], lay['s_down'], epilogue=L.EPI_RESIDUAL, residual=x_h, pdl=True)
-        ops.lm_head_argmax(eng.h, eng.w_lm, eng.s_lm, eng.lm_ws, norm_w=eng.final_norm, eps=eng.eps, token=eng.token,
-                           pdl=True)
-
-    s = torch.cuda.Stream()
-    s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        for _ in range(2):
-            chain()
-    torch.cuda.current_stream().wait_stream(s)
-    torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        chain()
-    nbytes = 0
-    for lay in eng.layers:
-        for w, s_ in (('w_qkv', 's_qkv'), ('w_o', 's_o'), ('w_gu', 's_gu'), ('w_down', 's_down')):
-            n, k = lay[w].shape
-            nbytes += n * k + n * lay[s_].element_size() + 2 * k + 2 * n
-        nbytes += 2 * lay['ln_in'].numel() + 2 * lay['ln_post'].numel() + 2 * H + 2 * H  # norm weights, residual rw
-    nbytes += eng.w_lm.numel() + eng.s_lm.numel() * eng.s_lm.element_size() + 2 * H * 2
-    return g, nbytes, 4 * len(eng.layers) + 1
-
-
-def time_replays(graph, k, reset=None, window=NEW_TOKENS):
-    st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    e0.record(st)
-    for i in range(k):
-        if reset is not None and i and i % window == 0:
-            reset()
-        graph.replay()
-    e1.record(st)
-    e1.synchronize()
-    return e0.elapsed_time(e1)
-
-
 def cpu_baseline(dec, n_tokens):
-    """The reference's CPU decode path (oracle/torch_ref.py) on this host: 1 warm-up + n_tokens timed steps at
-    the contexts right after the 32-token prompt (KV of the prompt copied from the GPU prefill)."""
+    """The reference's CPU decode path (oracle/torch_ref.py) on this host with the timed engine's weights: the
+    prompt prefilled on the CPU, 1 warm-up + n_tokens timed decode steps right after it."""
     from oracle.torch_ref import TorchCpuQwen3
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    eng = dec.engine
-    cpu = TorchCpuQwen3(eng, PROMPT_LEN + n_tokens + 2)
-    cpu.k[:, 0, :, :PROMPT_LEN] = eng.kv[:, 0, :, :PROMPT_LEN].cpu()
-    cpu.v[:, 0, :, :PROMPT_LEN] = eng.kv[:, 1, :, :PROMPT_LEN].cpu()
-    tok = int(eng.token)
+    cpu = TorchCpuQwen3.from_engine(dec.engine, PROMPT_LEN + n_tokens + 2)
+    prompt = torch.randint(0, dec.engine.vocab, (PROMPT_LEN,), generator=torch.Generator().manual_seed(0)).tolist()
+    tok = cpu.prefill(prompt)
     tok = cpu.step(tok, PROMPT_LEN)
     t0 = time.perf_counter()
     for i in range(n_tokens):
@@ -248,88 +270,100 @@ def cpu_baseline(dec, n_tokens):
                       f'bf16((x.float() @ q.float().T) * s) per linear'}
 
 
-class _CpuWeights:
-    """The attributes oracle/torch_ref.TorchCpuQwen3 reads, from tp.full_weights of a quantised model."""
+def run_config2(a, world, rank, local):
+    """Config 2 on every rank (N independent replicas at N > 1); returns rank 0's line (None elsewhere)."""
+    model, dec, prompt = build('cuda', persistent=False if a.launch_sequence else None)
+    eng = dec.engine
+    dec._capture()
+    eng.prefill(prompt.cuda())
 
-    def __init__(self, model):
-        from efficientgpt_b200 import tp
-        c = model.config
-        shape = tp.Qwen3Shape.from_config(c)
-        full = tp.full_weights(model)
-        self.nq, self.nkv, self.d, self.eps = shape.nq, shape.nkv, shape.d, shape.eps
-        self.hidden, self.inter = shape.hidden, shape.inter
-        self.layers = full['layers']
-        self.embed, self.final_norm, self.w_lm, self.s_lm = full['embed'], full['final_norm'], full['w_lm'], full['s_lm']
-        self.rope_cos, self.rope_sin = tp.rope_tables(shape, 4096 + NEW_TOKENS, model.device, full['rotary'])
+    def set_pos(p):
+        eng.position.fill_(p)
 
+    # warm-up, then one whole window (every KV row of contexts 33..288 written), then the timed region
+    time_replays(dec.graph, a.warmup, window_positions(a.warmup), set_pos)
+    set_pos(PROMPT_LEN)
+    time_replays(dec.graph, NEW_TOKENS)
+    positions = window_positions(a.steps)
+    barrier(world)
+    torch.cuda.synchronize()
+    sampler = ClockSampler()
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+    ms = time_replays(dec.graph, a.steps, positions, set_pos)
+    clocks = sampler.stop(local) if rank == 0 else None
+    ms = max_over_ranks(ms, world)
+    barrier(world)
+    from efficientgpt_b200._lib import device_error
+    err = device_error()
+    tok_s = a.steps / (ms / 1e3) * world
 
-def run_reference_8b(a, world, rank):
-    """The reference's CPU decode path on the config-5 model: a bounded sample of decode steps at context
-    4097.. with the 4096 prompt positions of the KV cache filled from a seeded draw (a CPU prefill of 4096 tokens
-    through an 8B model would take far longer than the run allows)."""
-    if rank != 0:
-        return
-    from oracle.torch_ref import TorchCpuQwen3
-    from efficientgpt_b200.configs import qwen3_8b_config, random_model
-    from efficientgpt_b200.int8_linear import quantize_model
-    model = random_model(qwen3_8b_config(), 'cuda', seed=0)
-    quantize_model(model, scale_dtype=torch.bfloat16)
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    n = max(1, min(a.steps, a.cpu_sample))
-    cpu = TorchCpuQwen3(_CpuWeights(model), 4096 + n + 2)
-    del model
-    g = torch.Generator().manual_seed(0)
-    cpu.k[:, :, :, :4096].copy_(torch.randn(cpu.k[:, :, :, :4096].shape, generator=g).to(torch.bfloat16))
-    cpu.v[:, :, :, :4096].copy_(torch.randn(cpu.v[:, :, :, :4096].shape, generator=g).to(torch.bfloat16))
-    tok = cpu.step(11, 4096)
-    t0 = time.perf_counter()
-    for i in range(n):
-        tok = cpu.step(tok, 4097 + i)
-    v = n / (time.perf_counter() - t0)
-    cb = {'value': v, 'unit': 'tok/s', 'cores': threads, 'kind': 'port',
-          'sample': f'{n} decode tokens (after 1 warm-up token) of the Qwen3-8B-shape int8 model at context '
-                    f'4098..{4097 + n}, KV of the 4096 prompt positions from a seeded draw, torch CPU ops, '
-                    f'bf16((x.float() @ q.float().T) * s) per linear'}
-    line = {'impl': 'reference', 'metric': METRIC.replace('Qwen3-1.7B', 'Qwen3-8B').replace('1 B200', f'{world} B200'),
-            'value': v, 'unit': 'tok/s', 'n_gpus': world, 'steps': n, 'warmup': 1, 'ms_per_step': 1e3 / v,
-            'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'int8-weight/bf16',
-            'data': 'synthetic',
-            'config': {'workload': 'qwen3_8b int8 decode, BASELINE config 5 (CPU port of the reference path)',
-                       'prompt': 4096, 'new_tokens': NEW_TOKENS, 'scale_dtype': 'bf16'},
-            'cpu_baseline': cb, 'e2e': {'value': v, 'unit': 'tok/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
-    print(json.dumps(line), flush=True)
+    # algorithmic bytes per token over the timed steps (context = position + 1 keys)
+    kv_mean = statistics.fmean(eng.kv_bytes_per_token(p + 1) for p in positions)
+    bytes_tok = eng.weight_bytes() + kv_mean
+    peaks, peak_src = measured_peaks()
+    hbm = float(peaks['hbm_gbs'])
+    gbs = bytes_tok / (ms / 1e3 / a.steps) / 1e9
+    launches_per_step = 1 if eng.persistent else 5 * eng.n_layers + 1
+    roofline = {'bound': 'hbm', 'kernel': 'decode_step_kernel' if eng.persistent else 'gemv_tc_kernel (step)',
+                'achieved': round(gbs, 1), 'peak': hbm, 'unit': 'GB/s', 'frac': round(gbs / hbm, 4),
+                'traffic': traffic_per_launch() if eng.persistent else None, 'launches_per_step': launches_per_step,
+                'bytes_per_launch': round(bytes_tok / launches_per_step),
+                'avg_launch_us': round(ms * 1e3 / a.steps / launches_per_step, 3), 'peak_source': peak_src,
+                'mean_context': round(statistics.fmean(p + 1 for p in positions), 1)}
 
+    e2e = None
+    if not a.no_e2e:
+        host_prompt = prompt.pin_memory()
+        vals = []
+        for _ in range(3):
+            out, st = dec.generate(host_prompt, NEW_TOKENS)
+            vals.append((st['tokens'] - 1) / (st['total_s'] - st['ttft_s']))
+        e2e_v = max_over_ranks(-statistics.median(vals), world)  # the slowest rank's rate, times the ranks
+        e2e = {'value': -e2e_v * world, 'unit': 'tok/s', 'h2d_bytes_per_step': PROMPT_LEN * 8 / NEW_TOKENS,
+               'd2h_bytes_per_step': 8, 'ttft_ms': round(st['ttft_s'] * 1e3, 3),
+               'api': 'efficientgpt_b200.GraphGreedyDecoder.generate (pinned host prompt, 256 new tokens)'}
 
-def run_reference(a, world, rank):
-    if a.workload == 'qwen3_8b':
-        run_reference_8b(a, world, rank)
-        return
-    if rank != 0:
-        return
-    _, dec, _ = build('cuda', pdl=True)
-    dec.engine.prefill(torch.randint(0, dec.engine.vocab, (1, PROMPT_LEN),
-                                     generator=torch.Generator().manual_seed(0)).cuda())
-    n = max(1, min(a.steps, a.cpu_sample))
-    cb = cpu_baseline(dec, n)
-    line = {'impl': 'reference', 'metric': METRIC, 'value': cb['value'], 'unit': 'tok/s', 'n_gpus': a.gpus,
-            'steps': n, 'warmup': 1, 'ms_per_step': 1e3 / cb['value'], 'higher_is_better': True, 'scaling': 'weak',
+    cb = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cb = cpu_baseline(dec, a.cpu_sample)
+    line = None
+    if rank == 0:
+        line = {
+            'metric': METRIC if world == 1 else METRIC.replace('1 B200', f'{world} B200 (independent replicas)'),
+            'value': round(tok_s, 2), 'unit': 'tok/s', 'n_gpus': world, 'steps': a.steps,
+            'warmup': a.warmup, 'ms_per_step': round(ms / a.steps, 5), 'higher_is_better': True, 'scaling': 'weak',
             'vs_baseline': None, 'dtype': 'int8-weight/bf16', 'data': 'synthetic',
-            'config': {'workload': 'qwen3_1.7b int8 decode, BASELINE config 2 (CPU port of the reference path)',
-                       'prompt': PROMPT_LEN, 'new_tokens': NEW_TOKENS, 'scale_dtype': 'bf16'},
-            'cpu_baseline': cb, 'e2e': {'value': cb['value'], 'unit': 'tok/s', 'h2d_bytes_per_step': 0,
-                                        'd2h_bytes_per_step': 0}}
-    print(json.dumps(line), flush=True)
+            'config': {'workload': 'qwen3_1.7b int8 decode, BASELINE config 2', 'prompt': PROMPT_LEN,
+                       'new_tokens': NEW_TOKENS, 'scale_dtype': 'bf16', 'init': 'HF random init N(0,0.02), seed 0',
+                       'parallelism': f'replicas{world}' if world > 1 else 'single',
+                       'timed_positions': 'whole windows' if a.steps >= NEW_TOKENS else
+                       f'{a.steps} positions spread over {PROMPT_LEN}..{PROMPT_LEN + NEW_TOKENS - 1}',
+                       'l2': 'no flush: 1.72 GB of weights streamed per step, larger than L2',
+                       'step': 'persistent' if eng.persistent else 'launch sequence'},
+            'tok_s_per_gpu': round(tok_s / world, 2),
+            'roofline': roofline,
+            'device_error': err,
+            'e2e': e2e,
+            'cpu_baseline': cb,
+            'gpu_launches': a.steps * launches_per_step,
+            'clocks': clocks,
+        }
+    del dec, model
+    torch.cuda.empty_cache()
+    return line
 
 
-def run_tp(a, world, rank, local):
+# --------------------------------------------------------------------------------------------- config 5 / TP
+def run_tp(a, world, rank, local, workload='qwen3_8b'):
     """Tensor-parallel decode over the `world` GPUs (world 1: the same engine on one GPU): K timed replays of a
     graph holding one step, device time max over ranks; every rank builds the same seeded model and keeps its
-    shard."""
+    shard. Returns rank 0's line (None elsewhere)."""
     from efficientgpt_b200 import tp
     from efficientgpt_b200.configs import qwen3_1p7b_config, qwen3_8b_config, random_model
     from efficientgpt_b200.int8_linear import quantize_model
-    big = a.workload == 'qwen3_8b'
+    big = workload == 'qwen3_8b'
     prompt_len = 4096 if big else PROMPT_LEN
     cfg = qwen3_8b_config() if big else qwen3_1p7b_config()
     dev = torch.device('cuda', local)
@@ -355,19 +389,23 @@ def run_tp(a, world, rank, local):
     with torch.cuda.graph(graph):
         eng.step()
 
-    def reset():
-        eng.position.fill_(prompt_len)
+    def set_pos(p):
+        eng.position.fill_(p)
 
-    reset()
-    time_replays(graph, a.warmup)
-    reset()
+    set_pos(prompt_len)
+    barrier(world)
+    time_replays(graph, a.warmup, window_positions(a.warmup, prompt_len), set_pos)
+    set_pos(prompt_len)
+    barrier(world)
+    time_replays(graph, NEW_TOKENS)
+    positions = window_positions(a.steps, prompt_len)
     sampler = ClockSampler()
     if rank == 0:
         sampler.start()
         time.sleep(0.3)
     torch.cuda.synchronize(dev)
     barrier(world)  # after the sampler's start-up: the ranks' kernels wait on one another with a bounded wait
-    ms = time_replays(graph, a.steps, reset)
+    ms = time_replays(graph, a.steps, positions, set_pos)
     clocks = sampler.stop(local) if rank == 0 else None
     ms = max_over_ranks(ms, world)
     barrier(world)
@@ -375,12 +413,11 @@ def run_tp(a, world, rank, local):
     err = device_error()
     tok_s = a.steps / (ms / 1e3)  # one token per step for the whole job (all ranks decode the same token)
 
-    ctxs = [prompt_len + 1 + (i % NEW_TOKENS) for i in range(a.steps)]
-    bytes_rank = eng.weight_bytes() + statistics.fmean(eng.kv_bytes_per_token(c) for c in ctxs)
+    bytes_rank = eng.weight_bytes() + statistics.fmean(eng.kv_bytes_per_token(p + 1) for p in positions)
     peaks, peak_src = measured_peaks()
     hbm = float(peaks['hbm_gbs'])
     gbs = bytes_rank / (ms / 1e3 / a.steps) / 1e9
-    nvlink = 2 * shape.n_layers * shape.hidden * 8 * (world - 1) + 8 * (world - 1) if world > 1 else 0
+    nvlink = 2 * shape.n_layers * shape.hidden * 16 * (world - 1) + 16 * (world - 1) if world > 1 else 0
 
     # end to end through the engine's public API: pinned host prompt in, every token read back to the host
     e2e = None
@@ -402,8 +439,9 @@ def run_tp(a, world, rank, local):
         dt = max_over_ranks(t2 - t1, world)
         e2e = {'value': (NEW_TOKENS - 1) / dt, 'unit': 'tok/s', 'h2d_bytes_per_step': prompt_len * 8 / NEW_TOKENS,
                'd2h_bytes_per_step': 8, 'ttft_ms': round((t1 - t0) * 1e3, 3),
-               'api': 'efficientgpt_b200.tp.TPQwen3Engine.feed (pinned host prompt: GEMM prefill beyond 64 tokens, '
-                      'token by token below), then one graph replay and one token read per step'}
+               'api': 'efficientgpt_b200.tp.TPQwen3Engine.feed (pinned host prompt), then one graph replay and one '
+                      'token read per step'}
+    line = None
     if rank == 0:
         wl = ('qwen3_8b int8 decode, BASELINE config 5' if big else 'qwen3_1.7b int8 decode, BASELINE config 2')
         line = {
@@ -416,7 +454,7 @@ def run_tp(a, world, rank, local):
                        'parallelism': f'tp{world}' if world > 1 else 'single',
                        'l2': f'no flush: {bytes_rank / 1e9:.2f} GB streamed per step per GPU, larger than L2',
                        'step': 'persistent' if eng.persistent else 'launch sequence'},
-            'roofline': {'bound': 'hbm', 'kernel': 'decode_step_kernel' if eng.persistent else 'gemv_i8_kernel',
+            'roofline': {'bound': 'hbm', 'kernel': 'decode_step_kernel' if eng.persistent else 'gemv_tc_kernel (step)',
                          'achieved': round(gbs, 1), 'peak': hbm, 'unit': 'GB/s', 'frac': round(gbs / hbm, 4),
                          'traffic': None, 'launches_per_step': 1 if eng.persistent else 5 * shape.n_layers + 1,
                          'bytes_per_launch': round(bytes_rank), 'avg_launch_us': round(ms * 1e3 / a.steps, 3),
@@ -428,15 +466,14 @@ def run_tp(a, world, rank, local):
             'gpu_launches': a.steps * (1 if eng.persistent else 5 * shape.n_layers + 1),
             'clocks': clocks,
         }
-        print(json.dumps(line), flush=True)
     del graph
     eng.close()
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+    torch.cuda.empty_cache()
+    return line
 
 
-def run_nanogpt(a, world, rank):
+# --------------------------------------------------------------------------------------------- config 1
+def run_nanogpt(a, rank):
     """the nanoGPT decode step (one CUDA graph per token) over the contexts 65..128 window, and
     the oracle's numpy restatement of the reference CPU path for a bounded sample. Rank 0 only."""
     if rank != 0:
@@ -452,12 +489,13 @@ def run_nanogpt(a, world, rank):
     eng = dec.engine.engine
     dec.engine.reset(prompt.cuda())
 
-    def reset():
-        eng.position.fill_(64)
+    def set_pos(p):
+        eng.position.fill_(p)
 
-    time_replays(dec.graph, a.warmup)
-    reset()
-    ms = time_replays(dec.graph, a.steps, reset, window=64)
+    time_replays(dec.graph, a.warmup, window_positions(a.warmup, 64, 64), set_pos)
+    set_pos(64)
+    positions = window_positions(a.steps, 64, 64)
+    ms = time_replays(dec.graph, a.steps, positions, set_pos)
     bytes_tok = sum(b.numel() * b.element_size() for b in model.buffers() if b.dtype in (torch.int8, torch.float32))
     peaks, peak_src = measured_peaks()
     hbm = float(peaks['hbm_gbs'])
@@ -511,110 +549,146 @@ def run_nanogpt(a, world, rank):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------------------------- configs 3 and 4
+def _time_graph(fn, reps):
+    """us per launch of `fn(i)` captured `reps` times in one graph, replayed 5 times (CUDA events)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(3):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(reps):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        g.replay()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / (5 * reps) * 1e3
+
+
+def run_gemv_sweep(a):
+    """each (N, K) as a graph of `reps` launches over enough weight copies that one pass exceeds
+    L2 (every launch reads HBM); CUDA-core kernel and the exact tensor-core kernel, alone and PDL-chained.
+    Algorithmic bytes N*K + 2N (bf16 scales) + 2K (x) + 2N (out)."""
+    from efficientgpt_b200 import ops
+    peaks, src = measured_peaks()
+    peak = float(peaks['hbm_gbs'])
+    for n, k, what in ((4096, 2048, 'qkv'), (2048, 2048, 'o'), (12288, 2048, 'gate_up'), (2048, 6144, 'down'),
+                       (151936, 2048, 'lm_head')):
+        if a.only not in f'config 3 {what}':
+            continue
+        g = torch.Generator(device='cuda').manual_seed(0)
+        copies = max(1, math.ceil(2 * L2_BYTES / (n * k)))
+        ws = [torch.randint(-127, 128, (n, k), dtype=torch.int8, device='cuda', generator=g) for _ in range(copies)]
+        s = (torch.rand(n, device='cuda', generator=g) * 0.019 + 0.001).to(torch.bfloat16)
+        x = torch.randn(1, k, device='cuda', generator=g).to(torch.bfloat16)
+        out = torch.empty(1, n, dtype=torch.bfloat16, device='cuda')
+        nbytes = n * k + 2 * n + 2 * k + 2 * n
+        f = lambda t: round(nbytes / (t * 1e-6) / 1e9 / peak, 4)
+        res = {}
+        for name, kw in (('alu', {}), ('alu_pdl', {'pdl': True}), ('exact', {'exact': True}),
+                         ('exact_pdl', {'exact': True, 'pdl': True})):
+            res[name] = _time_graph(lambda i: ops.gemv_i8(x, ws[i % copies], s, out=out, **kw), a.reps)
+        print(json.dumps({'kernel': 'gemv_i8_kernel / gemv_tc_kernel', 'case': f'config 3 {what} N={n} K={k}',
+                          'bytes': nbytes, 'peak_gbs': peak, 'peak_source': src, 'l2': f'{copies} weight copies rotated',
+                          **{f'us_{m}': round(t, 3) for m, t in res.items()},
+                          **{f'frac_{m}': f(t) for m, t in res.items()}}), flush=True)
+        del ws
+
+
+def run_attn_sweep(a):
+    """16 q / 8 kv heads of 128, one query, L in {512, 2048, 8192, 32768}; graphs of `reps`
+    launches over enough cache copies to exceed L2. Algorithmic bytes 4096 L + 8192."""
+    from efficientgpt_b200 import ops
+    peaks, src = measured_peaks()
+    peak = float(peaks['hbm_gbs'])
+    nq, nkv, d = 16, 8, 128
+    for length in (512, 2048, 8192, 32768):
+        if a.only not in f'config 4 L={length}':
+            continue
+        g = torch.Generator(device='cuda').manual_seed(length)
+        per = 2 * nkv * length * d * 2
+        copies = max(1, math.ceil(2 * L2_BYTES / per))
+        ks = [torch.randn(nkv, length, d, device='cuda', generator=g).to(torch.bfloat16) for _ in range(copies)]
+        vs = [torch.randn(nkv, length, d, device='cuda', generator=g).to(torch.bfloat16) for _ in range(copies)]
+        q = torch.randn(1, nq * d, device='cuda', generator=g).to(torch.bfloat16)
+        pos = torch.tensor([length - 1], device='cuda')
+        max_split = 64
+        ws = ops.attn_ws(1, nq, nkv, d, max_split, 'cuda')
+        out = torch.empty(1, nq * d, dtype=torch.bfloat16, device='cuda')
+        for ref in (False, True):
+            us = _time_graph(lambda i: ops.attn_decode(q, ks[i % copies], vs[i % copies], pos, nq, nkv, d,
+                                                       scale=d ** -0.5, max_split=max_split, ws=ws, out=out,
+                                                       ref_softmax=ref), a.reps)
+            nbytes = 4096 * length + 8192
+            gbs = nbytes / (us * 1e-6) / 1e9
+            print(json.dumps({'kernel': 'attn_split_kernel', 'case': f'config 4 L={length}' + (' ref_softmax' if ref else ''),
+                              'us': round(us, 3), 'bytes': nbytes, 'achieved_gbs': round(gbs, 1), 'peak_gbs': peak,
+                              'frac': round(gbs / peak, 4), 'peak_source': src,
+                              'l2': f'{copies} cache copies rotated'}), flush=True)
+        del ks, vs
+
+
+def run_profile_step(a):
+    """A small decode workload for ncu captures: the Qwen3-1.7B shape with --layers decoder layers, a 32-token
+    prefill and --steps decode steps of the persistent kernel (or the launch sequence)."""
+    from efficientgpt_b200 import _lib
+    from efficientgpt_b200.configs import qwen3_1p7b_config, random_model
+    from efficientgpt_b200.engine import Qwen3Engine
+    from efficientgpt_b200.int8_linear import quantize_model
+    cfg = qwen3_1p7b_config()
+    cfg.num_hidden_layers = a.layers
+    model = random_model(cfg, 'cuda', 0)
+    quantize_model(model, scale_dtype=torch.bfloat16)
+    eng = Qwen3Engine(model, PROMPT_LEN + NEW_TOKENS, persistent=False if a.launch_sequence else None)
+    eng.prefill(torch.randint(0, cfg.vocab_size, (1, PROMPT_LEN), generator=torch.Generator().manual_seed(0)).cuda())
+    for _ in range(a.steps):
+        eng.step()
+    torch.cuda.synchronize()
+    err = _lib.device_error()
+    if err != 0:
+        raise RuntimeError(f'device error {err}')
+    print(json.dumps({'workload': 'profile_step', 'layers': a.layers, 'steps': a.steps, 'token': int(eng.token),
+                      'position': int(eng.position), 'bytes_per_step': eng.weight_bytes(),
+                      'step': 'persistent' if eng.persistent else 'launch sequence'}), flush=True)
+
+
 def main():
     a = parse()
-    world, rank, local = dist_setup()
-    if a.workload == 'nanogpt':
-        run_nanogpt(a, world, rank)
-        return
     if a.impl == 'reference':
-        run_reference(a, world, rank)
+        # the CPU path: no process group, no GPU; ranks other than 0 exit without work
+        run_reference(a, int(os.environ.get('RANK', '0')))
         return
-    if a.workload == 'qwen3_8b' or (world > 1 and not a.replicas):
-        run_tp(a, world, rank, local)
-        return
-    model, dec, prompt = build('cuda', pdl=not a.no_pdl, persistent=False if a.launch_sequence else None)
-    eng = dec.engine
-    dec._capture()
-    eng.prefill(prompt.cuda())
-
-    def reset():
-        eng.position.fill_(PROMPT_LEN)
-
-    # warm-up, then the timed region: K replays of the graph (one token each)
-    time_replays(dec.graph, a.warmup)
-    reset()
-    barrier(world)
-    torch.cuda.synchronize()
-    sampler = ClockSampler()
-    if rank == 0:
-        sampler.start()
-        time.sleep(0.3)
-    ms = time_replays(dec.graph, a.steps, reset)
-    clocks = sampler.stop(local) if rank == 0 else None
-    ms = max_over_ranks(ms, world)
-    barrier(world)
-    tok_s = a.steps / (ms / 1e3) * world
-
-    # algorithmic bytes per token over the timed window
-    ctxs = [PROMPT_LEN + 1 + (i % NEW_TOKENS) for i in range(a.steps)]
-    kv_mean = statistics.fmean(eng.kv_bytes_per_token(c) for c in ctxs)
-    bytes_tok = eng.weight_bytes() + kv_mean
-    peaks, peak_src = measured_peaks()
-    hbm = float(peaks['hbm_gbs'])
-    step_gbs = bytes_tok / (ms / 1e3 / a.steps) / 1e9
-
-    # the GEMV launches of the launch-sequence path alone
-    gemv, g = None, None
-    if not a.no_gemv_chain or not eng.persistent:
-        g, gemv_bytes, gemv_launches = gemv_chain_graph(eng)
-        reps = 64
-        time_replays(g, 4)
-        gms = time_replays(g, reps) / reps
-        gemv_gbs = gemv_bytes / (gms / 1e3) / 1e9
-        gemv = {'kernel': 'gemv_i8_kernel', 'achieved': round(gemv_gbs, 1), 'peak': hbm, 'unit': 'GB/s',
-                'frac': round(gemv_gbs / hbm, 4), 'launches_per_step': gemv_launches, 'bytes_per_step': gemv_bytes,
-                'avg_launch_us': round(gms * 1e3 / gemv_launches, 3)}
-    if eng.persistent:  # one launch per token: the kernel's duration is the step's device time
-        roofline = {'bound': 'hbm', 'kernel': 'decode_step_kernel', 'achieved': round(step_gbs, 1), 'peak': hbm,
-                    'unit': 'GB/s', 'frac': round(step_gbs / hbm, 4), 'traffic': profile_traffic(),
-                    'launches_per_step': 1, 'bytes_per_launch': round(bytes_tok),
-                    'avg_launch_us': round(ms * 1e3 / a.steps, 3), 'peak_source': peak_src}
-        launches = a.steps
+    world, rank, local = dist_setup()
+    single = {'nanogpt': lambda: run_nanogpt(a, rank), 'gemv_sweep': lambda: run_gemv_sweep(a),
+              'attn_sweep': lambda: run_attn_sweep(a), 'profile_step': lambda: run_profile_step(a)}
+    if a.workload in single:
+        if rank == 0:
+            single[a.workload]()
+        line = None
+    elif a.workload == 'qwen3_8b':
+        line = run_tp(a, world, rank, local, 'qwen3_8b')
     else:
-        roofline = dict(gemv, bound='hbm', traffic=None, peak_source=peak_src)
-        launches = a.steps * (5 * eng.n_layers + 1)
-
-    e2e = None
-    if not a.no_e2e:
-        reset()
-        host_prompt = prompt.pin_memory()
-        vals = []
-        for _ in range(3):
-            out, st = dec.generate(host_prompt, NEW_TOKENS)
-            vals.append((st['tokens'] - 1) / (st['total_s'] - st['ttft_s']))
-        e2e = {'value': statistics.median(vals) * world, 'unit': 'tok/s', 'h2d_bytes_per_step': PROMPT_LEN * 8 / NEW_TOKENS,
-               'd2h_bytes_per_step': 8, 'ttft_ms': round(st['ttft_s'] * 1e3, 3),
-               'api': 'efficientgpt_b200.GraphGreedyDecoder.generate (pinned host prompt, 256 new tokens)'}
-
-    cb = None
-    if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        cb = cpu_baseline(dec, a.cpu_sample)
-
-    if rank == 0:
-        line = {
-            'metric': METRIC, 'value': round(tok_s, 2), 'unit': 'tok/s', 'n_gpus': world, 'steps': a.steps,
-            'warmup': a.warmup, 'ms_per_step': round(ms / a.steps, 5), 'higher_is_better': True, 'scaling': 'weak',
-            'vs_baseline': None, 'dtype': 'int8-weight/bf16', 'data': 'synthetic',
-            'config': {'workload': 'qwen3_1.7b int8 decode, BASELINE config 2', 'prompt': PROMPT_LEN,
-                       'new_tokens': NEW_TOKENS, 'scale_dtype': 'bf16', 'init': 'HF random init N(0,0.02), seed 0',
-                       'parallelism': f'replicas{world}' if world > 1 else 'single',
-                       'l2': 'no flush: 1.72 GB of weights streamed per step, larger than L2',
-                       'pdl': not a.no_pdl, 'step': 'persistent' if eng.persistent else 'launch sequence'},
-            'tok_s_per_gpu': round(tok_s / world, 2),
-            'step_roofline': {'bound': 'hbm', 'bytes_per_token': round(bytes_tok), 'achieved': round(step_gbs, 1),
-                              'peak': hbm, 'unit': 'GB/s', 'frac': round(step_gbs / hbm, 4), 'peak_source': peak_src},
-            'roofline': roofline,
-            'gemv_chain': gemv,
-            'e2e': e2e,
-            'cpu_baseline': cb,
-            'gpu_launches': launches,
-            'clocks': clocks,
-        }
+        line = run_config2(a, world, rank, local)
+        if world > 1 and not a.no_tp:
+            tp_line = run_tp(a, world, rank, local, 'qwen3_8b')
+            if line is not None:
+                line['tensor_parallel'] = {k: tp_line[k] for k in ('metric', 'value', 'unit', 'ms_per_step', 'config',
+                                                                   'roofline', 'nvlink_bytes_per_token_per_gpu',
+                                                                   'device_error', 'e2e', 'gpu_launches', 'clocks')}
+    if line is not None:
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
-        del g
+        barrier(world)
         dist.destroy_process_group()
 
 

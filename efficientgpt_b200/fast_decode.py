@@ -1,17 +1,24 @@
 """Sync-free greedy decoding with one CUDA graph per token, on the native B200 decode step.
 
-Drop-in for BagelsFun/efficientgpt research/realmodel/fast_decode.py:25-111 GraphGreedyDecoder: same
-constructor (model, max_cache_len, lookahead=8), same `generate(input_ids, max_new_tokens, eos_ids=(),
-on_token=None) -> (tokens, {'ttft_s', 'total_s', 'tokens', 'capture_s'})`, same guards (batch 1,
-max_new_tokens >= 1, prompt + new tokens <= max_cache_len) and the same host loop: per token one graph replay
-plus a non-blocking copy of the token into pinned memory and an event; tokens are emitted as their events
-complete, run-ahead is bounded by `lookahead`, EOS stops emission and run-ahead tokens are never emitted.
+Drop-in for BagelsFun/efficientgpt research/realmodel/fast_decode.py:25-111 GraphGreedyDecoder: same constructor
+(model, max_cache_len, lookahead=8), same `generate(input_ids, max_new_tokens, eos_ids=(), on_token=None) ->
+(tokens, {'ttft_s', 'total_s', 'tokens', 'capture_s'})`, the same errors (batch 1, max_new_tokens >= 1, prompt + new
+tokens <= max_cache_len) and the same streaming contract: the device runs at most `lookahead` tokens ahead of the
+host, tokens reach `on_token` in order as soon as their step has finished, EOS stops the stream and tokens computed
+past it are never emitted.
 
-What changed is the step inside the graph: instead of the Inductor-compiled HF forward, the graph holds the
-native step of Qwen3Engine (5 hand-written kernels per layer + lm_head/argmax, chained with programmatic
-dependent launch), and the prompt runs through the engine's native prefill. The model must be a transformers
+The step inside the graph is Qwen3Engine's native step: by default ONE persistent cooperative kernel per token
+(egpt_decode_step_persistent: every layer, the lm_head and the argmax, reading token and position from device
+memory and writing the next ones); models whose shapes that kernel does not cover take the per-stage launch
+sequence (egpt_decode_step). The prompt runs through the engine's native prefill. The model must be a transformers
 Qwen3 model quantised with efficientgpt_b200.quantize_model.
+
+Host side: a fixed ring of lookahead + 1 pinned int64 slots, each with one reusable CUDA event. Step i's token is
+copied into slot i mod R and the slot's event recorded; the next replay is launched before the host looks at any
+slot, so the GPU never waits for Python. A slot is rewritten only after the token it held was emitted (at most
+`lookahead` steps are pending when a new one is issued).
 """
+import collections
 import time
 
 import torch
@@ -23,73 +30,94 @@ class GraphGreedyDecoder:
     """One CUDA graph per decode step; token and position live on the device."""
 
     def __init__(self, model, max_cache_len, lookahead=8, pdl=True, persistent=None):
+        if lookahead < 0:
+            raise ValueError('lookahead must be >= 0')
         self.model, self.max_cache_len, self.lookahead = model, max_cache_len, lookahead
         self.engine = Qwen3Engine(model, max_cache_len, pdl=pdl, persistent=persistent)
         self.device = self.engine.device
         self.token = self.engine.token
         self.position = self.engine.position
-        self.host = torch.empty(max_cache_len, dtype=torch.long, pin_memory=True)
+        self.ring_size = lookahead + 1
+        self.ring = torch.zeros(self.ring_size, dtype=torch.long, pin_memory=True)
+        self.ring_events = [torch.cuda.Event() for _ in range(self.ring_size)]
         self.graph = None
 
     @torch.inference_mode()
     def _capture(self):
         eng = self.engine
         eng.reset()
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):  # warm-up outside capture (loads the module, sets kernel attributes)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):  # warm-up outside capture (loads the library, sets kernel attributes)
             for _ in range(3):
                 eng.position.zero_()
                 eng.step()
-        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             eng.step()
         eng.reset()
 
-    @torch.inference_mode()
-    def generate(self, input_ids, max_new_tokens, eos_ids=(), on_token=None):
-        p = input_ids.shape[1]
-        if input_ids.shape[0] != 1:
+    def _check(self, input_ids, max_new_tokens):
+        if input_ids.dim() != 2 or input_ids.shape[0] != 1:
             raise ValueError('GraphGreedyDecoder supports batch size 1')
         if max_new_tokens < 1:
             raise ValueError('max_new_tokens must be >= 1')
-        if p + max_new_tokens > self.max_cache_len:
+        if input_ids.shape[1] + max_new_tokens > self.max_cache_len:
             raise ValueError('prompt + max_new_tokens exceeds max_cache_len')
+
+    def _publish(self, step):
+        """Queue step's token (on the device now) into its ring slot and mark the slot with its event."""
+        slot = step % self.ring_size
+        self.ring[slot:slot + 1].copy_(self.token.view(-1), non_blocking=True)
+        self.ring_events[slot].record()
+
+    def _read(self, step):
+        slot = step % self.ring_size
+        self.ring_events[slot].synchronize()
+        return int(self.ring[slot])
+
+    @torch.inference_mode()
+    def generate(self, input_ids, max_new_tokens, eos_ids=(), on_token=None):
+        self._check(input_ids, max_new_tokens)
         capture_s = 0.0
         if self.graph is None:
             t = time.perf_counter()
             self._capture()
-            capture_s = time.perf_counter() - t
+            capture_s = time.perf_counter() - t  # reported on its own, outside the time to first token
         self.engine.reset()
-        eos = set(eos_ids)
+        stop = frozenset(eos_ids)
+        tokens, first_at = [], None
+        pending = collections.deque()  # steps whose token is queued but not yet emitted, oldest first
         t0 = time.perf_counter()
-        self.engine.prefill(input_ids.to(self.device, non_blocking=True))
-        events, out, emitted, first, launched, done = [], [], 0, None, 0, False
-        while not done:
-            self.host[launched:launched + 1].copy_(self.token.view(-1), non_blocking=True)
-            ev = torch.cuda.Event()
-            ev.record()
-            events.append(ev)
-            launched += 1
-            if launched < max_new_tokens:
-                self.graph.replay()  # computes the next token into self.token
-            while emitted < launched and (events[emitted].query() or launched - emitted > self.lookahead
-                                          or launched >= max_new_tokens):
-                events[emitted].synchronize()
-                tok = int(self.host[emitted])
-                if first is None:
-                    first = time.perf_counter()
-                out.append(tok)
-                if on_token:
-                    on_token(tok)
-                emitted += 1
-                if tok in eos:
-                    done = True
+        self.engine.prefill(input_ids.to(self.device, non_blocking=True))  # leaves step 0's token on the device
+
+        def emit(step):
+            nonlocal first_at
+            tok = self._read(step)
+            if first_at is None:
+                first_at = time.perf_counter()
+            tokens.append(tok)
+            if on_token:
+                on_token(tok)
+            return tok in stop
+
+        finished = False
+        for step in range(max_new_tokens):
+            self._publish(step)
+            pending.append(step)
+            if step + 1 < max_new_tokens:
+                self.graph.replay()  # step + 1's token, computed while the host emits
+            # emit every finished step; block on the oldest once the device is `lookahead` steps ahead
+            while pending and (len(pending) > self.lookahead or self.ring_events[pending[0] % self.ring_size].query()):
+                if emit(pending.popleft()):
+                    finished = True
                     break
-            if launched >= max_new_tokens and emitted >= launched:
-                done = True
+            if finished:
+                break
+        while not finished and pending:
+            finished = emit(pending.popleft())
         torch.cuda.synchronize()
-        return out, {'ttft_s': first - t0, 'total_s': time.perf_counter() - t0, 'tokens': len(out),
-                     'capture_s': capture_s}
+        return tokens, {'ttft_s': first_at - t0, 'total_s': time.perf_counter() - t0, 'tokens': len(tokens),
+                        'capture_s': capture_s}

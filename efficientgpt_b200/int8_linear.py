@@ -64,40 +64,56 @@ def quantize_weight(weight, scale_dtype=torch.float32):
 
 
 class Int8Linear(nn.Module):
+    """A frozen linear layer stored as int8 rows: buffers `qweight` int8 [out, in] and `scale` [out] (fp32, or bf16
+    with scale_dtype=torch.bfloat16), plus the source layer's bias (frozen) when it has one. The forward is the
+    custom op, then the bias add in the activation dtype (the reference's rounding order)."""
+
     def __init__(self, linear, scale_dtype=torch.float32):
         super().__init__()
-        q, s = quantize_weight(linear.weight, scale_dtype)
-        self.in_features, self.out_features = linear.in_features, linear.out_features
-        self.register_buffer('qweight', q)
-        self.register_buffer('scale', s)
-        self.bias = None if linear.bias is None else nn.Parameter(linear.bias.detach().clone(), requires_grad=False)
+        weight, bias = linear.weight, linear.bias
+        self.out_features, self.in_features = weight.shape
+        qweight, scale = quantize_weight(weight, scale_dtype)
+        self.register_buffer('qweight', qweight)
+        self.register_buffer('scale', scale)
+        self.bias = None if bias is None else nn.Parameter(bias.detach().clone(), requires_grad=False)
 
     def forward(self, x):
         y = int8_linear(x, self.qweight, self.scale)
-        return y if self.bias is None else y + self.bias
+        if self.bias is not None:
+            y = y + self.bias
+        return y
 
     def extra_repr(self):
-        return f'in={self.in_features}, out={self.out_features}, int8 per-channel'
+        return f'{self.in_features} -> {self.out_features}, int8 rows, {str(self.scale.dtype)[6:]} scales'
+
+
+def _convert_children(module, prefix, skip, scale_dtype):
+    """Depth-first over the module tree: every nn.Linear child (but `skip`) is replaced by its Int8Linear in the
+    parent's slot as soon as it is met, so its bf16 weight is released before the next one is quantised."""
+    count = 0
+    for name in list(module._modules):
+        child = module._modules[name]
+        path = f'{prefix}.{name}' if prefix else name
+        if isinstance(child, nn.Linear):
+            if path != skip:
+                module._modules[name] = Int8Linear(child, scale_dtype)
+                count += 1
+        elif child is not None:
+            count += _convert_children(child, path, skip, scale_dtype)
+        del child
+    return count
 
 
 @torch.no_grad()
 def quantize_model(model, include_lm_head=True, scale_dtype=torch.float32):
-    """Replace every nn.Linear in the decoder layers (and the lm_head) by Int8Linear, in place. Returns the count.
-    Embeddings and norms stay bf16. A tied lm_head becomes an untied int8 copy (the embedding keeps its weight)."""
-    names = [n for n, m in model.named_modules() if isinstance(m, nn.Linear) and (include_lm_head or n != 'lm_head')]
-    count = 0
-    for full in names:
-        parent_name, _, child_name = full.rpartition('.')
-        parent = model.get_submodule(parent_name) if parent_name else model
-        child = getattr(parent, child_name)
-        setattr(parent, child_name, Int8Linear(child, scale_dtype))
-        del child
-        count += 1
-        if count % 16 == 0:
-            torch.cuda.empty_cache()
-    if hasattr(model, 'config') and include_lm_head:
+    """Replace every nn.Linear of `model` (the lm_head too unless include_lm_head=False) by Int8Linear, in place;
+    returns how many. Embeddings and norms keep their dtype. A tied lm_head becomes its own int8 copy and the config
+    is marked untied (the input embedding keeps its weight)."""
+    count = _convert_children(model, '', None if include_lm_head else 'lm_head', scale_dtype)
+    if include_lm_head and getattr(model, 'config', None) is not None:
         model.config.tie_word_embeddings = False
-    torch.cuda.empty_cache()
+    if torch.cuda.is_available():
+        torch.cuda.empty_cache()
     return count
 
 
