@@ -1,7 +1,7 @@
 """efficientgpt_b200: batch-1 int8 decode engine for NVIDIA B200 (sm_100a).
 
 Drop-in for the research/realmodel path of BagelsFun/efficientgpt: `int8_linear` (op, Int8Linear, quantize_model),
-`fast_decode.GraphGreedyDecoder`, plus `tp.TPQwen3Engine` (tensor parallelism) and `nanogpt` (config 1), with the
+`fast_decode.GraphGreedyDecoder`, `backend.BucketedGraphDecoder` (the request-sized decoder pool of HFBackend), plus `tp.TPQwen3Engine` (tensor parallelism) and `nanogpt` (config 1), with the
 arithmetic in hand-written CUDA (libegpt_b200.so, C-ABI in
 include/egpt_b200.h). Submodules import lazily so the package imports without a GPU.
 """
@@ -17,6 +17,9 @@ def __getattr__(name):
     if name == 'GraphGreedyDecoder':
         from .fast_decode import GraphGreedyDecoder
         return GraphGreedyDecoder
+    if name in ('BucketedGraphDecoder', 'pick_bucket', 'GRAPH_BUCKETS', 'MAX_GRAPH_DECODERS'):  # serving decode layer
+        from . import backend as m
+        return getattr(m, name)
     if name == 'Qwen3Engine':
         from .engine import Qwen3Engine
         return Qwen3Engine

@@ -46,7 +46,8 @@ class Qwen3Plan(ctypes.Structure):
                 ('token', P), ('position', P), ('h', P), ('qkv', P), ('attn', P), ('act', P), ('logits', P),
                 ('attn_ws', P), ('attn_ws_bytes', SZ), ('lm_ws', P), ('lm_ws_bytes', SZ),
                 ('layers_dev', P), ('sync_ws', P), ('trace', P),
-                ('tp_rank', ctypes.c_int32), ('tp_world', ctypes.c_int32), ('tp_xchg', P * 8), ('h2', P)]
+                ('tp_rank', ctypes.c_int32), ('tp_world', ctypes.c_int32), ('tp_xchg', P * 8), ('h2', P),
+                ('df_ws', P), ('df_ws_bytes', SZ)]
 
 
 # name -> (restype, argtypes)
@@ -73,6 +74,10 @@ SIGNATURES = {
     'egpt_step_sync_ws_bytes': (SZ, []),
     'egpt_decode_step_persistent': (I32, [ctypes.POINTER(Qwen3Plan), P]),
     'egpt_decode_step_persistent_check': (I32, [ctypes.POINTER(Qwen3Plan)]),
+    'egpt_dataflow_ws_bytes': (SZ, [ctypes.POINTER(Qwen3Plan)]),
+    'egpt_dataflow_prepare': (I32, [ctypes.POINTER(Qwen3Plan)]),
+    'egpt_decode_step_dataflow': (I32, [ctypes.POINTER(Qwen3Plan), P]),
+    'egpt_decode_step_dataflow_check': (I32, [ctypes.POINTER(Qwen3Plan)]),
     'egpt_tp_xchg_bytes': (SZ, [I64]),
     'egpt_tp_xchg_alloc': (I32, [ctypes.POINTER(P), SZ]),
     'egpt_tp_xchg_free': (I32, [P]),

@@ -244,8 +244,10 @@ struct RawRow {
 };
 
 // Scores of keys t0 .. t0 + nkeys - 1 (nkeys <= 32) for every head of the group: lane l reads key t0 + l's row
-// in 16-byte pieces (batches of 8 independent loads) and dots it with each q head from shared memory (broadcast
-// reads), four partial sums per head; lane l returns key t0 + l's scores (0 for lanes past nkeys).
+// in 16-byte pieces (batches of 8 independent loads), starting at piece l mod 8 and wrapping around, so that the
+// eight lanes of a shared-memory phase read eight different bank groups when the rows sit in shared memory, and
+// dots it with each q head from shared memory, four partial sums per head (dims d = m mod 4, in the lane's piece
+// order); lane l returns key t0 + l's scores (0 for lanes past nkeys).
 template <int DPL, int GRP, bool BF16>
 __device__ __forceinline__ void tile_scores(const void *K, int64_t t0, int nkeys, const AttnScratch<DPL, GRP> &S,
                                             float scale, float (&sc)[GRP]) {
@@ -260,11 +262,12 @@ __device__ __forceinline__ void tile_scores(const void *K, int64_t t0, int nkeys
   for (int j = 0; j < GRP; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
   if (lane < nkeys) {
     const uint4 *row = (const uint4 *)((const char *)K + (t0 + lane) * (int64_t)D * ESZ);
+    const int rot = lane & 7;
 #pragma unroll 1
     for (int pb = 0; pb < NP; pb += NB) {
       uint4 w[NB];
 #pragma unroll
-      for (int u = 0; u < NB; ++u) w[u] = row[pb + u];
+      for (int u = 0; u < NB; ++u) w[u] = row[(pb + u + rot) & (NP - 1)];
 #pragma unroll
       for (int u = 0; u < NB; ++u) {
         float kv[EPP];
@@ -276,7 +279,7 @@ __device__ __forceinline__ void tile_scores(const void *K, int64_t t0, int nkeys
           kv[0] = __uint_as_float(w[u].x), kv[1] = __uint_as_float(w[u].y);
           kv[2] = __uint_as_float(w[u].z), kv[3] = __uint_as_float(w[u].w);
         }
-        const int d0 = (pb + u) * EPP;
+        const int d0 = ((pb + u + rot) & (NP - 1)) * EPP;
 #pragma unroll
         for (int j = 0; j < GRP; ++j) {
 #pragma unroll

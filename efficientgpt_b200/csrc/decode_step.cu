@@ -452,7 +452,8 @@ __device__ int stage_input(const uint16_t *src, int64_t k, const NormW *nw, floa
                            uint16_t *copy_to, const TpIn *tin) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   float v[kMaxPerThread];
-  float ss = 0.f, mx = 0.f;
+  double ss = 0.0;  // the bf16 squares are exact in fp32; their fp64 sum is exact in practice and order-free
+  float mx = 0.f;
   if (TP && tin) {
 #pragma unroll
     for (int j = 0; j < kGroups; ++j) {
@@ -522,20 +523,23 @@ __device__ int stage_input(const uint16_t *src, int64_t k, const NormW *nw, floa
   }
 #pragma unroll
   for (int e = 0; e < kMaxPerThread; ++e) {
-    ss = fmaf(v[e], v[e], ss);
+    ss += (double)(v[e] * v[e]);
     mx = fmaxf(mx, fabsf(nw ? v[e] * nw->w(e) : v[e]));
   }
-  ss = warp_sum(ss);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   mx = warp_max(mx);
-  if (lane == 0) red[warp] = ss, red[kNC + warp] = mx;
+  double *redd = (double *)red;  // red: 16 doubles (bytes 0-127), then the maxima at red[32..47]
+  if (lane == 0) redd[warp] = ss, red[32 + warp] = mx;
   csync();
-  float tot = 0.f, bound = red[kNC];
+  double tot = 0.0;
+  float bound = red[32];
 #pragma unroll
-  for (int w = 0; w < kNC; ++w) tot += red[w];
+  for (int w = 0; w < kNC; ++w) tot += redd[w];
 #pragma unroll
-  for (int w = 1; w < kNC; ++w) bound = fmaxf(bound, red[kNC + w]);
+  for (int w = 1; w < kNC; ++w) bound = fmaxf(bound, red[32 + w]);
   if (nw) {
-    const float inv = rsqrtf(tot / (float)k + eps);
+    const float inv = rsqrtf((float)tot / (float)k + eps);
 #pragma unroll
     for (int e = 0; e < kMaxPerThread; ++e) v[e] = round_bf16(round_bf16(v[e] * inv) * nw->w(e));
     bound = bound * inv * 1.0079f;

@@ -5,4 +5,5 @@
 #include "gemv_i8.cu"
 #include "attention.cu"
 #include "decode_step.cu"
+#include "decode_dataflow.cu"
 #include "gemv_tc.cu"

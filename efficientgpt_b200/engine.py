@@ -1,8 +1,11 @@
 """Native batch-1 decode engine for transformers Qwen3 models quantised with `quantize_model`.
 
-Everything per token runs in libegpt_b200.so: `step()` is one call of egpt_decode_step (C++), which launches
-5 kernels per layer plus the fused final-RMSNorm/lm_head/argmax kernel, reading the current token and position
-from device memory and writing the next ones; the caller captures it in one CUDA graph.
+Everything per token runs in libegpt_b200.so: `step()` is one C-ABI call that reads the current token and
+position from device memory and writes the next ones; the caller captures it in one CUDA graph. Three steps
+with the same arithmetic: egpt_decode_step_dataflow (default: one cooperative kernel, a TMA-fed weight ring per
+SM, stage outputs exchanged as tagged LL words, no grid barrier), egpt_decode_step_persistent (one cooperative
+kernel with grid barriers; also the tensor-parallel step) and egpt_decode_step (5 kernels per layer plus the
+fused final-RMSNorm/lm_head/argmax kernel).
 
 HBM layout (all owned here, allocated once):
   w_qkv [(nq+2nkv)d, H] int8  q_proj|k_proj|v_proj rows;   w_gu [2I, H] int8  gate_proj|up_proj rows
@@ -32,10 +35,35 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
 
+def _fused(parts):
+    """The row-concatenation of `parts` (same dtype, device and trailing shape). When they already sit back to back
+    in one storage (views made by an earlier engine) the result is a view of it, else a new contiguous tensor."""
+    first = parts[0]
+    rows = sum(p.shape[0] for p in parts)
+    shape = (rows,) + tuple(first.shape[1:])
+    adjacent = all(p.is_contiguous() for p in parts) and all(
+        p.untyped_storage().data_ptr() == first.untyped_storage().data_ptr() for p in parts)
+    if adjacent:
+        off = first.storage_offset()
+        for p in parts:
+            if p.storage_offset() != off:
+                adjacent = False
+                break
+            off += p.numel()
+    if adjacent:
+        return torch.empty(0, dtype=first.dtype, device=first.device).set_(
+            first.untyped_storage(), first.storage_offset(), shape, torch.empty(shape, device='meta').stride())
+    return torch.cat(parts).contiguous()
+
+
 class Qwen3Engine:
-    def __init__(self, model, max_cache_len, pdl=True, attn_max_split=None, keep_logits=False, persistent=None):
-        """persistent: True = one cooperative kernel per token (egpt_decode_step_persistent), False = the
-        per-stage launch sequence (egpt_decode_step), None = persistent when the model's shapes allow it."""
+    def __init__(self, model, max_cache_len, pdl=True, attn_max_split=None, keep_logits=False, persistent=None,
+                 step=None):
+        """step: 'dataflow' (egpt_decode_step_dataflow: one cooperative kernel per token, TMA weight ring, LL
+        activation exchange, no grid barrier), 'persistent' (egpt_decode_step_persistent: one cooperative kernel
+        with grid barriers), 'sequence' (egpt_decode_step: per-stage launches), or None: the first of these the
+        model's shapes allow. persistent=False is step='sequence'; persistent=True asks for a one-kernel step
+        (dataflow when it fits, else persistent)."""
         if not torch.cuda.is_available():
             raise RuntimeError('Qwen3Engine needs a CUDA device (there is no CPU path)')
         self.model = model
@@ -70,13 +98,14 @@ class Qwen3Engine:
             raise ValueError('all scales must share one dtype')
         self.scale_dtype = L.EGPT_BF16 if sdt == torch.bfloat16 else L.EGPT_F32
 
-        # ---- weights: fuse q|k|v and gate|up, re-point the modules' buffers to views (no duplicate copy)
+        # ---- weights: fuse q|k|v and gate|up, re-point the modules' buffers to views (no duplicate copy; a second
+        #      engine on the same model finds the buffers already fused and shares them)
         self.layers = []
         for blk, (q, k, v, o, g, u, dn) in zip(inner.layers, lins):
-            w_qkv = torch.cat([q.qweight, k.qweight, v.qweight]).contiguous()
-            s_qkv = torch.cat([q.scale, k.scale, v.scale]).contiguous()
-            w_gu = torch.cat([g.qweight, u.qweight]).contiguous()
-            s_gu = torch.cat([g.scale, u.scale]).contiguous()
+            w_qkv = _fused([q.qweight, k.qweight, v.qweight])
+            s_qkv = _fused([q.scale, k.scale, v.scale])
+            w_gu = _fused([g.qweight, u.qweight])
+            s_gu = _fused([g.scale, u.scale])
             r0 = 0
             for lin in (q, k, v):
                 n = lin.qweight.shape[0]
@@ -121,12 +150,29 @@ class Qwen3Engine:
         self.lm_ws = ops.lm_head_ws(self.vocab, dev)
         self.sync_ws = torch.zeros(int(L.load().egpt_step_sync_ws_bytes()), dtype=torch.uint8, device=dev)
         self.pdl = pdl
+        self.df_ws = None
         self._build_plan()
-        fits = self.vocab // 2 >= nsm and L.load().egpt_decode_step_persistent_check(ctypes.byref(self.plan)) == 0
-        if persistent and not fits:
-            raise ValueError('the persistent decode step is not built for this model shape: '
-                             + L.last_error())
-        self.persistent = fits if persistent is None else bool(persistent)
+        lib = L.load()
+        fits_v1 = self.vocab // 2 >= nsm and lib.egpt_decode_step_persistent_check(ctypes.byref(self.plan)) == 0
+        msg_v1 = L.last_error()
+        fits_df = lib.egpt_decode_step_dataflow_check(ctypes.byref(self.plan)) == 0
+        msg_df = L.last_error()
+        if step is None and persistent is False:
+            step = 'sequence'
+        if step is None:
+            step = 'dataflow' if fits_df else 'persistent' if fits_v1 else 'sequence'
+            if persistent and step == 'sequence':
+                raise ValueError('no one-kernel decode step is built for this model shape: ' + msg_v1)
+        if step not in ('dataflow', 'persistent', 'sequence'):
+            raise ValueError(f'unknown step {step!r}')
+        if step == 'dataflow' and not fits_df:
+            raise ValueError('the dataflow decode step is not built for this model shape: ' + msg_df)
+        if step == 'persistent' and not fits_v1:
+            raise ValueError('the persistent decode step is not built for this model shape: ' + msg_v1)
+        self.step_kind = step
+        self.persistent = step != 'sequence'
+        if step == 'dataflow':
+            L.check(lib.egpt_dataflow_prepare(ctypes.byref(self.plan)), 'dataflow_prepare')
 
     def _build_plan(self):
         arr = (L.Qwen3Layer * self.n_layers)()
@@ -156,6 +202,9 @@ class Qwen3Engine:
         self.layers_dev = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(self.device)
         p.layers_dev = self.layers_dev.data_ptr()
         p.sync_ws = self.sync_ws.data_ptr()
+        nbytes = int(L.load().egpt_dataflow_ws_bytes(ctypes.byref(p)))
+        self.df_ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        p.df_ws, p.df_ws_bytes = self.df_ws.data_ptr(), nbytes
         self._layer_arr = arr  # keep alive
         self.plan = p
 
@@ -163,7 +212,9 @@ class Qwen3Engine:
     def step(self):
         """One decode token on the current stream: token <- argmax(model(token, position)); position += 1."""
         stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-        if self.persistent:
+        if self.step_kind == 'dataflow':
+            L.check(L.load().egpt_decode_step_dataflow(ctypes.byref(self.plan), stream), 'decode_step_dataflow')
+        elif self.step_kind == 'persistent':
             L.check(L.load().egpt_decode_step_persistent(ctypes.byref(self.plan), stream), 'decode_step_persistent')
         else:
             L.check(L.load().egpt_decode_step(ctypes.byref(self.plan), stream), 'decode_step')

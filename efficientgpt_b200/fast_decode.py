@@ -7,10 +7,10 @@ tokens <= max_cache_len) and the same streaming contract: the device runs at mos
 host, tokens reach `on_token` in order as soon as their step has finished, EOS stops the stream and tokens computed
 past it are never emitted.
 
-The step inside the graph is Qwen3Engine's native step: by default ONE persistent cooperative kernel per token
-(egpt_decode_step_persistent: every layer, the lm_head and the argmax, reading token and position from device
-memory and writing the next ones); models whose shapes that kernel does not cover take the per-stage launch
-sequence (egpt_decode_step). The prompt runs through the engine's native prefill. The model must be a transformers
+The step inside the graph is Qwen3Engine's native step: by default ONE cooperative kernel per token
+(egpt_decode_step_dataflow: every layer, the lm_head and the argmax, reading token and position from device
+memory and writing the next ones); shapes that kernel does not cover take egpt_decode_step_persistent or the
+per-stage launch sequence (egpt_decode_step). The prompt runs through the engine's native prefill. The model must be a transformers
 Qwen3 model quantised with efficientgpt_b200.quantize_model.
 
 Host side: a fixed ring of lookahead + 1 pinned int64 slots, each with one reusable CUDA event. Step i's token is
@@ -29,11 +29,11 @@ from .engine import Qwen3Engine
 class GraphGreedyDecoder:
     """One CUDA graph per decode step; token and position live on the device."""
 
-    def __init__(self, model, max_cache_len, lookahead=8, pdl=True, persistent=None):
+    def __init__(self, model, max_cache_len, lookahead=8, pdl=True, persistent=None, step=None):
         if lookahead < 0:
             raise ValueError('lookahead must be >= 0')
         self.model, self.max_cache_len, self.lookahead = model, max_cache_len, lookahead
-        self.engine = Qwen3Engine(model, max_cache_len, pdl=pdl, persistent=persistent)
+        self.engine = Qwen3Engine(model, max_cache_len, pdl=pdl, persistent=persistent, step=step)
         self.device = self.engine.device
         self.token = self.engine.token
         self.position = self.engine.position

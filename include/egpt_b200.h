@@ -227,6 +227,10 @@ typedef struct egpt_qwen3_plan {
                                    filled before the first step), mapped in this process; [tp_rank] is own */
   void *h2;                     /* tp: second bf16 [hidden] residual buffer (the layer's two residual sums
                                    alternate between h and h2)                                            */
+  /* used by egpt_decode_step_dataflow only */
+  void *df_ws;                  /* egpt_dataflow_ws_bytes(plan) bytes, 256-byte aligned, zero-filled once, then
+                                   egpt_dataflow_prepare(plan) before the first step                      */
+  size_t df_ws_bytes;
 } egpt_qwen3_plan;
 
 EGPT_API int egpt_decode_step(const egpt_qwen3_plan *plan, void *stream);
@@ -246,6 +250,24 @@ EGPT_API int egpt_decode_step(const egpt_qwen3_plan *plan, void *stream);
 EGPT_API size_t egpt_step_sync_ws_bytes(void);
 EGPT_API int egpt_decode_step_persistent(const egpt_qwen3_plan *plan, void *stream);
 EGPT_API int egpt_decode_step_persistent_check(const egpt_qwen3_plan *plan);
+
+/* Dataflow variant of egpt_decode_step_persistent (one GPU): the same arithmetic in ONE cooperative kernel with
+ * one CTA per SM and no grid barrier. Per CTA one producer warp streams the CTA's share of every weight matrix
+ * of the step (16-row x 256-column items, each as two TMA tensor loads, no multicast) into a ring of shared-memory
+ * slots guarded by mbarriers, running ahead across stage boundaries; 15 consumer warps run the stages. Every
+ * stage output (q|k|v, attention, residual stream, act) is published as LL words in plan->df_ws (two bf16 values
+ * and a 32-bit tag of step, layer and site in one 8-byte word); consumers poll the words of their input until
+ * every tag matches, so data and readiness arrive together. Every wait is bounded (EGPT_ERR_TIMEOUT via
+ * egpt_device_error). RMSNorm sums its bf16 squares in fp64 (exact in practice, independent of the thread
+ * layout). egpt_dataflow_ws_bytes: size of plan->df_ws for this plan (tensor maps, step epoch, LL words);
+ * egpt_dataflow_prepare encodes the weights' tensor maps into plan->df_ws (synchronous copy; call once after
+ * the weight pointers are set, before the first step and before any stream capture). Built for head_dim 128
+ * with 2 or 4 q heads per kv head and head_dim 32 with 2; hidden, intermediate and nq*d multiples of 64 up to
+ * 7680, vocab a multiple of 16; tp_world <= 1. egpt_decode_step_dataflow_check runs the host-side checks. */
+EGPT_API size_t egpt_dataflow_ws_bytes(const egpt_qwen3_plan *plan);
+EGPT_API int egpt_dataflow_prepare(const egpt_qwen3_plan *plan);
+EGPT_API int egpt_decode_step_dataflow(const egpt_qwen3_plan *plan, void *stream);
+EGPT_API int egpt_decode_step_dataflow_check(const egpt_qwen3_plan *plan);
 
 /* ---- tensor-parallel decode step (2, 4 or 8 GPUs of one NVLink/NVSwitch box, one process per GPU) ------
  * No counterpart in the reference (its decode runs on one GPU): the Megatron-style split of the step.

@@ -11,11 +11,14 @@ through HF's Qwen3 forward with a static cache (the GraphGreedyDecoder step of r
 replaced by its arithmetic bf16((x.float() @ q.float().T) * s) (fp32 accumulation, as make_golden.py does).
 
 Recorded per step: the token, the top-2 logit margin, the top-1 logit and the runner-up index.
+--diagnostic-only keeps the recorded greedy run and redoes the diagnostic below.
 
 Diagnostic (skipped with --no-diagnostic): the same reference forward, teacher-forced along the golden tokens,
 with only the decode GEMV's summation changed to the exact sum rounded once to fp32 (fp64 accumulation of the
 bf16 x int8 products, which it holds exactly). The steps whose argmax then differs from the golden show how many
-greedy choices of this model turn on the fp32 summation order of the int8 GEMV alone, with no other change.
+greedy choices of this model turn on the fp32 summation order of the int8 GEMV alone, with no other change; the
+logits of the golden's top-1 and runner-up tokens in that run show how far the summation order alone moves the
+decisive logits.
 """
 import argparse
 import json
@@ -45,12 +48,13 @@ def set_decode_branch(il, exact):
     il.int8_matmul = cpu_int8_matmul
 
 
-def run(model, prompt, forced=None):
+def run(model, prompt, forced=None, probe=None):
     """Greedy static-cache loop; with `forced` (token list) the input of step i + 1 is forced[i] instead of the
-    step's own argmax. Returns tokens (argmax per step), margins, top-1 logits, runner-up ids."""
+    step's own argmax. Returns tokens (argmax per step), margins, top-1 logits, runner-up ids and, with `probe` (per
+    step a list of vocabulary ids), the logits at those ids."""
     from transformers import StaticCache
     cache = StaticCache(config=model.config, max_cache_len=CAP)
-    toks, margins, tops, second = [], [], [], []
+    toks, margins, tops, second, probed = [], [], [], [], []
     p = prompt.shape[1]
     with torch.inference_mode():
         logits = model(input_ids=prompt, past_key_values=cache, use_cache=True, logits_to_keep=1).logits[0, -1]
@@ -61,6 +65,8 @@ def run(model, prompt, forced=None):
             tok = int(logits.argmax(-1))
             second.append(int(top.indices[1]) if int(top.indices[0]) == tok else int(top.indices[0]))
             toks.append(tok)
+            if probe is not None:
+                probed.append([float(logits[j]) for j in probe[i]])
             if i == N_NEW - 1:
                 break
             nxt = forced[i] if forced is not None else tok
@@ -68,13 +74,14 @@ def run(model, prompt, forced=None):
                            use_cache=True, logits_to_keep=1).logits[0, -1]
             if i % 32 == 31:
                 print(f'  step {i + 1}', flush=True)
-    return toks, margins, tops, second
+    return toks, margins, tops, second, probed
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', required=True)
     ap.add_argument('--no-diagnostic', action='store_true')
+    ap.add_argument('--diagnostic-only', action='store_true', help='keep the golden run, redo the diagnostic')
     a = ap.parse_args()
     sys.path.insert(0, a.reference)
     import research.realmodel.int8_linear as il
@@ -88,8 +95,13 @@ def main():
         if isinstance(mod, il.Int8Linear):
             mod.scale = mod.scale.to(torch.bfloat16)
     prompt = gi.big_prompt()
-    set_decode_branch(il, exact=False)
-    toks, margins, tops, second = run(model, prompt)
+    if a.diagnostic_only:
+        out = json.loads((HERE / 'qwen3_1p7b_256.json').read_text())
+        assert out['state_sha256'] == h
+        toks, margins, tops, second = out['tokens'], out['margins'], out['tops'], out['runner_up']
+    else:
+        set_decode_branch(il, exact=False)
+        toks, margins, tops, second, _ = run(model, prompt)
     out = {'reference': 'BASELINE config 2 through research/realmodel/int8_linear.quantize_model (bf16 scales), HF '
                         'Qwen3 forward with a static cache, greedy; int8 decode branch as fp32-accumulated arithmetic',
            'torch': torch.__version__, 'transformers': transformers.__version__, 'state_sha256': h,
@@ -98,12 +110,18 @@ def main():
     if not a.no_diagnostic:
         t = time.time()
         set_decode_branch(il, exact=True)
-        ex, ex_m, _, _ = run(model, prompt, forced=toks)
+        pairs = [[toks[i], second[i]] for i in range(N_NEW)]
+        ex, ex_m, _, _, probed = run(model, prompt, forced=toks, probe=pairs)
         diff = [i for i in range(N_NEW) if ex[i] != toks[i]]
+        want = [[tops[i], tops[i] - margins[i]] for i in range(N_NEW)]
+        err = [abs(p - w) for pw, ww in zip(probed, want) for p, w in zip(pw, ww)]
+        within = sum(1 for e, ww in zip(err, [w for ww in want for w in ww]) if e <= 1e-2 + 1e-2 * abs(ww)) / len(err)
         out['exact_sum_diagnostic'] = {
             'what': 'same forward teacher-forced along `tokens`, int8 decode GEMV as the exact sum rounded once',
             'steps_differing': diff, 'identical': N_NEW - len(diff),
             'golden_margins_at_differing_steps': [margins[i] for i in diff],
+            'decisive_logits': probed,
+            'decisive_logits_max_abs_diff': max(err), 'decisive_logits_within_1e-2_abs_rel': within,
             'seconds': round(time.time() - t, 1)}
     (HERE / 'qwen3_1p7b_256.json').write_text(json.dumps(out, indent=1))
     print('wrote qwen3_1p7b_256.json', out.get('exact_sum_diagnostic', {}).get('identical'))

@@ -99,3 +99,17 @@ def test_tp_exchange_size_and_guards():
     assert lib.egpt_ipc_handle(None, None) == L.EGPT_ERR_ARG
     assert lib.egpt_ipc_open(None, None) == L.EGPT_ERR_ARG
     assert lib.egpt_ipc_close(None) == L.EGPT_OK
+
+
+def test_dataflow_workspace_and_guards():
+    """egpt_dataflow_ws_bytes: 256 B of step state + the LL words of every layer (h, q|k|v, attention, mid
+    residual, act: two bf16 per 8-byte word) and the final h."""
+    lib = L.load()
+    p = L.Qwen3Plan()
+    p.n_layers, p.hidden, p.n_q_heads, p.n_kv_heads, p.head_dim, p.intermediate = 28, 2048, 16, 8, 128, 6144
+    words = 28 * (1024 + 2048 + 1024 + 1024 + 3072) + 1024
+    assert lib.egpt_dataflow_ws_bytes(ctypes.byref(p)) == 256 + 8 * words
+    assert lib.egpt_dataflow_ws_bytes(None) == 0
+    assert lib.egpt_decode_step_dataflow_check(ctypes.byref(p)) == L.EGPT_ERR_ARG  # null pointers in the plan
+    assert lib.egpt_decode_step_dataflow(None, None) == L.EGPT_ERR_ARG
+    assert lib.egpt_dataflow_prepare(None) == L.EGPT_ERR_ARG
