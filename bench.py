@@ -16,9 +16,9 @@ Printed JSON line (rank 0):
   value        decode tok/s over all ranks, device-timed (CUDA events around the K replays, max over ranks)
   e2e          the same metric through GraphGreedyDecoder.generate with a pinned host prompt: H2D prompt copy,
                per-token D2H token reads, (n - 1) / (total - ttft) as research/realmodel/bench_int8.py
-  roofline     decode_step_kernel, one launch per token: achieved = algorithmic bytes per token (weights, scales,
+  roofline     the step kernel (dataflow_step_kernel unless --step says otherwise), one launch per token: achieved = algorithmic bytes per token (weights, scales,
                norms, embedding row, KV at each timed step's context) / (device time / K) against the measured
-               HBM copy bandwidth; traffic = its ncu dram bytes per launch (profiles/decode_step_kernel_traffic.json)
+               HBM copy bandwidth; traffic = its ncu dram bytes per launch (profiles/step_kernel_traffic.json)
   cpu_baseline the reference's CPU path (oracle/torch_ref.py) on this host's cores, bounded sample
 With N > 1 (torchrun, one rank per GPU) the same workload runs as N independent replicas (scaling "weak": the value
 is the tokens of all ranks per second), so every N measures the same thing; the line adds `tensor_parallel`, BASELINE
@@ -47,7 +47,9 @@ ROOT = Path(__file__).resolve().parent
 METRIC = 'batch-1 decode tok/s and % of HBM roofline, Qwen3-1.7B-shape int8, 1 B200'
 PROMPT_LEN, NEW_TOKENS = 32, 256
 FALLBACK_PEAKS = {'hbm_gbs': 6650.0}
-TRAFFIC_FILE = ROOT / 'profiles' / 'decode_step_kernel_traffic.json'
+STEP_KERNELS = {'dataflow': 'dataflow_step_kernel', 'persistent': 'decode_step_kernel',
+                'sequence': 'gemv_tc_kernel (step)'}
+TRAFFIC_FILE = ROOT / 'profiles' / 'step_kernel_traffic.json'
 L2_BYTES = 126 * 2 ** 20
 REF_MAX_STEPS = 512  # the reference arm's CPU steps are ~0.3 s each: bound the run to a few minutes
 
@@ -61,7 +63,8 @@ def parse(argv=None):
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-tp', action='store_true', help='N > 1: skip the config-5 tensor-parallel measurement')
-    ap.add_argument('--launch-sequence', action='store_true', help='per-stage kernels instead of the persistent step')
+    ap.add_argument('--step', choices=('dataflow', 'persistent', 'sequence'), default=None,
+                    help='decode step of configs 2 and profile_step (default: the engine\'s choice, dataflow)')
     ap.add_argument('--cpu-sample', type=int, default=16, help='timed CPU decode tokens of cpu_baseline')
     ap.add_argument('--workload', default='qwen3_1.7b',
                     choices=['qwen3_1.7b', 'qwen3_8b', 'nanogpt', 'gemv_sweep', 'attn_sweep', 'profile_step'])
@@ -158,12 +161,12 @@ class ClockSampler:
         return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': smax, 'reasons': sorted(reasons), 'samples': len(sm)}
 
 
-def traffic_per_launch():
-    """ncu dram bytes (read + write) per launch of decode_step_kernel at config 2, from the machine-readable
-    capture record (None when absent)."""
+def traffic_per_launch(kernel):
+    """ncu dram bytes (read + write) per launch of `kernel` at config 2, from the machine-readable capture record
+    (profiles/step_kernel_traffic.json: {kernel: {"traffic_bytes_per_launch": ..., ...}}); None when absent."""
     if not TRAFFIC_FILE.exists():
         return None
-    rec = json.loads(TRAFFIC_FILE.read_text())
+    rec = json.loads(TRAFFIC_FILE.read_text()).get(kernel) or {}
     return rec.get('traffic_bytes_per_launch')
 
 
@@ -238,14 +241,14 @@ def run_reference(a, rank):
 
 
 # --------------------------------------------------------------------------------------------- config 2
-def build(device, pdl=True, persistent=None):
+def build(device, pdl=True, step=None):
     from efficientgpt_b200.configs import qwen3_1p7b_config, random_model
     from efficientgpt_b200.fast_decode import GraphGreedyDecoder
     from efficientgpt_b200.int8_linear import quantize_model
     model = random_model(qwen3_1p7b_config(), device, seed=0)
     quantize_model(model, scale_dtype=torch.bfloat16)
     torch.cuda.empty_cache()
-    dec = GraphGreedyDecoder(model, max_cache_len=PROMPT_LEN + NEW_TOKENS, pdl=pdl, persistent=persistent)
+    dec = GraphGreedyDecoder(model, max_cache_len=PROMPT_LEN + NEW_TOKENS, pdl=pdl, step=step)
     prompt = torch.randint(0, model.config.vocab_size, (1, PROMPT_LEN), generator=torch.Generator().manual_seed(0))
     return model, dec, prompt
 
@@ -272,7 +275,7 @@ def cpu_baseline(dec, n_tokens):
 
 def run_config2(a, world, rank, local):
     """Config 2 on every rank (N independent replicas at N > 1); returns rank 0's line (None elsewhere)."""
-    model, dec, prompt = build('cuda', persistent=False if a.launch_sequence else None)
+    model, dec, prompt = build('cuda', step=a.step)
     eng = dec.engine
     dec._capture()
     eng.prefill(prompt.cuda())
@@ -306,9 +309,10 @@ def run_config2(a, world, rank, local):
     hbm = float(peaks['hbm_gbs'])
     gbs = bytes_tok / (ms / 1e3 / a.steps) / 1e9
     launches_per_step = 1 if eng.persistent else 5 * eng.n_layers + 1
-    roofline = {'bound': 'hbm', 'kernel': 'decode_step_kernel' if eng.persistent else 'gemv_tc_kernel (step)',
+    kernel = STEP_KERNELS[eng.step_kind]
+    roofline = {'bound': 'hbm', 'kernel': kernel,
                 'achieved': round(gbs, 1), 'peak': hbm, 'unit': 'GB/s', 'frac': round(gbs / hbm, 4),
-                'traffic': traffic_per_launch() if eng.persistent else None, 'launches_per_step': launches_per_step,
+                'traffic': traffic_per_launch(kernel) if eng.persistent else None, 'launches_per_step': launches_per_step,
                 'bytes_per_launch': round(bytes_tok / launches_per_step),
                 'avg_launch_us': round(ms * 1e3 / a.steps / launches_per_step, 3), 'peak_source': peak_src,
                 'mean_context': round(statistics.fmean(p + 1 for p in positions), 1)}
@@ -341,7 +345,7 @@ def run_config2(a, world, rank, local):
                        'timed_positions': 'whole windows' if a.steps >= NEW_TOKENS else
                        f'{a.steps} positions spread over {PROMPT_LEN}..{PROMPT_LEN + NEW_TOKENS - 1}',
                        'l2': 'no flush: 1.72 GB of weights streamed per step, larger than L2',
-                       'step': 'persistent' if eng.persistent else 'launch sequence'},
+                       'step': eng.step_kind},
             'tok_s_per_gpu': round(tok_s / world, 2),
             'roofline': roofline,
             'device_error': err,
@@ -453,8 +457,8 @@ def run_tp(a, world, rank, local, workload='qwen3_8b'):
                        'init': 'HF random init N(0,0.02) on the GPU, seed 0',
                        'parallelism': f'tp{world}' if world > 1 else 'single',
                        'l2': f'no flush: {bytes_rank / 1e9:.2f} GB streamed per step per GPU, larger than L2',
-                       'step': 'persistent' if eng.persistent else 'launch sequence'},
-            'roofline': {'bound': 'hbm', 'kernel': 'decode_step_kernel' if eng.persistent else 'gemv_tc_kernel (step)',
+                       'step': eng.step_kind},
+            'roofline': {'bound': 'hbm', 'kernel': STEP_KERNELS[eng.step_kind],
                          'achieved': round(gbs, 1), 'peak': hbm, 'unit': 'GB/s', 'frac': round(gbs / hbm, 4),
                          'traffic': None, 'launches_per_step': 1 if eng.persistent else 5 * shape.n_layers + 1,
                          'bytes_per_launch': round(bytes_rank), 'avg_launch_us': round(ms * 1e3 / a.steps, 3),
@@ -639,7 +643,7 @@ def run_attn_sweep(a):
 
 def run_profile_step(a):
     """A small decode workload for ncu captures: the Qwen3-1.7B shape with --layers decoder layers, a 32-token
-    prefill and --steps decode steps of the persistent kernel (or the launch sequence)."""
+    prefill and --steps decode steps of the --step kernel."""
     from efficientgpt_b200 import _lib
     from efficientgpt_b200.configs import qwen3_1p7b_config, random_model
     from efficientgpt_b200.engine import Qwen3Engine
@@ -648,7 +652,7 @@ def run_profile_step(a):
     cfg.num_hidden_layers = a.layers
     model = random_model(cfg, 'cuda', 0)
     quantize_model(model, scale_dtype=torch.bfloat16)
-    eng = Qwen3Engine(model, PROMPT_LEN + NEW_TOKENS, persistent=False if a.launch_sequence else None)
+    eng = Qwen3Engine(model, PROMPT_LEN + NEW_TOKENS, step=a.step)
     eng.prefill(torch.randint(0, cfg.vocab_size, (1, PROMPT_LEN), generator=torch.Generator().manual_seed(0)).cuda())
     for _ in range(a.steps):
         eng.step()
@@ -658,7 +662,7 @@ def run_profile_step(a):
         raise RuntimeError(f'device error {err}')
     print(json.dumps({'workload': 'profile_step', 'layers': a.layers, 'steps': a.steps, 'token': int(eng.token),
                       'position': int(eng.position), 'bytes_per_step': eng.weight_bytes(),
-                      'step': 'persistent' if eng.persistent else 'launch sequence'}), flush=True)
+                      'step': eng.step_kind}), flush=True)
 
 
 def main():

@@ -198,9 +198,10 @@ __device__ __forceinline__ void nt_sync() {
 }
 
 struct AttnTask {
-  const void *K, *V;  // this kv head's [cap][D] cache rows
+  const void *K, *V;  // this kv head's [cap][D] cache rows (global memory, or copies in shared memory)
   int64_t k0, k1;     // key range [k0, k1), k0 a multiple of kRefBlock
   float scale;
+  int prefetch_v;     // V in global memory: pass A prefetches the range's V rows into L2
 };
 
 // HD consecutive elements of a cache row, kept raw (bf16: 4, 8 or 16 bytes; fp32: 8, 16 or 32 bytes) until
@@ -309,7 +310,7 @@ __device__ void attn_pass_a(const AttnTask &t, AttnScratch<DPL, GRP> &S) {
   for (int ti = warp; ti < ntiles; ti += kAttnWarps) {
     const int64_t t0 = t.k0 + (int64_t)ti * kKeyTile;
     const int nkeys = (int)min((int64_t)kKeyTile, t.k1 - t0);
-    if (lane < nkeys) {
+    if (t.prefetch_v && lane < nkeys) {
       const char *vr = (const char *)t.V + (t0 + lane) * D * (BF16 ? 2 : 4);
 #pragma unroll
       for (int off = 0; off < D * (BF16 ? 2 : 4); off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(vr + off));
@@ -601,6 +602,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
   t.k0 = k0;
   t.k1 = k1;
   t.scale = p.scale;
+  t.prefetch_v = 1;
   if ((p.flags & EGPT_FLAG_REF_SOFTMAX) && k0 > 0) {
     attn_max_before<DPL, GRP, BF16, kAttnThreads>(t, S);
   } else if (threadIdx.x < GRP) {

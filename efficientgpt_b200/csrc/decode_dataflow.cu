@@ -52,6 +52,7 @@ struct Params {
   int scale_bf16;
   int rw;                           // ring slots per warp
   int kv_smem;                      // attention CTAs hold their K and V rows in shared memory
+  const int8_t *w_lm;
   const egpt_qwen3_layer *layers;  // device array
   const uint16_t *embed, *final_norm, *rope_cos, *rope_sin;
   const void *s_lm;
@@ -72,12 +73,14 @@ struct Params {
 // Per-stage description in shared memory (built once per launch; 32 bytes).
 struct DStage {
   const CUtensorMap *map;
+  const int8_t *w;
   const void *s;
-  int n, k;
-  short ntl;   // this CTA's tiles (tile t belongs to GEMV CTA t mod W)
-  short nk;    // 256-column chunks
-  int kind;
+  int k;               // columns
+  short ntl;           // this CTA's tiles (tile t belongs to GEMV CTA t mod W)
+  unsigned char nk;    // 256-column chunks
+  unsigned char kind;
 };
+static_assert(sizeof(DStage) == 32, "stage table entry");
 
 // ------------------------------------------------------------------------------------------------ LL words
 __device__ __forceinline__ void ll_put(unsigned long long *p, uint32_t payload, uint32_t tag) {
@@ -148,6 +151,15 @@ __device__ __forceinline__ bool mbar_try(uint64_t *bar, unsigned parity) {
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
+}
+// Wait (bounded by time only, whatever other waits reported) for copies still in flight before a CTA exits.
+__device__ void mbar_drain(uint64_t *bar, unsigned parity) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try(bar, parity))
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_device_error(EGPT_ERR_TIMEOUT);
+      return;
+    }
 }
 // Bounded wait for the phase of parity `parity` to complete; false after a timeout or another wait's error.
 __device__ bool mbar_wait(uint64_t *bar, unsigned parity) {
@@ -367,6 +379,7 @@ struct Ring {
   int issued;        // items issued so far
 };
 
+
 // Lane 0: issue the fill cursor's item into slot `slot` (two boxes: rows 0-7 and 8-15 of the tile; gate|up: 8 gate
 // rows and the 8 matching up rows).
 __device__ __forceinline__ void issue_item(const Params &P, const DStage *stab, int nstages, int W, Ring &R, int slot) {
@@ -422,8 +435,11 @@ __device__ __forceinline__ void fold_planes(const int (&c4)[4], long long &T0, l
 // Consume the warp's next item: wait for its slot and run the MMAs (c4 accumulates; the caller zeroes it). The slot
 // is refilled by refill(): right away in the lm_head stage, after the stage's last item in the layer stages, so that a
 // TMA issue that has to wait for room in the copy engine's queue never delays the stage's own items.
-__device__ __forceinline__ void consume(Ring &R, const int8_t *xd, int c, int xs, int (&c4)[4]) {
+__device__ __forceinline__ void refill(const Params &P, const DStage *stab, int nstages, int W, Ring &R);
+__device__ __forceinline__ void consume(const Params &P, const DStage *stab, int nstages, int W, Ring &R,
+                                        const int8_t *xd, int c, int xs, int (&c4)[4]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  if (R.issued <= R.n) refill(P, stab, nstages, W, R);  // a stage with more items than ring slots: issue on demand
   // the MMAs are warp-wide: every lane takes the same branch
   if (__all_sync(0xffffffffu, mbar_wait(R.full + R.slot, R.phase)))
     item_sums(R.slots + (size_t)R.slot * kItem, xd, c, xs, g, t, c4);
@@ -525,7 +541,7 @@ __device__ void gemv_stage(const Params &P, const DStage *stab, int nstages, int
     const int i = cur.i;
     const int tl = i / sd.nk, c = i - tl * sd.nk;
     int c4[4] = {0, 0, 0, 0};
-    consume(R, xd, c, xs, c4);
+    consume(P, stab, nstages, W, R, xd, c, xs, c4);
     long long T0, T1;
     fold_planes(c4, T0, T1);
     if (t == 0) {
@@ -534,10 +550,10 @@ __device__ void gemv_stage(const Params &P, const DStage *stab, int nstages, int
     }
     cur_next(stab, nstages, cur);
   }
-  refill(P, stab, nstages, W, R);
   csync();  // every item's sums are in `part`
   if (TRACE && tslot >= 0 && P.trace && threadIdx.x == 0) P.trace[tslot] = globaltimer_ns();
   if (epi) epilogue(P, sd, part, E, out, out_tag, res, res_tag, etl, ep, etile, s0, s1, s2, s3, rw);
+  refill(P, stab, nstages, W, R);  // off the stage's critical path: the outputs are out
   if (TRACE && tslot >= 0 && P.trace) {
     csync();
     if (threadIdx.x == 0) P.trace[tslot + 1] = globaltimer_ns();
@@ -562,7 +578,7 @@ __device__ void lm_stage(const Params &P, const DStage *stab, int nstages, int W
     if (t == 0) s0 = scale_of(P, raw_scale(P, sd.s, r0)), s1 = scale_of(P, raw_scale(P, sd.s, r1));
     int c4[4] = {0, 0, 0, 0};
     for (int c = 0; c < sd.nk; ++c) {
-      consume(R, xd, c, xs, c4);
+      consume(P, stab, nstages, W, R, xd, c, xs, c4);
       refill(P, stab, nstages, W, R);
       cur_next(stab, nstages, cur);
     }
@@ -593,6 +609,125 @@ __device__ __forceinline__ void kv_load(const Params &P, int l, int g, int64_t n
     bulk_copy(Ks, (const uint16_t *)Ly.k_cache + base, (unsigned)bytes, bar);
     bulk_copy(Vs, (const uint16_t *)Ly.v_cache + base, (unsigned)bytes, bar);
   }
+}
+
+// Scratch of the shared-memory attention (behind the K and V copies).
+template <int DPL, int GRP>
+struct SmemAttn {
+  static constexpr int D = DPL * 32;
+  static constexpr int KMAX = 1024;  // keys (cap bound of this mode)
+  static constexpr int PVW = 8;      // warps of the P.V pass
+  float sc[GRP][KMAX];               // scores
+  float pref[KMAX / kRefBlock][GRP]; // running maximum after each 128-key block
+  float wacc[PVW][GRP][D];           // per-warp numerators
+  float wl[PVW][GRP];                // per-warp denominators
+};
+
+// Attention over the n keys whose K and V rows sit in shared memory (Ks, Vs: [n][D] bf16), q heads in q (fp32 values
+// of bf16 numbers), with the reference GPU kernel's probability rounding: the keys are walked in 128-key blocks
+// with a running maximum m_b, p = exp(s - m_b) enters P.V rounded to bf16 and the denominator in fp32, and the
+// blocks are brought to the final maximum by exp(m_b - m_final). Scores: warp w takes keys w, w + 16, ...; lane l
+// holds dims [l DPL, (l + 1) DPL) of q and of the key (one 8-byte read per key), fp32 dot product over the lane's
+// dims then a butterfly sum. P.V: warp w < 8 takes keys w, w + 8, ...; lane i of a round computes p of the round's
+// key i, then each key's p is broadcast and every lane accumulates its dims; warps merge in a fixed order.
+// out(j, d) for word idx (two dims) is written as LL words by the caller's loop below.
+template <int DPL, int GRP>
+__device__ void attn_smem(const uint16_t *Ks, const uint16_t *Vs, int n, const float (*q)[DPL * 32], float scale,
+                          SmemAttn<DPL, GRP> &A) {
+  constexpr int D = DPL * 32, PVW = SmemAttn<DPL, GRP>::PVW;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // scores
+  float qr[GRP][DPL];
+#pragma unroll
+  for (int j = 0; j < GRP; ++j)
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) qr[j][i] = q[j][lane * DPL + i];
+  for (int k = warp; k < n; k += kW) {
+    float kv[DPL];
+    if (DPL == 4) {
+      const uint2 u = *(const uint2 *)(Ks + (int64_t)k * D + lane * 4);
+      kv[0] = bf16_lo(u.x), kv[1 % DPL] = bf16_hi(u.x), kv[2 % DPL] = bf16_lo(u.y), kv[3 % DPL] = bf16_hi(u.y);
+    } else {
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) kv[i] = bf16_bits_to_f32(Ks[(int64_t)k * D + lane * DPL + i]);
+    }
+#pragma unroll
+    for (int j = 0; j < GRP; ++j) {
+      float d = 0.f;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) d = fmaf(qr[j][i], kv[i], d);
+      d = warp_sum(d);
+      if (lane == 0) A.sc[j][k] = d * scale;
+    }
+  }
+  csync();
+  // running block maxima (warp j < GRP: head j)
+  const int nblk = (n + kRefBlock - 1) / kRefBlock;
+  if (warp < GRP) {
+    float run = -INFINITY;
+    for (int b = 0; b < nblk; ++b) {
+      float m = -INFINITY;
+      for (int k = b * kRefBlock + lane; k < min(n, (b + 1) * kRefBlock); k += 32) m = fmaxf(m, A.sc[warp][k]);
+      run = fmaxf(run, warp_max(m));
+      if (lane == 0) A.pref[b][warp] = run;
+    }
+  }
+  csync();
+  // P.V
+  if (warp < PVW) {
+    float mfin[GRP];
+#pragma unroll
+    for (int j = 0; j < GRP; ++j) mfin[j] = A.pref[nblk - 1][j];
+    float acc[GRP][DPL], l[GRP];
+#pragma unroll
+    for (int j = 0; j < GRP; ++j) {
+      l[j] = 0.f;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[j][i] = 0.f;
+    }
+    for (int r0 = warp; r0 < n; r0 += 32 * PVW) {
+      // lane i: key r0 + PVW i of this round
+      const int kk = r0 + PVW * lane;
+      float pw[GRP];
+#pragma unroll
+      for (int j = 0; j < GRP; ++j) {
+        pw[j] = 0.f;
+        if (kk < n) {
+          const int b = kk / kRefBlock;
+          const float p = expf(A.sc[j][kk] - A.pref[b][j]);
+          const float f = expf(A.pref[b][j] - mfin[j]);
+          l[j] = fmaf(p, f, l[j]);
+          pw[j] = round_bf16(p) * f;
+        }
+      }
+      const int cnt = min(32, (n - r0 + PVW - 1) / PVW);
+      for (int i = 0; i < cnt; ++i) {
+        const int k = r0 + PVW * i;
+        float vv[DPL];
+        if (DPL == 4) {
+          const uint2 u = *(const uint2 *)(Vs + (int64_t)k * D + lane * 4);
+          vv[0] = bf16_lo(u.x), vv[1 % DPL] = bf16_hi(u.x), vv[2 % DPL] = bf16_lo(u.y), vv[3 % DPL] = bf16_hi(u.y);
+        } else {
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) vv[e] = bf16_bits_to_f32(Vs[(int64_t)k * D + lane * DPL + e]);
+        }
+#pragma unroll
+        for (int j = 0; j < GRP; ++j) {
+          const float pk = __shfl_sync(0xffffffffu, pw[j], i);
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) acc[j][e] = fmaf(pk, vv[e], acc[j][e]);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < GRP; ++j) {
+      const float lt = warp_sum(l[j]);
+      if (lane == 0) A.wl[warp][j] = lt;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) A.wacc[warp][j][lane * DPL + e] = acc[j][e];
+    }
+  }
+  csync();
 }
 
 // Attention of kv head g for this step (one CTA): the q heads of the group and the new k row from the q|k|v words
@@ -659,12 +794,33 @@ __device__ void attention_ll(const Params &P, const egpt_qwen3_layer &Ly, int g,
   __threadfence();
   csync();
   if (TRACE && tslot >= 0 && P.trace && threadIdx.x == 0) P.trace[tslot] = globaltimer_ns();
+  if (Ks) {  // K and V rows in shared memory
+    SmemAttn<DPL, GRP> &A = *reinterpret_cast<SmemAttn<DPL, GRP> *>(Vs + P.cap * D);
+    attn_smem<DPL, GRP>(Ks, Vs, (int)(pos + 1), S.q, P.scale, A);
+    for (int idx = threadIdx.x; idx < GRP * D / 2; idx += kCT) {
+      const int j = (2 * idx) / D, dd = 2 * idx - j * D;
+      float num0 = 0.f, num1 = 0.f, den = 0.f;
+#pragma unroll
+      for (int w = 0; w < SmemAttn<DPL, GRP>::PVW; ++w) {
+        den += A.wl[w][j];
+        num0 += A.wacc[w][j][dd];
+        num1 += A.wacc[w][j][dd + 1];
+      }
+      ll_put(out_w + ((int64_t)g * GRP * D) / 2 + idx, pack2(num0 / den, num1 / den), out_tag);
+    }
+    if (TRACE && tslot >= 0 && P.trace) {
+      csync();
+      if (threadIdx.x == 0) P.trace[tslot + 1] = globaltimer_ns();
+    }
+    return;
+  }
   AttnTask tk;
   tk.K = Ks ? (const void *)Ks : (const void *)(kc + kv_base);
   tk.V = Vs ? (const void *)Vs : (const void *)(vc + kv_base);
   tk.k0 = 0;
   tk.k1 = pos + 1;
   tk.scale = P.scale;
+  tk.prefetch_v = Vs ? 0 : 1;  // rows in shared memory: nothing to prefetch
   attn_walk<DPL, GRP, true, kCT, false>(tk, S);
   csync();
   const int64_t ntiles = (tk.k1 - tk.k0 + kKeyTile - 1) / kKeyTile;
@@ -751,11 +907,14 @@ __global__ void __launch_bounds__(kCT, 1) dataflow_step_kernel(const __grid_cons
     }
     const int tiles = n / 16;
     d.map = &P.maps[i];
+    d.w = i == 4 * P.L ? P.w_lm
+                       : (i & 3) == 0 ? P.layers[i >> 2].w_qkv
+                       : (i & 3) == 1 ? P.layers[i >> 2].w_o
+                       : (i & 3) == 2 ? P.layers[i >> 2].w_gu : P.layers[i >> 2].w_down;
     d.s = sp;
-    d.n = n;
     d.k = k;
-    d.kind = kind;
-    d.nk = (short)((k + kChunkCols - 1) / kChunkCols);
+    d.kind = (unsigned char)kind;
+    d.nk = (unsigned char)((k + kChunkCols - 1) / kChunkCols);
     d.ntl = (short)(attn_g < 0 && (int)blockIdx.x < tiles ? (tiles - (int)blockIdx.x + W - 1) / W : 0);
     stab[i] = d;
   }
@@ -784,12 +943,21 @@ __global__ void __launch_bounds__(kCT, 1) dataflow_step_kernel(const __grid_cons
     uint64_t *kvbar = bars + kW * P.rw;
     uint16_t *Ks = P.kv_smem ? (uint16_t *)big : nullptr;
     uint16_t *Vs = P.kv_smem ? (uint16_t *)big + P.cap * D : nullptr;
-    if (ok && Ks && threadIdx.x == 0) kv_load<D>(P, 0, attn_g, pos, Ks, Vs, kvbar);
+    int kv_pending = -1;  // layer whose K/V copy is in flight and not yet waited for
+    if (ok && Ks) {
+      if (threadIdx.x == 0) kv_load<D>(P, 0, attn_g, pos, Ks, Vs, kvbar);
+      kv_pending = 0;
+    }
     for (int l = 0; l < P.L; ++l) {
       const egpt_qwen3_layer &Ly = P.layers[l];
       unsigned long long *lw = P.ll + (int64_t)l * M.LW;
       if (ok && !Ks) prefetch_kv<D>(P, Ly, attn_g, pos);
-      if (ok && Ks && !mbar_wait(kvbar, (unsigned)l & 1u)) ok = false;
+      if (ok && Ks) {
+        if (mbar_wait(kvbar, (unsigned)l & 1u))
+          kv_pending = -1;
+        else
+          ok = false;
+      }
       if (ok) {
         attention_ll<DPL, GRP, TRACE>(P, Ly, attn_g, pos, lw + M.o_qkv, tag_of(P, epoch, l, 0), lw + M.o_attn,
                                       tag_of(P, epoch, l, 1), u, Ks, Vs,
@@ -800,11 +968,15 @@ __global__ void __launch_bounds__(kCT, 1) dataflow_step_kernel(const __grid_cons
           ll_put(lw + M.o_attn + ((int64_t)attn_g * GRP * D) / 2 + idx, 0u, tag_of(P, epoch, l, 1));
       }
       csync();  // the copies' rows and the attention scratch are free again
-      if (ok && Ks && l + 1 < P.L && threadIdx.x == 0) {
-        fence_async_smem();
-        kv_load<D>(P, l + 1, attn_g, pos, Ks, Vs, kvbar);
+      if (ok && Ks && l + 1 < P.L) {
+        if (threadIdx.x == 0) {
+          fence_async_smem();
+          kv_load<D>(P, l + 1, attn_g, pos, Ks, Vs, kvbar);
+        }
+        kv_pending = l + 1;
       }
     }
+    if (kv_pending >= 0 && threadIdx.x == 0) mbar_drain(kvbar, (unsigned)kv_pending & 1u);  // none in flight at exit
   } else {
     // ------------------------------------------------------------ GEMV CTA
     Ring R;
@@ -818,8 +990,9 @@ __global__ void __launch_bounds__(kCT, 1) dataflow_step_kernel(const __grid_cons
     R.fill.s = 0;
     R.fill.i = 0;
     cur_seek(stab, nstages, R.fill);
-    if (lane == 0)
+    if (lane == 0) {
       for (int k = 0; k < P.rw; ++k) issue_item(P, stab, nstages, W, R, k);
+    }
     R.fill.s = __shfl_sync(0xffffffffu, R.fill.s, 0);
     R.fill.i = __shfl_sync(0xffffffffu, R.fill.i, 0);
     R.issued = __shfl_sync(0xffffffffu, R.issued, 0);
@@ -875,9 +1048,9 @@ __global__ void __launch_bounds__(kCT, 1) dataflow_step_kernel(const __grid_cons
       lm_stage(P, stab, nstages, W, 4 * P.L, R, cur, xd, E, best);
     }
     // every issued copy has landed before the CTA exits (normally the warp consumed all of them)
-    if (lane == 0)
-      for (int n = max(0, R.issued - R.rw); n < R.issued; ++n)
-        if (!mbar_wait(R.full + n % R.rw, (unsigned)(n / R.rw) & 1u)) break;
+    if (lane == 0) {
+      for (int n = max(0, R.issued - R.rw); n < R.issued; ++n) mbar_drain(R.full + n % R.rw, (unsigned)(n / R.rw) & 1u);
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, best.v, o);
@@ -1076,7 +1249,9 @@ static bool layout(const egpt_qwen3_plan *Pl, Layout &lo) {
   if (lo.rw == 0) return false;
   const size_t big = (size_t)kW * lo.rw * kItem;
   lo.smem = fixed0 + ((size_t)(kW * lo.rw + 1) * 8 + 127) / 128 * 128 + big;
-  lo.kv_smem = (size_t)Pl->cap * D * 2 * 2 <= big ? 1 : 0;  // attention CTAs: K and V rows of the whole cache
+  const size_t sa = D == 32 ? sizeof(SmemAttn<1, 2>) : grp == 2 ? sizeof(SmemAttn<4, 2>) : sizeof(SmemAttn<4, 4>);
+  // attention CTAs: K and V rows of the whole cache, then the attention scratch
+  lo.kv_smem = ((size_t)Pl->cap * D * 2 * 2 + sa <= big && Pl->cap <= SmemAttn<4, 2>::KMAX) ? 1 : 0;
   return true;
 }
 
@@ -1178,6 +1353,7 @@ extern "C" int egpt_decode_step_dataflow(const egpt_qwen3_plan *Pl, void *stream
   P.I = Pl->intermediate, P.V = Pl->vocab, P.cap = Pl->cap, P.eps = Pl->eps, P.scale = Pl->attn_scale;
   P.scale_bf16 = Pl->scale_dtype == EGPT_BF16;
   P.rw = lo.rw, P.kv_smem = lo.kv_smem;
+  P.w_lm = Pl->w_lm;
   P.layers = Pl->layers_dev;
   P.embed = (const uint16_t *)Pl->embed, P.final_norm = (const uint16_t *)Pl->final_norm;
   P.rope_cos = (const uint16_t *)Pl->rope_cos, P.rope_sin = (const uint16_t *)Pl->rope_sin;

@@ -899,6 +899,7 @@ __device__ void attention_task(const Params &P, const egpt_qwen3_layer &Ly, int 
   t.k0 = k0;
   t.k1 = k1;
   t.scale = P.scale;
+  t.prefetch_v = 1;
   attn_pass_a<DPL, GRP, true>(t, S);
   stamp<TRACE>(P, tslot);
   const int ntiles = (int)((k1 - k0 + kKeyTile - 1) / kKeyTile);
