@@ -19,8 +19,10 @@
 //     layer's buffers are separate, so nothing is overwritten within a step; tags make the previous step's words
 //     stale. Every poll is bounded and records EGPT_ERR_TIMEOUT instead of hanging.
 //   * Attention CTAs keep their kv head's cached K and V rows in shared memory when the cache fits (one bulk
-//     copy per layer, issued a layer ahead, so the rows are resident before the layer's q arrives); the
-//     attention core of attention.cu then reads them there.
+//     copy per layer, issued a layer ahead, so the rows are resident before the layer's q arrives) and run their
+//     own shared-memory attention (attn_smem) on them; otherwise the attention core of attention.cu reads the
+//     cache in global memory. Both keep the reference GPU kernel's 128-key softmax blocks; they differ only in
+//     fp32 summation order.
 //   * RMSNorm's sum of squares is accumulated in fp64 (the bf16 squares are exact, so the sum is exact in
 //     practice and independent of the thread layout), rounded once to fp32.
 #include <cuda.h>
@@ -611,129 +613,169 @@ __device__ __forceinline__ void kv_load(const Params &P, int l, int g, int64_t n
   }
 }
 
-// Scratch of the shared-memory attention (behind the K and V copies).
-template <int DPL, int GRP>
-struct SmemAttn {
-  static constexpr int D = DPL * 32;
-  static constexpr int KMAX = 1024;  // keys (cap bound of this mode)
-  static constexpr int PVW = 8;      // warps of the P.V pass
-  float sc[GRP][KMAX];               // scores
-  float pref[KMAX / kRefBlock][GRP]; // running maximum after each 128-key block
-  float wacc[PVW][GRP][D];           // per-warp numerators
-  float wl[PVW][GRP];                // per-warp denominators
-};
+// Scratch of the shared-memory attention, carved behind the K and V copies (cap rows each), in floats:
+// scores [GRP][capr] | block maxima [GRP][kMaxBlk] (order-preserving ints) | numerators [kW][GRP][D] |
+// denominators [kW][GRP]; capr = cap rounded up to 8.
+constexpr int kMaxBlk = 8;  // 128-key blocks: caches of at most 1024 rows
+__host__ __device__ inline int64_t smem_attn_floats(int64_t cap, int grp, int d) {
+  return grp * ((cap + 7) / 8 * 8) + grp * kMaxBlk + (int64_t)kW * grp * d + kW * grp;
+}
+__device__ __forceinline__ int ord_enc(float f) {  // int order == float order
+  const int i = __float_as_int(f);
+  return i >= 0 ? i : i ^ 0x7fffffff;
+}
+__device__ __forceinline__ float ord_dec(int i) { return __int_as_float(i >= 0 ? i : i ^ 0x7fffffff); }
+
+// Sums of NV partial values over the 32 lanes (NV = 16 or 32), halving the set at each butterfly step: after the
+// call lane l holds the full sum of value l >> 1 (NV = 16) or l (NV = 32) in v[0]. NV - 1 + (NV == 16) shuffles in
+// all instead of 5 NV.
+template <int NV>
+__device__ __forceinline__ void reduce_scatter(float (&v)[NV]) {
+  const int lane = threadIdx.x & 31;
+  int n = NV;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    if (n > 1) {
+      const bool up = lane & o;
+      const int h = n / 2;
+#pragma unroll
+      for (int i = 0; i < NV / 2; ++i) {
+        if (i < h) {
+          const float send = up ? v[i] : v[i + h];
+          const float keep = up ? v[i + h] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      n = h;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+    }
+  }
+}
 
 // Attention over the n keys whose K and V rows sit in shared memory (Ks, Vs: [n][D] bf16), q heads in q (fp32 values
 // of bf16 numbers), with the reference GPU kernel's probability rounding: the keys are walked in 128-key blocks
 // with a running maximum m_b, p = exp(s - m_b) enters P.V rounded to bf16 and the denominator in fp32, and the
-// blocks are brought to the final maximum by exp(m_b - m_final). Scores: warp w takes keys w, w + 16, ...; lane l
-// holds dims [l DPL, (l + 1) DPL) of q and of the key (one 8-byte read per key), fp32 dot product over the lane's
-// dims then a butterfly sum. P.V: warp w < 8 takes keys w, w + 8, ...; lane i of a round computes p of the round's
-// key i, then each key's p is broadcast and every lane accumulates its dims; warps merge in a fixed order.
-// out(j, d) for word idx (two dims) is written as LL words by the caller's loop below.
+// blocks are brought to the final maximum by exp(m_b - m_final).
+//   Scores: warp w takes the 8-key groups w, w + 16, ...; lane l holds dims [l DPL, (l + 1) DPL) of q and of the 8
+//   keys, so GRP x 8 partial dot products per lane, summed over the lanes by one reduce-scatter; each group's
+//   maximum per head goes to the block maxima by a shared atomic max.
+//   P.V: warp w takes the keys [w ck, (w + 1) ck), ck = ceil(n / 16); lane i of a round of 32 computes p of the
+//   round's key i (block maxima read directly), then each key's p is broadcast and every lane accumulates its
+//   dims; the 16 warps' sums merge in a fixed order in the caller. The block maxima must hold ord_enc(-inf) on
+//   entry.
 template <int DPL, int GRP>
 __device__ void attn_smem(const uint16_t *Ks, const uint16_t *Vs, int n, const float (*q)[DPL * 32], float scale,
-                          SmemAttn<DPL, GRP> &A) {
-  constexpr int D = DPL * 32, PVW = SmemAttn<DPL, GRP>::PVW;
+                          float *sc, int capr, int *bm, float *wacc, float *wl) {
+  constexpr int D = DPL * 32, NV = GRP * 8;
+  static_assert(NV == 16 || NV == 32, "heads per group: 2 or 4");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // scores
   float qr[GRP][DPL];
 #pragma unroll
   for (int j = 0; j < GRP; ++j)
 #pragma unroll
     for (int i = 0; i < DPL; ++i) qr[j][i] = q[j][lane * DPL + i];
-  for (int k = warp; k < n; k += kW) {
-    float kv[DPL];
-    if (DPL == 4) {
-      const uint2 u = *(const uint2 *)(Ks + (int64_t)k * D + lane * 4);
-      kv[0] = bf16_lo(u.x), kv[1 % DPL] = bf16_hi(u.x), kv[2 % DPL] = bf16_lo(u.y), kv[3 % DPL] = bf16_hi(u.y);
-    } else {
+  const int ngr = (n + 7) / 8;
+  for (int gq = warp; gq < ngr; gq += kW) {
+    float v[NV];
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) kv[i] = bf16_bits_to_f32(Ks[(int64_t)k * D + lane * DPL + i]);
-    }
+    for (int kk = 0; kk < 8; ++kk) {
+      const int key = min(8 * gq + kk, n - 1);  // past the end: a valid row, its sums are dropped
+      float kv[DPL];
+      if (DPL == 4) {
+        const uint2 u = *(const uint2 *)(Ks + (int64_t)key * D + lane * 4);
+        kv[0] = bf16_lo(u.x), kv[1 % DPL] = bf16_hi(u.x), kv[2 % DPL] = bf16_lo(u.y), kv[3 % DPL] = bf16_hi(u.y);
+      } else {
 #pragma unroll
-    for (int j = 0; j < GRP; ++j) {
-      float d = 0.f;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) d = fmaf(qr[j][i], kv[i], d);
-      d = warp_sum(d);
-      if (lane == 0) A.sc[j][k] = d * scale;
-    }
-  }
-  csync();
-  // running block maxima (warp j < GRP: head j)
-  const int nblk = (n + kRefBlock - 1) / kRefBlock;
-  if (warp < GRP) {
-    float run = -INFINITY;
-    for (int b = 0; b < nblk; ++b) {
-      float m = -INFINITY;
-      for (int k = b * kRefBlock + lane; k < min(n, (b + 1) * kRefBlock); k += 32) m = fmaxf(m, A.sc[warp][k]);
-      run = fmaxf(run, warp_max(m));
-      if (lane == 0) A.pref[b][warp] = run;
-    }
-  }
-  csync();
-  // P.V
-  if (warp < PVW) {
-    float mfin[GRP];
-#pragma unroll
-    for (int j = 0; j < GRP; ++j) mfin[j] = A.pref[nblk - 1][j];
-    float acc[GRP][DPL], l[GRP];
-#pragma unroll
-    for (int j = 0; j < GRP; ++j) {
-      l[j] = 0.f;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) acc[j][i] = 0.f;
-    }
-    for (int r0 = warp; r0 < n; r0 += 32 * PVW) {
-      // lane i: key r0 + PVW i of this round
-      const int kk = r0 + PVW * lane;
-      float pw[GRP];
+        for (int i = 0; i < DPL; ++i) kv[i] = bf16_bits_to_f32(Ks[(int64_t)key * D + lane * DPL + i]);
+      }
 #pragma unroll
       for (int j = 0; j < GRP; ++j) {
-        pw[j] = 0.f;
-        if (kk < n) {
-          const int b = kk / kRefBlock;
-          const float p = expf(A.sc[j][kk] - A.pref[b][j]);
-          const float f = expf(A.pref[b][j] - mfin[j]);
-          l[j] = fmaf(p, f, l[j]);
-          pw[j] = round_bf16(p) * f;
-        }
-      }
-      const int cnt = min(32, (n - r0 + PVW - 1) / PVW);
-      for (int i = 0; i < cnt; ++i) {
-        const int k = r0 + PVW * i;
-        float vv[DPL];
-        if (DPL == 4) {
-          const uint2 u = *(const uint2 *)(Vs + (int64_t)k * D + lane * 4);
-          vv[0] = bf16_lo(u.x), vv[1 % DPL] = bf16_hi(u.x), vv[2 % DPL] = bf16_lo(u.y), vv[3 % DPL] = bf16_hi(u.y);
-        } else {
+        float d = 0.f;
 #pragma unroll
-          for (int e = 0; e < DPL; ++e) vv[e] = bf16_bits_to_f32(Vs[(int64_t)k * D + lane * DPL + e]);
-        }
-#pragma unroll
-        for (int j = 0; j < GRP; ++j) {
-          const float pk = __shfl_sync(0xffffffffu, pw[j], i);
-#pragma unroll
-          for (int e = 0; e < DPL; ++e) acc[j][e] = fmaf(pk, vv[e], acc[j][e]);
-        }
+        for (int i = 0; i < DPL; ++i) d = fmaf(qr[j][i], kv[i], d);
+        v[j * 8 + kk] = d;
       }
     }
+    reduce_scatter<NV>(v);
+    const int idx = NV == 16 ? lane >> 1 : lane;  // value held: head idx / 8, key 8 gq + idx % 8
+    const int j = idx >> 3, key = 8 * gq + (idx & 7);
+    const float sv = v[0] * scale;
+    float m = key < n ? sv : -INFINITY;
+    // maximum over the group's 8 keys of head j: lanes of one head are 16 (NV 16) or 8 (NV 32) apart in a run
+#pragma unroll
+    for (int o = NV == 16 ? 2 : 1; o < (NV == 16 ? 16 : 8); o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const bool writer = NV == 16 ? (lane & 1) == 0 : true;
+    if (writer && key < n) sc[j * capr + key] = sv;
+    if (writer && (idx & 7) == 0) atomicMax(&bm[j * kMaxBlk + key / kRefBlock], ord_enc(m));
+  }
+  csync();
+  const int nblk = (n + kRefBlock - 1) / kRefBlock;
+  float mfin[GRP];
+#pragma unroll
+  for (int j = 0; j < GRP; ++j) {
+    float mm = -INFINITY;
+    for (int b = 0; b < nblk; ++b) mm = fmaxf(mm, ord_dec(bm[j * kMaxBlk + b]));
+    mfin[j] = mm;
+  }
+  float acc[GRP][DPL], l[GRP];
+#pragma unroll
+  for (int j = 0; j < GRP; ++j) {
+    l[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[j][i] = 0.f;
+  }
+  const int ck = (n + kW - 1) / kW, kend = min(n, (warp + 1) * ck);  // warp w: keys [w ck, (w + 1) ck)
+  for (int r0 = warp * ck; r0 < kend; r0 += 32) {
+    const int kk = r0 + lane;  // lane i: key r0 + i of this round
+    float pw[GRP];
 #pragma unroll
     for (int j = 0; j < GRP; ++j) {
-      const float lt = warp_sum(l[j]);
-      if (lane == 0) A.wl[warp][j] = lt;
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) A.wacc[warp][j][lane * DPL + e] = acc[j][e];
+      pw[j] = 0.f;
+      if (kk < kend) {
+        const int b = kk / kRefBlock;
+        float mb = -INFINITY;
+        for (int c = 0; c <= b; ++c) mb = fmaxf(mb, ord_dec(bm[j * kMaxBlk + c]));  // running max after block b
+        const float p = expf(sc[j * capr + kk] - mb);
+        const float f = expf(mb - mfin[j]);
+        l[j] = fmaf(p, f, l[j]);
+        pw[j] = round_bf16(p) * f;
+      }
     }
+    const int cnt = min(32, kend - r0);
+    for (int i = 0; i < cnt; ++i) {
+      const int k = r0 + i;
+      float vv[DPL];
+      if (DPL == 4) {
+        const uint2 u = *(const uint2 *)(Vs + (int64_t)k * D + lane * 4);
+        vv[0] = bf16_lo(u.x), vv[1 % DPL] = bf16_hi(u.x), vv[2 % DPL] = bf16_lo(u.y), vv[3 % DPL] = bf16_hi(u.y);
+      } else {
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) vv[e] = bf16_bits_to_f32(Vs[(int64_t)k * D + lane * DPL + e]);
+      }
+#pragma unroll
+      for (int j = 0; j < GRP; ++j) {
+        const float pk = __shfl_sync(0xffffffffu, pw[j], i);
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) acc[j][e] = fmaf(pk, vv[e], acc[j][e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < GRP; ++j) {
+    const float lt = warp_sum(l[j]);
+    if (lane == 0) wl[warp * GRP + j] = lt;
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) wacc[(warp * GRP + j) * D + lane * DPL + e] = acc[j][e];
   }
   csync();
 }
 
 // Attention of kv head g for this step (one CTA): the q heads of the group and the new k row from the q|k|v words
 // (normalised and rotated by one warp each), the new k and v rows appended to the cache (and to the shared-memory
-// copies Ks / Vs when those hold the cache), then the attention core of attention.cu (the reference GPU kernel's
-// 128-key block walk) over keys [0, pos], and the group's output published as LL words.
+// copies Ks / Vs when those hold the cache), then attention over keys [0, pos] (attn_smem on the shared-memory
+// copies, else the attention core of attention.cu: both the reference GPU kernel's 128-key block walk), and the
+// group's output published as LL words.
 template <int DPL, int GRP, bool TRACE>
 __device__ void attention_ll(const Params &P, const egpt_qwen3_layer &Ly, int g, int64_t pos,
                              const unsigned long long *qkv_w, uint32_t qkv_tag, unsigned long long *out_w,
@@ -791,20 +833,42 @@ __device__ void attention_ll(const Params &P, const egpt_qwen3_layer &Ly, int g,
     }
   }
   if (threadIdx.x < GRP) S.mb[threadIdx.x] = -INFINITY;
+  if (Ks && threadIdx.x < GRP * kMaxBlk)  // block maxima of the shared-memory attention
+    ((int *)((float *)(Vs + P.cap * D) + GRP * ((P.cap + 7) / 8 * 8)))[threadIdx.x] = ord_enc(-INFINITY);
   __threadfence();
   csync();
   if (TRACE && tslot >= 0 && P.trace && threadIdx.x == 0) P.trace[tslot] = globaltimer_ns();
   if (Ks) {  // K and V rows in shared memory
-    SmemAttn<DPL, GRP> &A = *reinterpret_cast<SmemAttn<DPL, GRP> *>(Vs + P.cap * D);
-    attn_smem<DPL, GRP>(Ks, Vs, (int)(pos + 1), S.q, P.scale, A);
-    for (int idx = threadIdx.x; idx < GRP * D / 2; idx += kCT) {
+    const int capr = (P.cap + 7) / 8 * 8;
+    float *sc = (float *)(Vs + P.cap * D);
+    int *bm = (int *)(sc + GRP * capr);
+    float *wacc = (float *)(bm + GRP * kMaxBlk), *wl = wacc + kW * GRP * D;
+    attn_smem<DPL, GRP>(Ks, Vs, (int)(pos + 1), S.q, P.scale, sc, capr, bm, wacc, wl);
+    // merge of the 16 warps' sums in a fixed order: 4 parts of 4 warps each (into the part's first warp's slot),
+    // then the 4 parts
+    constexpr int NW = GRP * D / 2;  // output words (two dims each)
+    for (int t = threadIdx.x; t < 4 * NW; t += kCT) {
+      const int idx = t % NW, part = t / NW;
+      const int j = (2 * idx) / D, dd = 2 * idx - j * D, w0 = 4 * part;
+      float num0 = 0.f, num1 = 0.f;
+#pragma unroll
+      for (int w = w0; w < w0 + 4; ++w) {
+        num0 += wacc[(w * GRP + j) * D + dd];
+        num1 += wacc[(w * GRP + j) * D + dd + 1];
+      }
+      wacc[(w0 * GRP + j) * D + dd] = num0;
+      wacc[(w0 * GRP + j) * D + dd + 1] = num1;
+    }
+    csync();
+    for (int idx = threadIdx.x; idx < NW; idx += kCT) {
       const int j = (2 * idx) / D, dd = 2 * idx - j * D;
       float num0 = 0.f, num1 = 0.f, den = 0.f;
 #pragma unroll
-      for (int w = 0; w < SmemAttn<DPL, GRP>::PVW; ++w) {
-        den += A.wl[w][j];
-        num0 += A.wacc[w][j][dd];
-        num1 += A.wacc[w][j][dd + 1];
+      for (int w = 0; w < kW; ++w) den += wl[w * GRP + j];
+#pragma unroll
+      for (int w = 0; w < kW; w += 4) {
+        num0 += wacc[(w * GRP + j) * D + dd];
+        num1 += wacc[(w * GRP + j) * D + dd + 1];
       }
       ll_put(out_w + ((int64_t)g * GRP * D) / 2 + idx, pack2(num0 / den, num1 / den), out_tag);
     }
@@ -1249,9 +1313,9 @@ static bool layout(const egpt_qwen3_plan *Pl, Layout &lo) {
   if (lo.rw == 0) return false;
   const size_t big = (size_t)kW * lo.rw * kItem;
   lo.smem = fixed0 + ((size_t)(kW * lo.rw + 1) * 8 + 127) / 128 * 128 + big;
-  const size_t sa = D == 32 ? sizeof(SmemAttn<1, 2>) : grp == 2 ? sizeof(SmemAttn<4, 2>) : sizeof(SmemAttn<4, 4>);
+  const size_t sa = 4 * (size_t)smem_attn_floats(Pl->cap, grp, D);
   // attention CTAs: K and V rows of the whole cache, then the attention scratch
-  lo.kv_smem = ((size_t)Pl->cap * D * 2 * 2 + sa <= big && Pl->cap <= SmemAttn<4, 2>::KMAX) ? 1 : 0;
+  lo.kv_smem = ((size_t)Pl->cap * D * 2 * 2 + sa <= big && Pl->cap <= kMaxBlk * kRefBlock) ? 1 : 0;
   return true;
 }
 
