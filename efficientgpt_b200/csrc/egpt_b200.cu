@@ -7,3 +7,4 @@
 #include "decode_step.cu"
 #include "decode_dataflow.cu"
 #include "gemv_tc.cu"
+#include "sampling.cu"

@@ -29,11 +29,12 @@ from .engine import Qwen3Engine
 class GraphGreedyDecoder:
     """One CUDA graph per decode step; token and position live on the device."""
 
-    def __init__(self, model, max_cache_len, lookahead=8, pdl=True, persistent=None, step=None):
+    def __init__(self, model, max_cache_len, lookahead=8, pdl=True, persistent=None, step=None, keep_logits=False):
         if lookahead < 0:
             raise ValueError('lookahead must be >= 0')
         self.model, self.max_cache_len, self.lookahead = model, max_cache_len, lookahead
-        self.engine = Qwen3Engine(model, max_cache_len, pdl=pdl, persistent=persistent, step=step)
+        self.engine = Qwen3Engine(model, max_cache_len, pdl=pdl, persistent=persistent, step=step,
+                                  keep_logits=keep_logits)
         self.device = self.engine.device
         self.token = self.engine.token
         self.position = self.engine.position
@@ -51,13 +52,20 @@ class GraphGreedyDecoder:
         with torch.cuda.stream(side):  # warm-up outside capture (loads the library, sets kernel attributes)
             for _ in range(3):
                 eng.position.zero_()
-                eng.step()
+                self._step()
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            eng.step()
+            self._step()
         eng.reset()
+
+    def _step(self):
+        """The work of one graph replay: the next token from the current one."""
+        self.engine.step()
+
+    def _first(self):
+        """After the prefill: step 0's token is on the device (greedy: the prefill's argmax)."""
 
     def _check(self, input_ids, max_new_tokens):
         if input_ids.dim() != 2 or input_ids.shape[0] != 1:
@@ -92,6 +100,7 @@ class GraphGreedyDecoder:
         pending = collections.deque()  # steps whose token is queued but not yet emitted, oldest first
         t0 = time.perf_counter()
         self.engine.prefill(input_ids.to(self.device, non_blocking=True))  # leaves step 0's token on the device
+        self._first()
 
         def emit(step):
             nonlocal first_at
@@ -121,3 +130,42 @@ class GraphGreedyDecoder:
         torch.cuda.synchronize()
         return tokens, {'ttft_s': first_at - t0, 'total_s': time.perf_counter() - t0, 'tokens': len(tokens),
                         'capture_s': capture_s}
+
+
+class SampledGraphDecoder(GraphGreedyDecoder):
+    """Stochastic decoding in the same graph loop: each replay runs the native step with its logits kept, then draws
+    the next token on the device (efficientgpt_b200.sampling: temperature -> top-k -> top-p -> inverse CDF) from the
+    caller's pre-drawn uniforms, one per generated token, the contract of research/phase5/sampling.py:133-152
+    (SampledGraphDecoder) and SampledEngine.reset/step (103-124): token 0 from the prompt's last logits with u[0],
+    token i with u[i]. generate(input_ids, max_new_tokens, uniforms, eos_ids=(), on_token=None), uniforms float32
+    [1, >= max_new_tokens] (e.g. sampling.draw_uniforms); otherwise as GraphGreedyDecoder."""
+
+    def __init__(self, model, max_cache_len, cfg, lookahead=8, pdl=True, step=None):
+        from .sampling import sample_ws
+        super().__init__(model, max_cache_len, lookahead=lookahead, pdl=pdl, step=step, keep_logits=True)
+        self.cfg = cfg
+        self.uniforms = torch.zeros(1, max_cache_len, dtype=torch.float32, device=self.device)
+        self.u_index = torch.zeros((), dtype=torch.int64, device=self.device)
+        self.ws = sample_ws(1, self.device)
+
+    def _draw(self):
+        from .sampling import sample
+        eng = self.engine
+        sample(eng.logits.view(1, -1), self.cfg, self.uniforms, out=eng.token.view(1, 1), ws=self.ws,
+               u_index=self.u_index)
+
+    def _step(self):
+        self.engine.step()
+        self._draw()
+
+    def _first(self):
+        self.u_index.zero_()
+        self._draw()
+
+    def generate(self, input_ids, max_new_tokens, uniforms, eos_ids=(), on_token=None):
+        self._check(input_ids, max_new_tokens)
+        if uniforms.dim() != 2 or uniforms.shape[0] != 1 or uniforms.shape[1] < max_new_tokens or \
+                uniforms.dtype != torch.float32:
+            raise ValueError('uniforms must be float32 [batch, >= count]')
+        self.uniforms[:, :max_new_tokens].copy_(uniforms[:, :max_new_tokens], non_blocking=True)
+        return super().generate(input_ids, max_new_tokens, eos_ids=eos_ids, on_token=on_token)

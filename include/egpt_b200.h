@@ -168,6 +168,23 @@ EGPT_API int egpt_attn_decode_noalloc(void *out, int64_t ldo, const void *q, int
  * replaces: logits[:, -1].argmax(-1) (research/realmodel/fast_decode.py:48,84): first index on ties. */
 EGPT_API int egpt_argmax_rows(int64_t *out, const void *logits, int64_t rows, int64_t n, int64_t ld, int dtype, void *stream);
 
+/* ---- stochastic sampling: temperature -> top-k -> top-p -> inverse CDF -------------------------------
+ * replaces: filtered_probs + sample_from (research/phase5/sampling.py:39-71; the Triton families
+ * temperature_softmax / topk_softmax / inverse_cdf_sample of research/kernelagent/templates.py:131-343).
+ * One token per row of `rows` x V logits (V <= 2^24; bf16 or fp32, leading dimension ld): x = logit / temperature; top_k > 0
+ * keeps x >= the k-th largest x (ties kept; 0 = off); top_p < 1 keeps the smallest prefix of the stable descending
+ * order of softmax(x) whose exclusive prefix mass stays below top_p, then renormalises (1 = off); the token is the
+ * first index whose cumulative probability exceeds u * total, never a zero-probability token. u for row r is
+ * u[r * u_ld + (u_index ? *u_index : 0)]; with u_index the call adds 1 to *u_index after drawing (one uniform per
+ * generated token, as the reference's pre-drawn uniforms). Result in out[r * out_ld] (int64).
+ * Workspace: egpt_sample_ws_bytes(rows) bytes, 16-byte aligned, zero-filled once by the caller; every call leaves
+ * it zeroed. Deterministic (integer histograms and fixed-order sums). Errors: temperature <= 0, top_k < 0 or top_p
+ * outside (0, 1] -> EGPT_ERR_ARG with the reference's messages. */
+EGPT_API size_t egpt_sample_ws_bytes(int64_t rows);
+EGPT_API int egpt_sample(const void *logits, int dtype, int64_t rows, int64_t V, int64_t ld, float temperature,
+                         int64_t top_k, float top_p, const float *u, int64_t u_ld, int64_t *u_index, int64_t *out,
+                         int64_t out_ld, void *ws, size_t ws_bytes, void *stream);
+
 /* ---- whole decode step (Qwen3 family) ---------------------------------------------------------------
  * replaces: research/realmodel/fast_decode.py:45-49 GraphGreedyDecoder._step (HF Qwen3 forward with
  *           StaticCache + argmax + position += 1), captured into one CUDA graph by the caller.

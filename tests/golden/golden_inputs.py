@@ -80,3 +80,14 @@ def tiny_prompts():
 
 def big_prompt():
     return torch.randint(0, 151936, (1, 32), generator=torch.Generator().manual_seed(0))
+
+
+def sampling_logits(v, seed, scale, dtype=torch.bfloat16):
+    """One row of seeded logits for the sampling cases: N(0, scale^2) on the CPU generator, rounded to `dtype`."""
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(v, generator=g) * scale).to(dtype)
+
+
+def sampling_uniforms(n, seed):
+    g = torch.Generator().manual_seed(10_000 + seed)
+    return torch.rand(n, generator=g)
