@@ -269,18 +269,20 @@ EGPT_API int egpt_decode_step_persistent(const egpt_qwen3_plan *plan, void *stre
 EGPT_API int egpt_decode_step_persistent_check(const egpt_qwen3_plan *plan);
 
 /* Dataflow variant of egpt_decode_step_persistent (one GPU): the same arithmetic in ONE cooperative kernel with
- * one CTA per SM and no grid barrier. Per CTA one producer warp streams the CTA's share of every weight matrix
- * of the step (16-row x 256-column items, each as two TMA tensor loads, no multicast) into a ring of shared-memory
- * slots guarded by mbarriers, running ahead across stage boundaries; 15 consumer warps run the stages. Every
+ * one CTA per SM and no grid barrier. The last n_kv_heads CTAs run the attention of one kv head each (holding its
+ * cached K/V rows in shared memory when they fit); every warp of the other CTAs streams its share of every weight
+ * matrix of the step (16-row x 256-column items, each as two TMA tensor loads, no multicast, this GPU's memory)
+ * through its own ring of shared-memory slots guarded by mbarriers, running ahead across stage boundaries. Every
  * stage output (q|k|v, attention, residual stream, act) is published as LL words in plan->df_ws (two bf16 values
  * and a 32-bit tag of step, layer and site in one 8-byte word); consumers poll the words of their input until
  * every tag matches, so data and readiness arrive together. Every wait is bounded (EGPT_ERR_TIMEOUT via
  * egpt_device_error). RMSNorm sums its bf16 squares in fp64 (exact in practice, independent of the thread
- * layout). egpt_dataflow_ws_bytes: size of plan->df_ws for this plan (tensor maps, step epoch, LL words);
- * egpt_dataflow_prepare encodes the weights' tensor maps into plan->df_ws (synchronous copy; call once after
- * the weight pointers are set, before the first step and before any stream capture). Built for head_dim 128
- * with 2 or 4 q heads per kv head and head_dim 32 with 2; hidden, intermediate and nq*d multiples of 64 up to
- * 7680, vocab a multiple of 16; tp_world <= 1. egpt_decode_step_dataflow_check runs the host-side checks. */
+ * layout). egpt_dataflow_ws_bytes: size of plan->df_ws for this plan (step epoch and LL words; zero-filled once).
+ * egpt_dataflow_prepare checks the plan and encodes the weights' tensor maps into a host-side cache keyed by
+ * plan->df_ws and the weight pointers (call once after the weight pointers are set, before any stream capture;
+ * the step re-encodes by itself when the pointers change). Built for head_dim 128 with 2 or 4 q heads per kv head
+ * and head_dim 32 with 2; hidden, intermediate and nq*d multiples of 64 up to 7680, vocab a multiple of 16, at
+ * most 56 layers; tp_world <= 1. egpt_decode_step_dataflow_check runs the host-side checks. */
 EGPT_API size_t egpt_dataflow_ws_bytes(const egpt_qwen3_plan *plan);
 EGPT_API int egpt_dataflow_prepare(const egpt_qwen3_plan *plan);
 EGPT_API int egpt_decode_step_dataflow(const egpt_qwen3_plan *plan, void *stream);
