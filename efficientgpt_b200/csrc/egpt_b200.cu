@@ -8,3 +8,4 @@
 #include "decode_dataflow.cu"
 #include "gemv_tc.cu"
 #include "sampling.cu"
+#include "gemm_tc.cu"

@@ -1,0 +1,359 @@
+// int8-weight GEMM for long-prompt prefill on the 5th-generation tensor cores (tcgen05, sm_100a):
+//
+//   Y[m, n] = bf16( bf16( sum_k X[m, k] * bf16(Q[n, k]) ) * s[n] )        (double rounding: the reference's
+//                                                                          >16-row branch, int8_linear.py:96-97)
+//   or, without EGPT_FLAG_DOUBLE_ROUND, bf16(fp32 sum * s[n]).
+//
+// X bf16 [M, K] (row stride ldx), Q int8 [N, K] (row-major, the model's own buffer), s bf16 or fp32 [N]. The
+// reference materialises bf16(Q) in HBM on every call; here the int8 rows are converted to bf16 in shared memory
+// on their way to the tensor cores, so HBM sees the int8 bytes once per output tile column.
+//
+// One CTA per 128 x 256 output tile, 320 threads:
+//   warp 0   lane 0 issues the TMA loads of X (box 64 columns x 128 rows, 128-byte swizzle) and of the int8 Q tile
+//            (box 64 columns x 256 rows, 64-byte swizzle), this GPU's memory, no multicast, into a ring of kStages
+//            slots;
+//   warp 1   allocates 256 TMEM columns (the fp32 accumulator, lane = row) and, lane 0, issues
+//            tcgen05.mma.cta_group::1.kind::f16 (M 128, N 256, K 16; both operands bf16, K-major, 128-byte
+//            swizzled shared-memory descriptors), four per 64-column k block, then tcgen05.commit to the slot's
+//            "empty" barrier and, after the last block, to the accumulator barrier;
+//   warps 2-9 convert Q: each thread reads one row's 64 int8 of the k block from the slot (the 64-byte swizzle
+//            makes the 16-byte reads of 8 consecutive rows hit 32 distinct banks), widens them to bf16 (exact:
+//            |q| <= 127) and stores them in the operand's swizzled layout (row r at 128 r bytes, 16-byte chunk c at
+//            (c ^ (r & 7)) * 16), then fence.proxy.async and an arrival on the slot's "B full" barrier; the slot is
+//            reused once the MMAs that read it have committed; after the last block the same warps read the accumulator
+//            with tcgen05.ld (warp w owns TMEM lanes 32 (w % 4) .., two warps per lane quarter split the columns),
+//            scale, round and store Y. The widening needs no int-to-float conversion (byte_val).
+// Every mbarrier wait is bounded (EGPT_ERR_TIMEOUT through egpt_device_error); a role that gives up skips its
+// remaining work, and before the CTA exits the issued TMA loads and MMAs are drained (bounded) and TMEM is freed.
+#include "internal.h"
+#include "common.cuh"
+
+namespace egpt {
+namespace gtc {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64;  // output tile and k block (64 bf16 = one 128-byte swizzle row)
+constexpr int kStages = 5;   // TMA ring: X and int8 Q tiles (latency cover)
+constexpr int kBStages = 2;  // widened Q tiles between the converters and the MMAs
+constexpr int kThreads = 320;
+constexpr int kABytes = kBM * kBK * 2;  // 16 KB: X tile, bf16
+constexpr int kRBytes = kBN * kBK;      // 16 KB: Q tile as loaded, int8
+constexpr int kBBytes = kBN * kBK * 2;  // 32 KB: Q tile widened to bf16
+constexpr int kConvThreads = 256;       // warps 2-9: one Q row each
+constexpr size_t kSmem = 1024 /* alignment slack */ + (size_t)kStages * (kABytes + kRBytes) + (size_t)kBStages * kBBytes + 256;
+
+struct Args {
+  CUtensorMap xmap;  // X bf16 [M, K], box {64, 128}, 128-byte swizzle
+  CUtensorMap qmap;  // Q int8 [N, K], box {64, 256}, 64-byte swizzle
+  const int8_t *q;
+  const void *s;
+  int s_bf16;
+  uint16_t *y;
+  int64_t M, N, K, ldy;
+  int double_round;
+};
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t *bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t *bar, unsigned parity) {
+  unsigned ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok)
+               : "r"(smem_u32(bar)), "r"(parity)
+               : "memory");
+  return ok != 0;
+}
+// Bounded wait; false after a timeout or once another wait of the grid has reported an error.
+__device__ bool mbar_wait(uint64_t *bar, unsigned parity) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (int it = 0;; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 15) == 15) {
+      if (device_error_set()) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        set_device_error(EGPT_ERR_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+// Bounded by time only (whatever the error state): used to drain work in flight before the CTA exits.
+__device__ void mbar_drain(uint64_t *bar, unsigned parity) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try(bar, parity))
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_device_error(EGPT_ERR_TIMEOUT);
+      return;
+    }
+}
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile whose rows are 128 bytes, 8-row groups 1024 bytes
+// apart, 128-byte swizzle (start address 1024-aligned; the k offset inside the row is added to the start field).
+__device__ __forceinline__ uint64_t sw128_desc(const void *tile) {
+  const uint64_t addr = smem_u32(tile);
+  return ((addr >> 4) & 0x3FFFull)          // start address
+         | (1ull << 16)                     // leading byte offset (unused with swizzling): 16 bytes
+         | ((uint64_t)(1024 >> 4) << 32)    // stride byte offset: 8 rows x 128 bytes
+         | (1ull << 46)                     // descriptor version (sm100)
+         | (2ull << 61);                    // 128-byte swizzle
+}
+// Instruction descriptor: D fp32, A and B bf16, both K-major, M = 128, N = 256.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Two fp32 values (exact integers) -> packed bf16x2, a in the low half (exact).
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+// Byte i of w (already XORed with 0x80: v + 128 as an unsigned byte) as the fp32 value v, without an int-to-float
+// conversion: the bits 0x4B0000uu are the float 2^23 + uu, and subtracting 2^23 + 128 leaves v exactly.
+__device__ __forceinline__ float byte_val(uint32_t w, int i) {
+  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650u + (uint32_t)i)) - 8388736.0f;
+}
+// 16 int8 (a uint4) -> 16 bf16 (two uint4), element order kept.
+__device__ __forceinline__ void widen16(const uint4 v, uint4 &lo, uint4 &hi) {
+  const uint32_t w[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u};
+  uint32_t o[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    o[2 * i] = pack_bf16x2(byte_val(w[i], 0), byte_val(w[i], 1));
+    o[2 * i + 1] = pack_bf16x2(byte_val(w[i], 2), byte_val(w[i], 3));
+  }
+  lo = make_uint4(o[0], o[1], o[2], o[3]);
+  hi = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_constant__ Args A) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);  // 1024-aligned operand tiles
+  uint8_t *sa = smem;                                      // kStages x [128 rows][128 B], bf16, 128-byte swizzle
+  uint8_t *sb = smem + (size_t)kStages * kABytes;          // kStages x [256 rows][128 B], bf16, 128-byte swizzle
+  uint8_t *sr = sb + (size_t)kBStages * kBBytes;           // kStages x [256 rows][64 B], int8, 64-byte swizzle
+  uint64_t *bars = (uint64_t *)(sr + (size_t)kStages * kRBytes);
+  uint64_t *full_a = bars, *empty = bars + kStages;                 // TMA ring
+  uint64_t *full_b = bars + 2 * kStages, *bempty = full_b + kBStages;  // widened-Q ring
+  uint64_t *acc = bempty + kBStages;
+  uint32_t *tmem_slot = (uint32_t *)(acc + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m0 = (int64_t)blockIdx.y * kBM, n0 = (int64_t)blockIdx.x * kBN;
+  const int nkb = (int)(A.K / kBK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full_a + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int s = 0; s < kBStages; ++s) {
+      mbar_init(full_b + s, kConvThreads);
+      mbar_init(bempty + s, 1);
+    }
+    mbar_init(acc, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // TMEM: 256 fp32 columns x 128 lanes
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kBN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- X producer
+    int issued = 0;
+    if (lane == 0) {
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kStages;
+        if (kb >= kStages && !mbar_wait(empty + s, (unsigned)((kb / kStages) - 1) & 1u)) break;
+        mbar_arrive_tx(full_a + s, kABytes + kRBytes);
+        tma_load_2d(sa + (size_t)s * kABytes, &A.xmap, kb * kBK, (int)m0, full_a + s);
+        tma_load_2d(sr + (size_t)s * kRBytes, &A.qmap, kb * kBK, (int)n0, full_a + s);
+        ++issued;
+      }
+      // none of this CTA's copies may still be landing when it exits
+      for (int kb = max(0, issued - kStages); kb < issued; ++kb) mbar_drain(full_a + kb % kStages, (unsigned)(kb / kStages) & 1u);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kStages, sbi = kb % kBStages;
+        if (!mbar_wait(full_a + s, (unsigned)(kb / kStages) & 1u) ||
+            !mbar_wait(full_b + sbi, (unsigned)(kb / kBStages) & 1u))
+          break;
+        tc_fence_after();
+        const uint64_t ad = sw128_desc(sa + (size_t)s * kABytes), bd = sw128_desc(sb + (size_t)sbi * kBBytes);
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k)  // 16 bf16 = 32 bytes per step inside the swizzled row
+          umma_f16(tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), (kb | k) != 0 ? 1u : 0u);
+        umma_commit(empty + s);     // the TMA slot is free once these MMAs have read it
+        umma_commit(bempty + sbi);  // and so is the widened-Q slot
+      }
+      umma_commit(acc);  // completes when every MMA issued above has finished (also after an early stop)
+    }
+  } else {
+    // ---------------------------------------------------------------- Q converters, then the epilogue
+    const int r = threadIdx.x - 64;  // the Q row (of the 256-row tile) this thread widens
+    bool ok = true;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % kStages;
+      if (!mbar_wait(full_a + s, (unsigned)(kb / kStages) & 1u)) {  // X and the int8 Q tile have landed
+        ok = false;
+        break;
+      }
+      const int sbi = kb % kBStages;
+      if (kb >= kBStages && !mbar_wait(bempty + sbi, (unsigned)((kb / kBStages) - 1) & 1u)) {
+        ok = false;
+        break;
+      }
+      const uint8_t *raw_tile = sr + (size_t)s * kRBytes;
+      uint8_t *tile = sb + (size_t)sbi * kBBytes;
+      {
+        const uint8_t *rrow = raw_tile + (size_t)r * 64;  // 64-byte swizzle: chunk c at (c ^ ((r >> 1) & 3)) * 16
+        uint8_t *row = tile + (size_t)r * 128;
+        uint4 v[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) v[c] = *(const uint4 *)(rrow + ((c ^ ((r >> 1) & 3)) << 4));
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // 16 int8 -> chunks 2c, 2c + 1 (8 bf16 each) of the 128-byte swizzle
+          uint4 lo, hi;
+          widen16(v[c], lo, hi);
+          *(uint4 *)(row + (((2 * c) ^ (r & 7)) << 4)) = lo;
+          *(uint4 *)(row + (((2 * c + 1) ^ (r & 7)) << 4)) = hi;
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> the tensor cores' reads
+      mbar_arrive(full_b + sbi);
+    }
+    // ---------------------------------------------------------------- epilogue: TMEM -> scale -> bf16 -> Y
+    const bool have = mbar_wait(acc, 0u);
+    if (!have) mbar_drain(acc, 0u);  // the MMAs must be done before TMEM is freed
+    tc_fence_after();
+    if (have && ok) {
+      const int quarter = warp & 3;  // TMEM lanes a warp may access: 32 (warp % 4) ..
+      const int half = (warp - 2) >> 2;  // warps 2-5: columns [0, 128); warps 6-9: [128, 256)
+      const int64_t m = m0 + 32 * quarter + lane;
+#pragma unroll 1
+      for (int c0 = 128 * half; c0 < 128 * half + 128; c0 += 32) {
+        uint32_t v[32];
+        const uint32_t taddr = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+            "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+              "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+              "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (m < A.M) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            float y2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int64_t n = n0 + c0 + j + e;
+              float acc_v = __uint_as_float(v[j + e]);
+              if (A.double_round) acc_v = round_bf16(acc_v);
+              const float sc = n < A.N ? (A.s_bf16 ? bf16_bits_to_f32(((const uint16_t *)A.s)[n]) : ((const float *)A.s)[n])
+                                       : 0.f;
+              y2[e] = acc_v * sc;
+            }
+            packed[j / 2] = (uint32_t)f32_to_bf16_bits(y2[0]) | ((uint32_t)f32_to_bf16_bits(y2[1]) << 16);
+          }
+          uint16_t *dst = A.y + m * A.ldy + n0 + c0;
+          if (n0 + c0 + 32 <= A.N) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ((uint4 *)dst)[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+          } else {
+            for (int j = 0; j < 32 && n0 + c0 + j < A.N; ++j) dst[j] = (uint16_t)(packed[j / 2] >> (16 * (j & 1)));
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBN) : "memory");
+  }
+}
+
+}  // namespace gtc
+}  // namespace egpt
+
+using namespace egpt;
+
+extern "C" int egpt_gemm_i8_tc(void *y, int64_t ldy, const void *x, int64_t ldx, int64_t M, const int8_t *q,
+                               const void *s, int s_dtype, int64_t N, int64_t K, unsigned flags, void *stream) {
+  clear_error();
+  if (!y || !x || !q || !s) return set_error(EGPT_ERR_ARG, "gemm_i8_tc: null pointer");
+  if (s_dtype != EGPT_BF16 && s_dtype != EGPT_F32) return set_error(EGPT_ERR_DTYPE, "gemm_i8_tc: scale dtype");
+  if (M < 1 || N < 1 || K < gtc::kBK || K % gtc::kBK || ldx < K || ldy < N || M > ((int64_t)65535 * gtc::kBM) ||
+      N > ((int64_t)1 << 30) || K > ((int64_t)1 << 20))
+    return set_error(EGPT_ERR_SHAPE, "gemm_i8_tc: bad shape (K a multiple of 64)");
+  if ((uintptr_t)x % 16 || (uintptr_t)y % 16 || (uintptr_t)q % 16 || ldx % 8 || ldy % 8)
+    return set_error(EGPT_ERR_ALIGN, "gemm_i8_tc: x, y, q 16-byte aligned and leading dimensions multiples of 8");
+  auto fn = df::encode_fn();
+  if (!fn) return set_error(EGPT_ERR_LAUNCH, "gemm_i8_tc: this driver does not encode tensor maps");
+  gtc::Args A{};
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+  const cuuint32_t box[2] = {gtc::kBK, gtc::kBM}, es[2] = {1, 1};
+  if (fn(&A.xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), dims, strides, box, es,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return set_error(EGPT_ERR_ALIGN, "gemm_i8_tc: tensor map of x rejected");
+  const cuuint64_t qdims[2] = {(cuuint64_t)K, (cuuint64_t)N};
+  const cuuint64_t qstrides[1] = {(cuuint64_t)K};
+  const cuuint32_t qbox[2] = {gtc::kBK, gtc::kBN};
+  if (fn(&A.qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(q), qdims, qstrides, qbox, es,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return set_error(EGPT_ERR_ALIGN, "gemm_i8_tc: tensor map of q rejected");
+  A.q = q, A.s = s, A.s_bf16 = s_dtype == EGPT_BF16, A.y = (uint16_t *)y;
+  A.M = M, A.N = N, A.K = K, A.ldy = ldy, A.double_round = (flags & EGPT_FLAG_DOUBLE_ROUND) ? 1 : 0;
+  static bool attr = false;
+  if (!attr) {
+    const cudaError_t e = cudaFuncSetAttribute(gtc::gemm_i8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)gtc::kSmem);
+    if (e != cudaSuccess) return check_launch(e, "gemm_i8_tc (shared memory attribute)");
+    attr = true;
+  }
+  const dim3 grid((unsigned)((N + gtc::kBN - 1) / gtc::kBN), (unsigned)((M + gtc::kBM - 1) / gtc::kBM));
+  gtc::gemm_i8_tc_kernel<<<grid, gtc::kThreads, gtc::kSmem, (cudaStream_t)stream>>>(A);
+  return check_launch(cudaGetLastError(), "gemm_i8_tc_kernel");
+}

@@ -10,7 +10,8 @@ Triton (decode) and cuBLAS (prefill).
                     bf16(s) (BASELINE configs 2 and 5), q is computed from the fp32 s as in the reference.
   int8_matmul       int8_linear.py:67-85    <= 16 rows: bf16(s * (x @ q.T)), fp32 accumulation
   int8_linear (op)  int8_linear.py:88-103   bf16 only; > 16 rows reproduces the reference's prefill rounding,
-                    bf16(bf16(x @ q.T) * s), with the same kernel run over 16-row blocks (no cuBLAS)
+                    bf16(bf16(x @ q.T) * s), on the tcgen05 GEMM (csrc/gemm_tc.cu; K a multiple of 64) or the
+                    GEMV kernel over 16-row blocks (other K); no cuBLAS
   Int8Linear        int8_linear.py:120-134
   quantize_model    int8_linear.py:137-157  every nn.Linear incl. lm_head; a tied lm_head becomes an int8 copy
 
@@ -43,7 +44,9 @@ def int8_linear(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor) -> torch.Tens
         return x.new_empty(*x.shape[:-1], w.shape[0])
     if x2.shape[0] <= MAX_DECODE_ROWS:
         y = int8_matmul(x2.contiguous(), w, s)
-    else:  # the reference's prefill branch: bf16 GEMM output, then the scale in fp32
+    elif k % 64 == 0 and w.is_contiguous():  # the reference's prefill branch: bf16 GEMM output, then the scale
+        y = ops.gemm_i8_tc(x2.contiguous(), w, s, double_round=True)
+    else:
         y = ops.gemv_i8_rows(x2.contiguous(), w, s, double_round=True)
     return y.reshape(*x.shape[:-1], w.shape[0])
 

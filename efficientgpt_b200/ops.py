@@ -203,3 +203,20 @@ def argmax_rows(logits):
     L.check(L.load().egpt_argmax_rows(_p(out), _p(x2), x2.shape[0], x2.shape[1], x2.stride(0), _dt(x2), _stream()),
             'argmax_rows')
     return out.reshape(logits.shape[:-1])
+
+
+def gemm_i8_tc(x, w, s, *, double_round=True, out=None):
+    """bf16 [M, K] x int8 [N, K]^T on the tcgen05 tensor cores -> bf16 [M, N]: bf16(bf16(acc) * s) (the reference's
+    >16-row arithmetic) or, with double_round=False, bf16(acc * s). K a multiple of 64."""
+    _cuda(x, w, s)
+    if x.dtype != torch.bfloat16 or w.dtype != torch.int8 or x.dim() != 2 or w.dim() != 2:
+        raise ValueError('gemm_i8_tc: x bf16 [M, K], w int8 [N, K]')
+    m, k = x.shape
+    n = w.shape[0]
+    if w.shape[1] != k or x.stride(1) != 1 or not w.is_contiguous():
+        raise ValueError('gemm_i8_tc: shapes or strides')
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+    L.check(L.load().egpt_gemm_i8_tc(_p(out), out.stride(0), _p(x), x.stride(0), m, _p(w), _p(s), _dt(s), n, k,
+                                     L.FLAG_DOUBLE_ROUND if double_round else 0, _stream()), 'gemm_i8_tc')
+    return out

@@ -4,10 +4,12 @@ replaces: research/realmodel/int8_linear.py:96-97 (`bf16(bf16(x @ bf16(q).T) * s
 the HF Qwen3 forward over the prompt (modeling_qwen3.py:258-335), as GraphGreedyDecoder's prefill runs it
 (research/realmodel/fast_decode.py:77-85).
 
-Prompts of hundreds or thousands of tokens are GEMMs, not GEMVs: the projections run through cuBLAS on the
-dequantised bf16 weights (the reference materialises `bf16(q)` the same way, one layer at a time here), RMSNorm
-and the q/k-norm + RoPE + KV-cache write run on this library's kernels, and causal attention over the prompt
-runs through PyTorch's SDPA (the reference's own prefill attention). Only the KV cache is produced: the caller
+Prompts of hundreds or thousands of tokens are GEMMs, not GEMVs: the projections run on this library's tcgen05 GEMM
+(`egpt_gemm_i8_tc`: the int8 weights are widened to bf16 in shared memory on their way to the tensor cores, where
+the reference materialises `bf16(q)` in HBM on every call), RMSNorm and the q/k-norm + RoPE + KV-cache write run on
+this library's kernels, and causal attention over the prompt runs through PyTorch's SDPA (the reference's own
+prefill attention). Under tensor parallelism the row-sharded projections (o_proj, down_proj) need their unscaled
+fp32 partial products for the cross-rank sum and stay on a cuBLAS GEMM of the dequantised shard. Only the KV cache is produced: the caller
 runs the prompt's last token through the decode step, which writes the first generated token (and, for tensor
 parallelism, exchanges the lm_head keys). With `allreduce` (tensor parallelism) o_proj and down_proj give
 per-rank partial products that are summed across ranks in fp32 before the scale.
@@ -19,8 +21,11 @@ from . import ops
 
 
 def _proj(x, q, s):
-    """bf16(bf16(x @ bf16(q).T) * s): the op's >16-row arithmetic (int8_linear.py:96-97)."""
-    y = torch.matmul(x, q.to(torch.bfloat16).t())
+    """bf16(bf16(x @ bf16(q).T) * s): the op's >16-row arithmetic (int8_linear.py:96-97), on this library's tcgen05
+    GEMM (int8 rows widened to bf16 in shared memory, fp32 accumulation in TMEM)."""
+    if x.shape[-1] % 64 == 0:
+        return ops.gemm_i8_tc(x.contiguous(), q, s, double_round=True)
+    y = torch.matmul(x, q.to(torch.bfloat16).t())  # widths the tcgen05 tiles do not take
     return (y.float() * s.float()).to(torch.bfloat16)
 
 

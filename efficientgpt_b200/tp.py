@@ -188,6 +188,7 @@ class TPQwen3Engine:
         elif world > 1:
             self._map_exchange()
         self.persistent = self.lib.egpt_decode_step_persistent_check(ctypes.byref(self.plan)) == 0
+        self.step_kind = 'persistent' if self.persistent else 'sequence'
         if world > 1 and not self.persistent:
             raise ValueError('the tensor-parallel step needs the persistent kernel: ' + L.last_error())
 

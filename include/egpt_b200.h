@@ -168,6 +168,15 @@ EGPT_API int egpt_attn_decode_noalloc(void *out, int64_t ldo, const void *q, int
  * replaces: logits[:, -1].argmax(-1) (research/realmodel/fast_decode.py:48,84): first index on ties. */
 EGPT_API int egpt_argmax_rows(int64_t *out, const void *logits, int64_t rows, int64_t n, int64_t ld, int dtype, void *stream);
 
+/* ---- int8-weight GEMM for prefill on the tcgen05 tensor cores --------------------------------------------
+ * replaces: research/realmodel/int8_linear.py:96-97, the op's > 16-row branch bf16(bf16(x @ bf16(q).T) * s)
+ * (with EGPT_FLAG_DOUBLE_ROUND; without it bf16(fp32 sum * s)). x bf16 [M, K] (leading dimension ldx),
+ * q int8 [N, K] row-major, s [N] bf16 or fp32, y bf16 [M, N] (leading dimension ldy). fp32 accumulation on
+ * tcgen05.mma (128 x 256 tiles, int8 widened to bf16 in shared memory). K a multiple of 64; x, y, q 16-byte
+ * aligned, ldx and ldy multiples of 8. */
+EGPT_API int egpt_gemm_i8_tc(void *y, int64_t ldy, const void *x, int64_t ldx, int64_t M, const int8_t *q,
+                             const void *s, int s_dtype, int64_t N, int64_t K, unsigned flags, void *stream);
+
 /* ---- stochastic sampling: temperature -> top-k -> top-p -> inverse CDF -------------------------------
  * replaces: filtered_probs + sample_from (research/phase5/sampling.py:39-71; the Triton families
  * temperature_softmax / topk_softmax / inverse_cdf_sample of research/kernelagent/templates.py:131-343).
