@@ -28,7 +28,8 @@ persistent kernel per GPU and token, o_proj / down_proj partial sums exchanged o
 --impl reference times the reference's CPU decode path (oracle/torch_ref.py: the seeded model built, quantised
 and prefilled on the CPU, no GPU and no library of this package) for the same K steps on rank 0.
 
-Other workloads: --workload qwen3_8b (config 5 at any N), nanogpt (config 1), gemv_sweep / attn_sweep (configs 3
+Other workloads: --workload qwen3_8b (config 5 at any N), nanogpt (config 1), gemm_prefill (the prefill GEMMs on
+tcgen05 against the reference's dequantise + cuBLAS arithmetic), gemv_sweep / attn_sweep (configs 3
 and 4, one JSON line per case), profile_step (a small engine for ncu captures: --layers, --steps).
 """
 import argparse
@@ -67,7 +68,8 @@ def parse(argv=None):
                     help='decode step of configs 2 and profile_step (default: the engine\'s choice, dataflow)')
     ap.add_argument('--cpu-sample', type=int, default=16, help='timed CPU decode tokens of cpu_baseline')
     ap.add_argument('--workload', default='qwen3_1.7b',
-                    choices=['qwen3_1.7b', 'qwen3_8b', 'nanogpt', 'gemv_sweep', 'attn_sweep', 'profile_step'])
+                    choices=['qwen3_1.7b', 'qwen3_8b', 'nanogpt', 'gemv_sweep', 'attn_sweep', 'gemm_prefill',
+                             'profile_step'])
     ap.add_argument('--layers', type=int, default=4, help='profile_step: decoder layers')
     ap.add_argument('--reps', type=int, default=50, help='gemv_sweep / attn_sweep: launches per graph')
     ap.add_argument('--only', default='', help='gemv_sweep / attn_sweep: cases whose name contains this text')
@@ -608,6 +610,35 @@ def run_gemv_sweep(a):
         del ws
 
 
+def run_gemm_prefill(a):
+    """Prefill GEMMs of BASELINE config 5 (Qwen3-8B shape, 4096-token prompt) and config 2's gate|up at the same
+    prompt length: egpt_gemm_i8_tc (bf16 x, int8 weights widened in shared memory, tcgen05) against the reference's
+    own arithmetic on PyTorch (dequantise to bf16, cuBLAS GEMM, scale in fp32), both timed as graphs of `reps`
+    launches. Compute-bound: 2 M N K flops against the measured dense bf16 peak."""
+    from efficientgpt_b200 import ops
+    peaks, src = measured_peaks()
+    peak = float(peaks.get('bf16_tflops', 0)) or None
+    m = 4096
+    for what, n, k in (('8B qkv', 6144, 4096), ('8B o', 4096, 4096), ('8B gate_up', 24576, 4096),
+                       ('8B down', 4096, 12288), ('1.7B gate_up', 12288, 2048)):
+        if a.only not in f'prefill {what}':
+            continue
+        g = torch.Generator(device='cuda').manual_seed(n + k)
+        x = torch.randn(m, k, device='cuda', generator=g).to(torch.bfloat16)
+        q = torch.randint(-127, 128, (n, k), dtype=torch.int8, device='cuda', generator=g)
+        sc = (torch.rand(n, device='cuda', generator=g) * 0.019 + 0.001).to(torch.bfloat16)
+        out = torch.empty(m, n, dtype=torch.bfloat16, device='cuda')
+        t_tc = _time_graph(lambda i: ops.gemm_i8_tc(x, q, sc, out=out), a.reps)
+        t_ref = _time_graph(lambda i: ((x @ q.to(torch.bfloat16).t()).float() * sc.float()).to(torch.bfloat16), a.reps)
+        tf = lambda t: 2.0 * m * n * k / (t * 1e-6) / 1e12
+        print(json.dumps({'kernel': 'gemm_i8_tc_kernel', 'case': f'prefill {what} M={m} N={n} K={k}',
+                          'us_tcgen05': round(t_tc, 2), 'tflops_tcgen05': round(tf(t_tc), 1),
+                          'us_reference_torch': round(t_ref, 2), 'tflops_reference_torch': round(tf(t_ref), 1),
+                          'peak_tflops': peak, 'frac_tcgen05': round(tf(t_tc) / peak, 4) if peak else None,
+                          'peak_source': src}), flush=True)
+        del x, q, out
+
+
 def run_attn_sweep(a):
     """16 q / 8 kv heads of 128, one query, L in {512, 2048, 8192, 32768}; graphs of `reps`
     launches over enough cache copies to exceed L2. Algorithmic bytes 4096 L + 8192."""
@@ -673,6 +704,7 @@ def main():
         return
     world, rank, local = dist_setup()
     single = {'nanogpt': lambda: run_nanogpt(a, rank), 'gemv_sweep': lambda: run_gemv_sweep(a),
+              'gemm_prefill': lambda: run_gemm_prefill(a),
               'attn_sweep': lambda: run_attn_sweep(a), 'profile_step': lambda: run_profile_step(a)}
     if a.workload in single:
         if rank == 0:
