@@ -56,7 +56,7 @@ def test_tokens_match_reference_golden(cuda, golden, scale_dtype, semantics):
     assert h == golden['tiny_qwen3']['state_sha256'], 'HF random init changed: golden tokens do not apply'
     key = 'fp32' if scale_dtype == torch.float32 else 'bf16'
     dec = GraphGreedyDecoder(model, max_cache_len=128)
-    exact = 0
+    report = []
     for p, x in gi.tiny_prompts().items():
         run = golden['tiny_qwen3']['runs'][key][str(p)]
         got, st = dec.generate(x.cuda(), 40)
@@ -64,8 +64,18 @@ def test_tokens_match_reference_golden(cuda, golden, scale_dtype, semantics):
         assert len(set(got)) > 8, 'degenerate model output would make equality trivial'
         ok, first, detail = parity.near_tie_match(run['tokens'], run['margins'], run['tops'], got)
         assert ok, (key, p, detail)
-        exact += first is None
-    assert exact >= 1
+        report.append((p, first, None if first is None else run['margins'][first],
+                       None if first is None else parity.bf16_ulp(run['tops'][first])))
+    import warnings
+    warnings.warn(f'tiny Qwen3 {key} scales, {semantics} quantiser: (prompt length, first divergence, reference '
+                  f'top-2 margin there, one bf16 ulp of its top-1 logit) = {report}')
+    # Every prompt identical over all 40 tokens, or its first divergence where the reference's own bf16 logits are
+    # tied to within ONE ulp: the reference's near-tie rule (research/phase5/benchmark_review.py:54-67, margin
+    # < 1e-2) was written for fp32 logits; these logits are bf16, whose spacing above |4| is 0.03125, so the
+    # smallest non-zero margin there is already three times 1e-2, and one rounding step anywhere in the forward
+    # can swap a one-ulp pair. Measured: one or two of the three prompts diverge, at margins 0 or one ulp.
+    assert all(first is None or margin < 1e-2 or margin <= ulp for _, first, margin, ulp in report), report
+    assert sum(first is None for _, first, _, _ in report) >= 1
 
 
 def test_quantized_weights_equal_oracle(cuda):
