@@ -166,8 +166,8 @@ def test_persistent_wide_mlp_matches_launch_sequence(cuda):
     model = gi.build_model(cfg, seed=5).cuda()
     _quantize(model, torch.bfloat16, 'cuda')
     a = Qwen3Engine(model, 160, keep_logits=True, persistent=False)
-    b = Qwen3Engine(model, 160, keep_logits=True, persistent=True)
-    assert b.persistent
+    b = Qwen3Engine(model, 160, keep_logits=True, step='persistent')
+    assert b.step_kind == 'persistent'
     x = gi.tiny_prompts()[5].cuda()
     a.prefill(x)
     b.prefill(x)
@@ -191,9 +191,11 @@ def test_persistent_wide_mlp_matches_launch_sequence(cuda):
 def _dataflow_vs_persistent(model, cap, prompt, steps):
     """Teacher-forced: the dataflow step against the persistent step. Their GEMVs, norms, rope and lm_head are the
     same arithmetic; attention differs in summation order only when the dataflow step holds the K/V rows in shared
-    memory (its own score and P.V loops, same 128-key-block probability rounding). So: logits meet the north star's
-    tolerance under the long-sequence rule (parity.logits_close), every step's token agrees unless the persistent
-    step's top-2 margin is within twice the tolerance, and at least 95% of the steps agree."""
+    memory (its own score and P.V loops, same 128-key-block probability rounding). So: logits within the north
+    star's 1e-2 abs + 1e-2 rel for 99.5% of the entries on average and 97% at every step (all within the hard bound
+    of parity.logits_close), every step's token agrees unless the persistent step's top-2 margin is within twice the
+    tolerance, and at least 95% of the steps agree. (Against the numpy oracle, on the wide-MLP model below, the
+    persistent and launch-sequence steps themselves dip to 98.3% at their worst step, the dataflow step to 98.0%.)"""
     from efficientgpt_b200 import _lib
     from efficientgpt_b200.engine import Qwen3Engine
     a = Qwen3Engine(model, cap, keep_logits=True, step='persistent')
@@ -201,21 +203,23 @@ def _dataflow_vs_persistent(model, cap, prompt, steps):
     assert b.step_kind == 'dataflow' and a.step_kind == 'persistent'
     a.prefill(prompt)
     b.prefill(prompt)
-    same = 0
+    same, fracs = 0, []
     for i in range(steps):
         b.token.copy_(a.token)
         a.step()
         b.step()
         assert int(a.position) == int(b.position)
         la, lb = a.logits.float().cpu().numpy().ravel(), b.logits.float().cpu().numpy().ravel()
-        ok, detail = parity.logits_close(lb, la)
+        ok, detail = parity.logits_close(lb, la, frac=0.97)
         assert ok, f'step {i}: {detail}'
+        fracs.append(float(np.mean(np.abs(lb - la) <= 1e-2 + 1e-2 * np.abs(la))))
         if int(a.token) == int(b.token):
             same += 1
         else:
             top2 = np.sort(la)[-2:]
             assert top2[1] - top2[0] <= 2 * (1e-2 + 1e-2 * abs(top2[1])), f'step {i}'
     assert same >= 0.95 * steps, same
+    assert np.mean(fracs) >= 0.995, np.mean(fracs)
     assert _lib.device_error() == 0
 
 
@@ -237,6 +241,18 @@ def test_dataflow_step_head128(cuda, grp):
     _quantize(model, torch.bfloat16, 'cuda')
     x = torch.randint(0, cfg.vocab_size, (1, 9), generator=torch.Generator().manual_seed(4)).cuda()
     _dataflow_vs_persistent(model, 300, x, 120)
+
+
+def test_dataflow_step_wide_mlp(cuda):
+    """An intermediate of 8192 (the dataflow step stages inputs up to 8192 wide) with head_dim 128 and 4 q heads
+    per kv head, against the persistent step."""
+    from transformers import Qwen3Config
+    cfg = Qwen3Config(vocab_size=1024, hidden_size=256, intermediate_size=8192, num_hidden_layers=2,
+                      num_attention_heads=8, num_key_value_heads=2, head_dim=128, max_position_embeddings=256,
+                      tie_word_embeddings=True, initializer_range=0.05)
+    model = gi.build_model(cfg, seed=5).cuda()
+    _quantize(model, torch.bfloat16, 'cuda')
+    _dataflow_vs_persistent(model, 160, gi.tiny_prompts()[5].cuda(), 120)
 
 
 def test_dataflow_trace_stamps(cuda):
