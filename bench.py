@@ -29,7 +29,7 @@ persistent kernel per GPU and token, o_proj / down_proj partial sums exchanged o
 and prefilled on the CPU, no GPU and no library of this package) for the same K steps on rank 0.
 
 Other workloads: --workload qwen3_8b (config 5 at any N), nanogpt (config 1), gemm_prefill (the prefill GEMMs on
-tcgen05 against the reference's dequantise + cuBLAS arithmetic), gemv_sweep / attn_sweep (configs 3
+tcgen05 against the reference's dequantise + cuBLAS arithmetic), ragged (B = 1, 4, 16 sequences decoded together), gemv_sweep / attn_sweep (configs 3
 and 4, one JSON line per case), profile_step (a small engine for ncu captures: --layers, --steps).
 """
 import argparse
@@ -69,7 +69,7 @@ def parse(argv=None):
     ap.add_argument('--cpu-sample', type=int, default=16, help='timed CPU decode tokens of cpu_baseline')
     ap.add_argument('--workload', default='qwen3_1.7b',
                     choices=['qwen3_1.7b', 'qwen3_8b', 'nanogpt', 'gemv_sweep', 'attn_sweep', 'gemm_prefill',
-                             'profile_step'])
+                             'ragged', 'profile_step'])
     ap.add_argument('--layers', type=int, default=4, help='profile_step: decoder layers')
     ap.add_argument('--reps', type=int, default=50, help='gemv_sweep / attn_sweep: launches per graph')
     ap.add_argument('--only', default='', help='gemv_sweep / attn_sweep: cases whose name contains this text')
@@ -639,6 +639,38 @@ def run_gemm_prefill(a):
         del x, q, out
 
 
+def run_ragged(a):
+    """Ragged small-batch greedy decode (efficientgpt_b200.ragged) on the BASELINE config 2 model: B in {1, 4, 16}
+    sequences with prompt lengths spread over 8..32, `--steps` graph replays timed with CUDA events after the
+    prompts; aggregate tok/s = B x steps / time. The weights stream once per step for the whole batch."""
+    from efficientgpt_b200.configs import qwen3_1p7b_config, random_model
+    from efficientgpt_b200.int8_linear import quantize_model
+    from efficientgpt_b200.ragged import RaggedGraphDecoder
+    cfg = qwen3_1p7b_config()
+    model = random_model(cfg, 'cuda', 0)
+    quantize_model(model, scale_dtype=torch.bfloat16)
+    for b in (1, 4, 16):
+        g = torch.Generator().manual_seed(b)
+        lengths = torch.randint(8, 33, (b,), generator=g)
+        prompts = torch.randint(0, cfg.vocab_size, (b, int(lengths.max())), generator=g)
+        dec = RaggedGraphDecoder(model, b, int(lengths.max()) + a.steps + a.warmup + 1)
+        dec.generate(prompts.cuda(), lengths.cuda(), a.warmup + 1)  # capture, prefill, warm-up replays
+        for r in range(b):
+            dec.engine.prefill_row(r, prompts[r, :int(lengths[r])].cuda())
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            dec.graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / a.steps
+        print(json.dumps({'workload': 'ragged', 'model': 'qwen3_1.7b int8 (config 2 shape)', 'batch': b,
+                          'prompt_lengths': lengths.tolist(), 'steps': a.steps, 'ms_per_step': round(ms, 4),
+                          'tok_s': round(b * 1e3 / ms, 1)}), flush=True)
+        del dec
+
+
 def run_attn_sweep(a):
     """16 q / 8 kv heads of 128, one query, L in {512, 2048, 8192, 32768}; graphs of `reps`
     launches over enough cache copies to exceed L2. Algorithmic bytes 4096 L + 8192."""
@@ -704,7 +736,7 @@ def main():
         return
     world, rank, local = dist_setup()
     single = {'nanogpt': lambda: run_nanogpt(a, rank), 'gemv_sweep': lambda: run_gemv_sweep(a),
-              'gemm_prefill': lambda: run_gemm_prefill(a),
+              'gemm_prefill': lambda: run_gemm_prefill(a), 'ragged': lambda: run_ragged(a),
               'attn_sweep': lambda: run_attn_sweep(a), 'profile_step': lambda: run_profile_step(a)}
     if a.workload in single:
         if rank == 0:

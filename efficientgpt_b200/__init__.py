@@ -3,7 +3,8 @@
 Drop-in for the research/realmodel path of BagelsFun/efficientgpt: `int8_linear` (op, Int8Linear, quantize_model),
 `fast_decode.GraphGreedyDecoder` (and `SampledGraphDecoder` with `sampling`: temperature, top-k, top-p, inverse
 CDF on the device), `backend.BucketedGraphDecoder` (the request-sized decoder pool of HFBackend), plus
-`tp.TPQwen3Engine` (tensor parallelism) and `nanogpt` (config 1), with the
+`ragged.RaggedGraphDecoder` (up to 16 sequences of different lengths), `tp.TPQwen3Engine` (tensor parallelism)
+and `nanogpt` (config 1), with the
 arithmetic in hand-written CUDA (libegpt_b200.so, C-ABI in
 include/egpt_b200.h). Submodules import lazily so the package imports without a GPU.
 """
@@ -18,6 +19,9 @@ def __getattr__(name):
         return getattr(m, name)
     if name in ('GraphGreedyDecoder', 'SampledGraphDecoder'):
         from . import fast_decode as m
+        return getattr(m, name)
+    if name in ('RaggedEngine', 'RaggedGraphDecoder'):  # ragged small-batch decode
+        from . import ragged as m
         return getattr(m, name)
     if name in ('SamplingConfig', 'draw_uniforms', 'sample'):
         from . import sampling as m

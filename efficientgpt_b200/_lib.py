@@ -20,6 +20,7 @@ FLAG_DOUBLE_ROUND, FLAG_RMSNORM, FLAG_PDL, FLAG_EMBED, FLAG_ADVANCE, FLAG_APPEND
 FLAG_REF_SOFTMAX = 128
 FLAG_X_F32 = 256
 FLAG_EXACT = 512
+FLAG_RAGGED = 1024
 
 _VALUE_ERRORS = {EGPT_ERR_SHAPE, EGPT_ERR_DTYPE, EGPT_ERR_ALIGN, EGPT_ERR_ARG, EGPT_ERR_WORKSPACE}
 

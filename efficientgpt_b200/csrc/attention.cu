@@ -72,6 +72,15 @@ struct AttnParams {
   unsigned flags;
 };
 
+// Rows of one sequence (row i at *position + i, one cache) or, with EGPT_FLAG_RAGGED, m sequences (row i at
+// position[i], its own cache: heads [i nkv, (i + 1) nkv) of caches laid out [m nkv][cap][d]).
+__device__ __forceinline__ int64_t row_pos(const AttnParams &p, int64_t row) {
+  return (p.flags & EGPT_FLAG_RAGGED) ? p.position[row] : *p.position + row;
+}
+__device__ __forceinline__ int64_t row_kv_head(const AttnParams &p, int64_t row, int g) {
+  return (p.flags & EGPT_FLAG_RAGGED) ? row * p.nkv + g : g;
+}
+
 // ---------------------------------------------------------------------------------------------- head prologue
 // Normalise (optional) and rotate (optional) one head vector of length d held as bf16 at `src`; the result
 // (bf16-rounded) goes to dst_f (fp32, smem) and, when dst_bf16 is non-null, to global memory as bf16.
@@ -115,7 +124,7 @@ __global__ void qk_norm_rope_append_kernel(AttnParams p, int is_bf16) {
   pdl_launch_dependents();
   const int64_t row = blockIdx.x;
   const int head = blockIdx.y;
-  const int64_t pos = *p.position + row;
+  const int64_t pos = row_pos(p, row);
   const int d = p.d;
   if (pos >= p.cap || pos < 0) {
     if (threadIdx.x == 0) set_device_error(EGPT_ERR_SHAPE);
@@ -127,12 +136,12 @@ __global__ void qk_norm_rope_append_kernel(AttnParams p, int is_bf16) {
       uint16_t *dst = (uint16_t *)p.out + row * p.ldo + (int64_t)head * d;
       head_norm_rope(src, p.q_norm_w, p.eps, p.rope_cos, p.rope_sin, pos, d, outf, dst, tmp, red);
     } else if (head < p.nq + p.nkv) {
-      const int g = head - p.nq;
-      uint16_t *dst = (uint16_t *)p.k_cache + ((int64_t)g * p.cap + pos) * d;
+      const int64_t g = row_kv_head(p, row, head - p.nq);
+      uint16_t *dst = (uint16_t *)p.k_cache + (g * p.cap + pos) * d;
       head_norm_rope(src, p.k_norm_w, p.eps, p.rope_cos, p.rope_sin, pos, d, outf, dst, tmp, red);
     } else {
-      const int g = head - p.nq - p.nkv;
-      uint16_t *dst = (uint16_t *)p.v_cache + ((int64_t)g * p.cap + pos) * d;
+      const int64_t g = row_kv_head(p, row, head - p.nq - p.nkv);
+      uint16_t *dst = (uint16_t *)p.v_cache + (g * p.cap + pos) * d;
       for (int t = threadIdx.x; t < d; t += blockDim.x) dst[t] = src[t];
     }
   } else {  // fp32 (nanoGPT): no norm, no RoPE, plain copies
@@ -141,9 +150,9 @@ __global__ void qk_norm_rope_append_kernel(AttnParams p, int is_bf16) {
     if (head < p.nq)
       dst = (float *)p.out + row * p.ldo + (int64_t)head * d;
     else if (head < p.nq + p.nkv)
-      dst = (float *)p.k_cache + ((int64_t)(head - p.nq) * p.cap + pos) * d;
+      dst = (float *)p.k_cache + (row_kv_head(p, row, head - p.nq) * p.cap + pos) * d;
     else
-      dst = (float *)p.v_cache + ((int64_t)(head - p.nq - p.nkv) * p.cap + pos) * d;
+      dst = (float *)p.v_cache + (row_kv_head(p, row, head - p.nq - p.nkv) * p.cap + pos) * d;
     for (int t = threadIdx.x; t < d; t += blockDim.x) dst[t] = src[t];
   }
 }
@@ -560,7 +569,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
 
   const int g = blockIdx.x, split = blockIdx.y;
   const int64_t row = blockIdx.z;
-  const int64_t pos = *p.position + row;
+  const int64_t pos = row_pos(p, row);
   const int64_t L = pos + 1;
   if (L > p.cap || pos < 0) {
     if (threadIdx.x == 0) set_device_error(EGPT_ERR_SHAPE);
@@ -572,7 +581,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
   const int64_t k0 = (int64_t)split * bps * kRefBlock;
   const int64_t k1 = min(L, k0 + (int64_t)bps * kRefBlock);
 
-  const int64_t kv_base = (int64_t)g * p.cap * D;
+  const int64_t kv_base = row_kv_head(p, row, g) * p.cap * D;
   // ---- q (and, with APPEND, this step's k/v) ----
   if (p.flags & EGPT_FLAG_APPEND) {
     const uint16_t *qkv = (const uint16_t *)p.q + row * p.ldq;
@@ -703,8 +712,8 @@ extern "C" int egpt_attn_decode(void *out, int64_t ldo, const void *q, int64_t l
   if (m < 1 || m > 65535 || cap < 1) return set_error(EGPT_ERR_SHAPE, "attn: bad m or cap");
   if (max_split < 1 || max_split > 1024) return set_error(EGPT_ERR_SHAPE, "attn: max_split must be in [1, 1024]");
   if (dtype != EGPT_BF16 && dtype != EGPT_F32) return set_error(EGPT_ERR_DTYPE, "attn: dtype");
-  if ((flags & EGPT_FLAG_APPEND) && (m != 1 || dtype != EGPT_BF16))
-    return set_error(EGPT_ERR_ARG, "attn: fused append needs m == 1 and bf16");
+  if ((flags & EGPT_FLAG_APPEND) && ((m != 1 && !(flags & EGPT_FLAG_RAGGED)) || dtype != EGPT_BF16))
+    return set_error(EGPT_ERR_ARG, "attn: fused append needs bf16 and m == 1 (or EGPT_FLAG_RAGGED)");
   if ((flags & EGPT_FLAG_APPEND) && ldq < (int64_t)(nq + 2 * nkv) * d) return set_error(EGPT_ERR_SHAPE, "attn: ldq too small for qkv rows");
   if (!(flags & EGPT_FLAG_APPEND) && ldq < (int64_t)nq * d) return set_error(EGPT_ERR_SHAPE, "attn: ldq too small");
   if (ldo < (int64_t)nq * d) return set_error(EGPT_ERR_SHAPE, "attn: ldo too small");

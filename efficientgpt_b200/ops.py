@@ -176,9 +176,11 @@ def attn_ws(m, nq, nkv, d, max_split, device):
 
 
 def attn_decode(q, k_cache, v_cache, position, nq, nkv, d, *, scale, max_split=16, ws=None, out=None, append=False,
-                q_norm_w=None, k_norm_w=None, eps=1e-6, rope_cos=None, rope_sin=None, pdl=False, ref_softmax=False):
+                q_norm_w=None, k_norm_w=None, eps=1e-6, rope_cos=None, rope_sin=None, pdl=False, ref_softmax=False,
+                ragged=False):
     """Split-K decode attention for rows i of q (L_i = *position + i + 1 keys); caches [nkv, cap, d].
-    ref_softmax: round the bf16 probabilities as the reference's GPU SDPA kernel does (128-key block walk)."""
+    ref_softmax: round the bf16 probabilities as the reference's GPU SDPA kernel does (128-key block walk).
+    ragged: row i is its own sequence at position[i] (int64 [m]) with caches [m * nkv, cap, d]."""
     _cuda(q, k_cache, v_cache, position, ws, out, q_norm_w, k_norm_w, rope_cos, rope_sin)
     _contig_rows(q, 'q')
     m = q.shape[0]
@@ -187,7 +189,8 @@ def attn_decode(q, k_cache, v_cache, position, nq, nkv, d, *, scale, max_split=1
         out = torch.empty((m, nq * d), dtype=q.dtype, device=q.device)
     if ws is None:
         ws = attn_ws(m, nq, nkv, d, max_split, q.device)
-    flags = (L.FLAG_APPEND if append else 0) | (L.FLAG_PDL if pdl else 0) | (L.FLAG_REF_SOFTMAX if ref_softmax else 0)
+    flags = ((L.FLAG_APPEND if append else 0) | (L.FLAG_PDL if pdl else 0) | (L.FLAG_REF_SOFTMAX if ref_softmax else 0)
+             | (L.FLAG_RAGGED if ragged else 0))
     L.check(L.load().egpt_attn_decode(_p(out), out.stride(0), _p(q), q.stride(0), _p(k_cache), _p(v_cache), cap,
                                       _p(position), m, nq, nkv, d, _p(q_norm_w), _p(k_norm_w), float(eps), _p(rope_cos),
                                       _p(rope_sin), float(scale), int(max_split), _p(ws), ws.numel(), _dt(q), flags,

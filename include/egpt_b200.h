@@ -58,6 +58,8 @@ extern "C" {
 #define EGPT_FLAG_REF_SOFTMAX 128u /* attention: bf16 probabilities rounded as the reference GPU kernel does */
 #define EGPT_FLAG_X_F32 256u      /* lm_head argmax: x and logits are fp32 (nanoGPT), no bf16 rounding      */
 #define EGPT_FLAG_EXACT 512u      /* GEMV, one bf16 row: exact int8 tensor-core sums, one rounding per row    */
+#define EGPT_FLAG_RAGGED 1024u    /* attention: the m rows are m sequences, row i at position[i] with its own
+                                     cache (kv heads [i nkv, (i + 1) nkv) of caches laid out [m nkv][cap][d]) */
 
 /* ---- library ---------------------------------------------------------------------------------------- */
 EGPT_API const char *egpt_version(void);
@@ -128,8 +130,10 @@ EGPT_API int egpt_embed(void *out, const int64_t *ids, int64_t rows, const void 
  *   rope_cos / rope_sin are bf16 [cap][d/2] (the HF table, cos[i] == cos[i + d/2]).
  *   q_norm_w / k_norm_w may be NULL (no q/k norm: nanoGPT-style attention), rope_cos NULL = no RoPE.
  * egpt_attn_decode: out[i, h] = softmax(scale * q_i,h . K[0..L_i)) V[0..L_i), L_i = pos0 + i + 1, GQA head
- *   h uses kv head h / (nq / nkv). With EGPT_FLAG_APPEND (m must be 1) the norm/RoPE/append above is done
- *   in-kernel from the raw qkv row, else q comes from q (ldq) already rotated.
+ *   h uses kv head h / (nq / nkv). With EGPT_FLAG_APPEND (m must be 1, or any m with EGPT_FLAG_RAGGED) the
+ *   norm/RoPE/append above is done in-kernel from the raw qkv row, else q comes from q (ldq) already rotated.
+ *   With EGPT_FLAG_RAGGED (ragged batches, research/phase5/ragged.py) row i is its own sequence at
+ *   position[i] (position is an int64 array of m) with its own cache heads [i nkv, (i + 1) nkv).
  *   Work is split over up to max_split ranges of whole 128-key blocks per kv head; ws must hold
  *   egpt_attn_ws_bytes(m, nq, nkv, d, max_split) bytes, zero-filled once before first use.
  *   bf16: probabilities enter P.V rounded to bf16. With EGPT_FLAG_REF_SOFTMAX they are rounded relative to
