@@ -34,12 +34,14 @@ namespace gtc {
 constexpr int kBM = 128, kBN = 256, kBK = 64;  // output tile and k block (64 bf16 = one 128-byte swizzle row)
 constexpr int kStages = 5;   // TMA ring: X and int8 Q tiles (latency cover)
 constexpr int kBStages = 2;  // widened Q tiles between the converters and the MMAs
-constexpr int kThreads = 320;
+constexpr int kEpiWarps = 4;          // warps 10-13
+constexpr int kThreads = 320 + 32 * kEpiWarps;
 constexpr int kABytes = kBM * kBK * 2;  // 16 KB: X tile, bf16
 constexpr int kRBytes = kBN * kBK;      // 16 KB: Q tile as loaded, int8
 constexpr int kBBytes = kBN * kBK * 2;  // 32 KB: Q tile widened to bf16
 constexpr int kConvThreads = 256;       // warps 2-9: one Q row each
 constexpr size_t kSmem = 1024 /* alignment slack */ + (size_t)kStages * (kABytes + kRBytes) + (size_t)kBStages * kBBytes + 256;
+static_assert(kThreads == 448, "roles: TMA, MMA, 8 widening warps, 4 epilogue warps");
 
 struct Args {
   CUtensorMap xmap;  // X bf16 [M, K], box {64, 128}, 128-byte swizzle
@@ -151,20 +153,27 @@ __device__ __forceinline__ void widen16(const uint4 v, uint4 &lo, uint4 &hi) {
   hi = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
+__device__ __forceinline__ void tile_of(const Args &A, int64_t t, int64_t mt, int64_t &m0, int64_t &n0) {
+  // consecutive tiles share a weight tile (one N column of tiles, all M tiles): the CTAs running together read
+  // each weight tile once from HBM and the x tiles from L2
+  n0 = (t / mt) * kBN;
+  m0 = (t % mt) * kBM;
+}
+
 __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_constant__ Args A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);  // 1024-aligned operand tiles
   uint8_t *sa = smem;                                      // kStages x [128 rows][128 B], bf16, 128-byte swizzle
-  uint8_t *sb = smem + (size_t)kStages * kABytes;          // kStages x [256 rows][128 B], bf16, 128-byte swizzle
+  uint8_t *sb = smem + (size_t)kStages * kABytes;          // kBStages x [256 rows][128 B], bf16, 128-byte swizzle
   uint8_t *sr = sb + (size_t)kBStages * kBBytes;           // kStages x [256 rows][64 B], int8, 64-byte swizzle
   uint64_t *bars = (uint64_t *)(sr + (size_t)kStages * kRBytes);
-  uint64_t *full_a = bars, *empty = bars + kStages;                 // TMA ring
+  uint64_t *full_a = bars, *empty = bars + kStages;                    // TMA ring
   uint64_t *full_b = bars + 2 * kStages, *bempty = full_b + kBStages;  // widened-Q ring
-  uint64_t *acc = bempty + kBStages;
-  uint32_t *tmem_slot = (uint32_t *)(acc + 1);
+  uint64_t *acc_full = bempty + kBStages, *acc_empty = acc_full + 2;   // two TMEM accumulators
+  uint32_t *tmem_slot = (uint32_t *)(acc_empty + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t m0 = (int64_t)blockIdx.y * kBM, n0 = (int64_t)blockIdx.x * kBN;
   const int nkb = (int)(A.K / kBK);
+  const int64_t mt = (A.M + kBM - 1) / kBM, tiles = mt * ((A.N + kBN - 1) / kBN);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -175,12 +184,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_co
       mbar_init(full_b + s, kConvThreads);
       mbar_init(bempty + s, 1);
     }
-    mbar_init(acc, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(acc_full + s, 1);
+      mbar_init(acc_empty + s, kEpiWarps);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {  // TMEM: 256 fp32 columns x 128 lanes
+  if (warp == 1) {  // TMEM: two accumulators of 256 fp32 columns x 128 lanes
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kBN)
+                 "r"(2 * kBN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -190,58 +202,71 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_co
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- X producer
-    int issued = 0;
+    // ---------------------------------------------------------------- TMA producer: X and int8 Q tiles
     if (lane == 0) {
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % kStages;
-        if (kb >= kStages && !mbar_wait(empty + s, (unsigned)((kb / kStages) - 1) & 1u)) break;
-        mbar_arrive_tx(full_a + s, kABytes + kRBytes);
-        tma_load_2d(sa + (size_t)s * kABytes, &A.xmap, kb * kBK, (int)m0, full_a + s);
-        tma_load_2d(sr + (size_t)s * kRBytes, &A.qmap, kb * kBK, (int)n0, full_a + s);
-        ++issued;
+      int64_t kg = 0;  // k blocks issued by this CTA over all its tiles
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        int64_t m0, n0;
+        tile_of(A, t, mt, m0, n0);
+        for (int kb = 0; kb < nkb; ++kb, ++kg) {
+          const int s = (int)(kg % kStages);
+          if (kg >= kStages && !mbar_wait(empty + s, (unsigned)((kg / kStages) - 1) & 1u)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_tx(full_a + s, kABytes + kRBytes);
+          tma_load_2d(sa + (size_t)s * kABytes, &A.xmap, kb * kBK, (int)m0, full_a + s);
+          tma_load_2d(sr + (size_t)s * kRBytes, &A.qmap, kb * kBK, (int)n0, full_a + s);
+        }
       }
       // none of this CTA's copies may still be landing when it exits
-      for (int kb = max(0, issued - kStages); kb < issued; ++kb) mbar_drain(full_a + kb % kStages, (unsigned)(kb / kStages) & 1u);
+      for (int64_t k = max((int64_t)0, kg - kStages); k < kg; ++k)
+        mbar_drain(full_a + k % kStages, (unsigned)(k / kStages) & 1u);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % kStages, sbi = kb % kBStages;
-        if (!mbar_wait(full_a + s, (unsigned)(kb / kStages) & 1u) ||
-            !mbar_wait(full_b + sbi, (unsigned)(kb / kBStages) & 1u))
-          break;
+      int64_t kg = 0, i = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+        const int buf = (int)(i & 1);
+        if (i >= 2 && !mbar_wait(acc_empty + buf, (unsigned)((i >> 1) - 1) & 1u)) break;  // epilogue drained it
         tc_fence_after();
-        const uint64_t ad = sw128_desc(sa + (size_t)s * kABytes), bd = sw128_desc(sb + (size_t)sbi * kBBytes);
+        const uint32_t acc = tmem + (uint32_t)(buf * kBN);
+        for (int kb = 0; kb < nkb; ++kb, ++kg) {
+          const int s = (int)(kg % kStages), sbi = (int)(kg % kBStages);
+          if (!mbar_wait(full_a + s, (unsigned)(kg / kStages) & 1u) ||
+              !mbar_wait(full_b + sbi, (unsigned)(kg / kBStages) & 1u)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(sa + (size_t)s * kABytes), bd = sw128_desc(sb + (size_t)sbi * kBBytes);
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k)  // 16 bf16 = 32 bytes per step inside the swizzled row
-          umma_f16(tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), (kb | k) != 0 ? 1u : 0u);
-        umma_commit(empty + s);     // the TMA slot is free once these MMAs have read it
-        umma_commit(bempty + sbi);  // and so is the widened-Q slot
+          for (int k = 0; k < kBK / 16; ++k)  // 16 bf16 = 32 bytes per step inside the swizzled row
+            umma_f16(acc, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), (kb | k) != 0 ? 1u : 0u);
+          umma_commit(empty + s);     // the TMA slot is free once these MMAs have read it
+          umma_commit(bempty + sbi);  // and so is the widened-Q slot
+        }
+        umma_commit(acc_full + buf);  // completes when every MMA issued above has finished
       }
-      umma_commit(acc);  // completes when every MMA issued above has finished (also after an early stop)
     }
-  } else {
-    // ---------------------------------------------------------------- Q converters, then the epilogue
+  } else if (warp < 2 + kConvThreads / 32) {
+    // ---------------------------------------------------------------- Q converters
     const int r = threadIdx.x - 64;  // the Q row (of the 256-row tile) this thread widens
+    int64_t kg = 0;
     bool ok = true;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % kStages;
-      if (!mbar_wait(full_a + s, (unsigned)(kb / kStages) & 1u)) {  // X and the int8 Q tile have landed
-        ok = false;
-        break;
-      }
-      const int sbi = kb % kBStages;
-      if (kb >= kBStages && !mbar_wait(bempty + sbi, (unsigned)((kb / kBStages) - 1) & 1u)) {
-        ok = false;
-        break;
-      }
-      const uint8_t *raw_tile = sr + (size_t)s * kRBytes;
-      uint8_t *tile = sb + (size_t)sbi * kBBytes;
-      {
-        const uint8_t *rrow = raw_tile + (size_t)r * 64;  // 64-byte swizzle: chunk c at (c ^ ((r >> 1) & 3)) * 16
-        uint8_t *row = tile + (size_t)r * 128;
+    for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      for (int kb = 0; kb < nkb; ++kb, ++kg) {
+        const int s = (int)(kg % kStages), sbi = (int)(kg % kBStages);
+        if (!mbar_wait(full_a + s, (unsigned)(kg / kStages) & 1u) ||
+            (kg >= kBStages && !mbar_wait(bempty + sbi, (unsigned)((kg / kBStages) - 1) & 1u))) {
+          ok = false;
+          break;
+        }
+        const uint8_t *rrow = sr + (size_t)s * kRBytes + (size_t)r * 64;  // chunk c at (c ^ ((r >> 1) & 3)) * 16
+        uint8_t *row = sb + (size_t)sbi * kBBytes + (size_t)r * 128;
         uint4 v[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) v[c] = *(const uint4 *)(rrow + ((c ^ ((r >> 1) & 3)) << 4));
@@ -252,22 +277,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_co
           *(uint4 *)(row + (((2 * c) ^ (r & 7)) << 4)) = lo;
           *(uint4 *)(row + (((2 * c + 1) ^ (r & 7)) << 4)) = hi;
         }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> the tensor cores' reads
+        mbar_arrive(full_b + sbi);
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> the tensor cores' reads
-      mbar_arrive(full_b + sbi);
     }
+  } else {
     // ---------------------------------------------------------------- epilogue: TMEM -> scale -> bf16 -> Y
-    const bool have = mbar_wait(acc, 0u);
-    if (!have) mbar_drain(acc, 0u);  // the MMAs must be done before TMEM is freed
-    tc_fence_after();
-    if (have && ok) {
-      const int quarter = warp & 3;  // TMEM lanes a warp may access: 32 (warp % 4) ..
-      const int half = (warp - 2) >> 2;  // warps 2-5: columns [0, 128); warps 6-9: [128, 256)
+    const int quarter = warp & 3;  // TMEM lanes a warp may access: 32 (warp % 4) ..
+    int64_t i = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const int buf = (int)(i & 1);
+      if (!mbar_wait(acc_full + buf, (unsigned)(i >> 1) & 1u)) break;
+      tc_fence_after();
+      int64_t m0, n0;
+      tile_of(A, t, mt, m0, n0);
       const int64_t m = m0 + 32 * quarter + lane;
 #pragma unroll 1
-      for (int c0 = 128 * half; c0 < 128 * half + 128; c0 += 32) {
+      for (int c0 = 0; c0 < kBN; c0 += 32) {
         uint32_t v[32];
-        const uint32_t taddr = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0;
+        const uint32_t taddr = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(buf * kBN + c0);
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
             "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
@@ -302,13 +330,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_co
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty + buf);  // the MMAs of tile i + 2 may overwrite this accumulator
     }
+  }
+  // every MMA this CTA issued has completed before TMEM is freed: the epilogue waited for each accumulator it
+  // read; on an early stop, wait here (bounded) for the last commit of each buffer that was used
+  if (warp == 1 && lane == 0) {
+    int64_t used = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) ++used;
+    for (int64_t i = max((int64_t)0, used - 2); i < used; ++i) mbar_drain(acc_full + (i & 1), (unsigned)(i >> 1) & 1u);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kBN) : "memory");
   }
 }
 
@@ -322,7 +360,7 @@ extern "C" int egpt_gemm_i8_tc(void *y, int64_t ldy, const void *x, int64_t ldx,
   clear_error();
   if (!y || !x || !q || !s) return set_error(EGPT_ERR_ARG, "gemm_i8_tc: null pointer");
   if (s_dtype != EGPT_BF16 && s_dtype != EGPT_F32) return set_error(EGPT_ERR_DTYPE, "gemm_i8_tc: scale dtype");
-  if (M < 1 || N < 1 || K < gtc::kBK || K % gtc::kBK || ldx < K || ldy < N || M > ((int64_t)65535 * gtc::kBM) ||
+  if (M < 1 || N < 1 || K < gtc::kBK || K % gtc::kBK || ldx < K || ldy < N || M > ((int64_t)1 << 31) ||
       N > ((int64_t)1 << 30) || K > ((int64_t)1 << 20))
     return set_error(EGPT_ERR_SHAPE, "gemm_i8_tc: bad shape (K a multiple of 64)");
   if ((uintptr_t)x % 16 || (uintptr_t)y % 16 || (uintptr_t)q % 16 || ldx % 8 || ldy % 8)
@@ -353,7 +391,8 @@ extern "C" int egpt_gemm_i8_tc(void *y, int64_t ldy, const void *x, int64_t ldx,
     if (e != cudaSuccess) return check_launch(e, "gemm_i8_tc (shared memory attribute)");
     attr = true;
   }
-  const dim3 grid((unsigned)((N + gtc::kBN - 1) / gtc::kBN), (unsigned)((M + gtc::kBM - 1) / gtc::kBM));
+  const int64_t tiles = ((N + gtc::kBN - 1) / gtc::kBN) * ((M + gtc::kBM - 1) / gtc::kBM);
+  const unsigned grid = (unsigned)std::min<int64_t>(tiles, (int64_t)egpt_num_sms());  // persistent: one CTA per SM
   gtc::gemm_i8_tc_kernel<<<grid, gtc::kThreads, gtc::kSmem, (cudaStream_t)stream>>>(A);
   return check_launch(cudaGetLastError(), "gemm_i8_tc_kernel");
 }
