@@ -28,7 +28,7 @@ from . import ops
 from .int8_linear import Int8Linear
 
 
-PREFILL_GEMM_MIN = 256  # prompts longer than this take the GEMM prefill
+PREFILL_GEMM_MIN = 16  # prompts longer than this take the GEMM prefill (the op's own branch point, > 16 rows)
 
 
 def _ptr(t):
@@ -226,20 +226,21 @@ class Qwen3Engine:
     @torch.no_grad()
     def prefill(self, input_ids):
         """Run the prompt (int64 [p] or [1, p] on the device) from position 0; leaves token = first generated id
-        and position = p. Returns the token tensor (device). Prompts longer than PREFILL_GEMM_MIN tokens fill the
-        KV cache with the GEMM prefill (efficientgpt_b200.prefill) and run their last token through the decode
-        step; shorter ones run the per-stage kernels on 16-row blocks."""
+        and position = p. Returns the token tensor (device). Prompts longer than PREFILL_GEMM_MIN tokens (the
+        reference op's >16-row branch) run the GEMM prefill (efficientgpt_b200.prefill: tcgen05 projections with
+        the >16-row rounding, SDPA over the prompt) up to the last row's hidden state, then the final norm and the
+        lm_head argmax on that row; shorter ones run the per-stage kernels on one block of rows."""
         ids = input_ids.reshape(-1).to(device=self.device, dtype=torch.int64).contiguous()
         p = ids.numel()
         if p < 1 or p > self.cap:
             raise ValueError('prompt length must be in [1, max_cache_len]')
         if p > PREFILL_GEMM_MIN:
             from .prefill import fill_kv
-            fill_kv(ids[:-1], self.layers, self.embed, self.kv, self.rope_cos, self.rope_sin, self.nq, self.nkv,
-                    self.d, self.eps)
-            self.position.fill_(p - 1)
-            self.token.copy_(ids[-1:])
-            self.step()
+            h_last = fill_kv(ids, self.layers, self.embed, self.kv, self.rope_cos, self.rope_sin, self.nq, self.nkv,
+                             self.d, self.eps, last_hidden=True)
+            ops.lm_head_argmax(h_last[0], self.w_lm, self.s_lm, self.lm_ws, norm_w=self.final_norm, eps=self.eps,
+                               logits=self.logits, token=self.token)
+            self.position.fill_(p)
             return self.token
         self.position.zero_()
         h = ops.embed(ids, self.embed)

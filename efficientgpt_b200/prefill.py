@@ -1,18 +1,17 @@
-"""Long-prompt prefill of the Qwen3 engines: the reference's >16-row int8 branch as a plain library GEMM.
+"""Prompt prefill of the Qwen3 engines: the reference's >16-row int8 branch on this library's tcgen05 GEMM.
 
 replaces: research/realmodel/int8_linear.py:96-97 (`bf16(bf16(x @ bf16(q).T) * s)` for more than 16 rows) inside
 the HF Qwen3 forward over the prompt (modeling_qwen3.py:258-335), as GraphGreedyDecoder's prefill runs it
 (research/realmodel/fast_decode.py:77-85).
 
-Prompts of hundreds or thousands of tokens are GEMMs, not GEMVs: the projections run on this library's tcgen05 GEMM
-(`egpt_gemm_i8_tc`: the int8 weights are widened to bf16 in shared memory on their way to the tensor cores, where
-the reference materialises `bf16(q)` in HBM on every call), RMSNorm and the q/k-norm + RoPE + KV-cache write run on
-this library's kernels, and causal attention over the prompt runs through PyTorch's SDPA (the reference's own
-prefill attention). Under tensor parallelism the row-sharded projections (o_proj, down_proj) need their unscaled
-fp32 partial products for the cross-rank sum and stay on a cuBLAS GEMM of the dequantised shard. Only the KV cache is produced: the caller
-runs the prompt's last token through the decode step, which writes the first generated token (and, for tensor
-parallelism, exchanges the lm_head keys). With `allreduce` (tensor parallelism) o_proj and down_proj give
-per-rank partial products that are summed across ranks in fp32 before the scale.
+Prompts of more than 16 tokens are GEMMs, not GEMVs: the projections run on `egpt_gemm_i8_tc` (the int8 weights are
+widened to bf16 in shared memory on their way to the tensor cores, where the reference materialises `bf16(q)` in HBM
+on every call), RMSNorm and the q/k-norm + RoPE + KV-cache write run on this library's kernels, and causal attention
+over the prompt runs through PyTorch's SDPA (the reference's own prefill attention). The one-GPU engine takes the
+last prompt row's hidden state (`last_hidden`) to its final norm and lm_head; the tensor-parallel engine fills the
+cache of all but the last token and runs that one through its decode step, which exchanges the lm_head keys. With
+`allreduce` (tensor parallelism) o_proj and down_proj give per-rank unscaled fp32 partial products (a cuBLAS GEMM of
+the dequantised shard) that are summed across ranks before the scale.
 """
 import torch
 import torch.nn.functional as F
@@ -38,11 +37,14 @@ def _proj_partial(x, q, s, allreduce):
 
 
 @torch.no_grad()
-def fill_kv(ids, layers, embed, kv, rope_cos, rope_sin, nq, nkv, d, eps, allreduce=None):
+def fill_kv(ids, layers, embed, kv, rope_cos, rope_sin, nq, nkv, d, eps, allreduce=None, last_hidden=False):
     """KV cache entries of positions 0 .. len(ids) - 1 for the prompt `ids` (int64 [p] on the device).
 
     layers: fused per-layer weights (w_qkv, s_qkv, w_o, s_o, w_gu, s_gu, w_down, s_down, ln_in, ln_post, q_norm,
     k_norm), this rank's shard under tensor parallelism (nq, nkv the rank's heads); kv [L, 2, nkv, cap, d] bf16.
+    last_hidden: also run the last layer for the last prompt row (its attention over the whole prompt, o_proj and
+    MLP with the same >16-row arithmetic) and return that row's hidden state [1, hidden], for the caller's final
+    norm and lm_head; otherwise return p.
     """
     p = ids.numel()
     dev = ids.device
@@ -54,8 +56,19 @@ def fill_kv(ids, layers, embed, kv, rope_cos, rope_sin, nq, nkv, d, eps, allredu
         qkv = _proj(x, lay['w_qkv'], lay['s_qkv'])
         q = ops.qk_norm_rope_kv_append(qkv, kv[i, 0], kv[i, 1], pos0, nq, nkv, d, q_norm_w=lay['q_norm'],
                                        k_norm_w=lay['k_norm'], eps=eps, rope_cos=rope_cos, rope_sin=rope_sin)
-        if i == len(layers) - 1:  # the last layer's keys and values are all the decode step needs
-            break
+        if i == len(layers) - 1:
+            if not last_hidden:  # the last layer's keys and values are all the decode step needs
+                break
+            # the last layer only matters for the last row: its attention over the prompt, then o_proj and the MLP
+            # on that row (the per-element arithmetic of the >16-row branch does not depend on the row count)
+            qh = q[p - 1:p].view(1, nq, d).transpose(0, 1).unsqueeze(0)
+            kh, vh = kv[i, 0, :, :p].unsqueeze(0), kv[i, 1, :, :p].unsqueeze(0)
+            a = F.scaled_dot_product_attention(qh, kh, vh, scale=d ** -0.5, enable_gqa=nq != nkv)
+            a = a[0].transpose(0, 1).reshape(1, nq * d)
+            hl = h[p - 1:p] + _proj(a, lay['w_o'], lay['s_o'])
+            x = ops.rmsnorm(hl, lay['ln_post'], eps)
+            gu = _proj(x, lay['w_gu'], lay['s_gu'])
+            return hl + _proj(F.silu(gu[:, :inter]) * gu[:, inter:], lay['w_down'], lay['s_down'])
         qh = q.view(p, nq, d).transpose(0, 1).unsqueeze(0)
         kh, vh = kv[i, 0, :, :p].unsqueeze(0), kv[i, 1, :, :p].unsqueeze(0)
         a = F.scaled_dot_product_attention(qh, kh, vh, is_causal=True, scale=d ** -0.5, enable_gqa=nq != nkv)
