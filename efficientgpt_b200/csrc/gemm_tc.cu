@@ -52,6 +52,8 @@ struct Args {
   uint16_t *y;
   int64_t M, N, K, ldy;
   int double_round;
+  int ksplit;     // k ranges per output tile (work unit = tile x range); > 1: fp32 partials into ws, then reduce
+  float *ws;      // [ksplit][M][N] fp32 partial sums (ksplit > 1)
 };
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
@@ -174,6 +176,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_co
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb = (int)(A.K / kBK);
   const int64_t mt = (A.M + kBM - 1) / kBM, tiles = mt * ((A.N + kBN - 1) / kBN);
+  const int S = A.ksplit;
+  const int64_t units = tiles * S;
+  // work unit u: tile u / S, k blocks [kb_lo(u), kb_lo(u) + kb_n(u))
+  auto kb_lo = [&](int64_t u) { return (int)((int64_t)(u % S) * nkb / S); };
+  auto kb_n = [&](int64_t u) { return (int)((int64_t)(u % S + 1) * nkb / S) - kb_lo(u); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -206,10 +213,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_co
     if (lane == 0) {
       int64_t kg = 0;  // k blocks issued by this CTA over all its tiles
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
         int64_t m0, n0;
-        tile_of(A, t, mt, m0, n0);
-        for (int kb = 0; kb < nkb; ++kb, ++kg) {
+        tile_of(A, u / S, mt, m0, n0);
+        for (int kb = kb_lo(u), ke = kb_lo(u) + kb_n(u); kb < ke; ++kb, ++kg) {
           const int s = (int)(kg % kStages);
           if (kg >= kStages && !mbar_wait(empty + s, (unsigned)((kg / kStages) - 1) & 1u)) {
             ok = false;
@@ -229,12 +236,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_co
     if (lane == 0) {
       int64_t kg = 0, i = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+      for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x, ++i) {
         const int buf = (int)(i & 1);
         if (i >= 2 && !mbar_wait(acc_empty + buf, (unsigned)((i >> 1) - 1) & 1u)) break;  // epilogue drained it
         tc_fence_after();
         const uint32_t acc = tmem + (uint32_t)(buf * kBN);
-        for (int kb = 0; kb < nkb; ++kb, ++kg) {
+        const int kb0 = kb_lo(u);
+        for (int kb = kb0, ke = kb0 + kb_n(u); kb < ke; ++kb, ++kg) {
           const int s = (int)(kg % kStages), sbi = (int)(kg % kBStages);
           if (!mbar_wait(full_a + s, (unsigned)(kg / kStages) & 1u) ||
               !mbar_wait(full_b + sbi, (unsigned)(kg / kBStages) & 1u)) {
@@ -245,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_co
           const uint64_t ad = sw128_desc(sa + (size_t)s * kABytes), bd = sw128_desc(sb + (size_t)sbi * kBBytes);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k)  // 16 bf16 = 32 bytes per step inside the swizzled row
-            umma_f16(acc, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), (kb | k) != 0 ? 1u : 0u);
+            umma_f16(acc, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), (kb != kb0 || k != 0) ? 1u : 0u);
           umma_commit(empty + s);     // the TMA slot is free once these MMAs have read it
           umma_commit(bempty + sbi);  // and so is the widened-Q slot
         }
@@ -257,8 +265,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_co
     const int r = threadIdx.x - 64;  // the Q row (of the 256-row tile) this thread widens
     int64_t kg = 0;
     bool ok = true;
-    for (int64_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-      for (int kb = 0; kb < nkb; ++kb, ++kg) {
+    for (int64_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      for (int kb = 0, ke = kb_n(u); kb < ke; ++kb, ++kg) {
         const int s = (int)(kg % kStages), sbi = (int)(kg % kBStages);
         if (!mbar_wait(full_a + s, (unsigned)(kg / kStages) & 1u) ||
             (kg >= kBStages && !mbar_wait(bempty + sbi, (unsigned)((kg / kBStages) - 1) & 1u))) {
@@ -285,12 +293,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_co
     // ---------------------------------------------------------------- epilogue: TMEM -> scale -> bf16 -> Y
     const int quarter = warp & 3;  // TMEM lanes a warp may access: 32 (warp % 4) ..
     int64_t i = 0;
-    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+    for (int64_t u = blockIdx.x; u < units; u += gridDim.x, ++i) {
       const int buf = (int)(i & 1);
       if (!mbar_wait(acc_full + buf, (unsigned)(i >> 1) & 1u)) break;
       tc_fence_after();
       int64_t m0, n0;
-      tile_of(A, t, mt, m0, n0);
+      tile_of(A, u / S, mt, m0, n0);
       const int64_t m = m0 + 32 * quarter + lane;
 #pragma unroll 1
       for (int c0 = 0; c0 < kBN; c0 += 32) {
@@ -305,7 +313,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_co
               "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (m < A.M) {
+        if (S > 1) {  // k range partial: the raw fp32 sums, reduced (and scaled) by gemm_reduce_kernel
+          if (m < A.M) {
+            float *dst = A.ws + ((int64_t)(u % S) * A.M + m) * A.N + n0 + c0;
+            if (n0 + c0 + 32 <= A.N) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) ((uint4 *)dst)[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            } else {
+              for (int j = 0; j < 32 && n0 + c0 + j < A.N; ++j) dst[j] = __uint_as_float(v[j]);
+            }
+          }
+        } else if (m < A.M) {
           uint32_t packed[16];
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
@@ -339,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_co
   // read; on an early stop, wait here (bounded) for the last commit of each buffer that was used
   if (warp == 1 && lane == 0) {
     int64_t used = 0;
-    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) ++used;
+    for (int64_t u = blockIdx.x; u < units; u += gridDim.x) ++used;
     for (int64_t i = max((int64_t)0, used - 2); i < used; ++i) mbar_drain(acc_full + (i & 1), (unsigned)(i >> 1) & 1u);
   }
   tc_fence_before();
@@ -350,13 +368,47 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_co
   }
 }
 
+// y[m, n] = bf16(bf16(sum_s ws[s][m][n]) * s[n]) (double rounding) or bf16(sum * s[n]); the k ranges in order.
+__global__ void __launch_bounds__(256) gemm_reduce_kernel(const __grid_constant__ Args A) {
+  const int64_t pairs = A.M * (A.N / 2);
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < pairs; i += (int64_t)gridDim.x * 256) {
+    const int64_t m = i / (A.N / 2), n = 2 * (i - m * (A.N / 2));
+    float acc0 = 0.f, acc1 = 0.f;
+    for (int s = 0; s < A.ksplit; ++s) {
+      const float2 v = *(const float2 *)(A.ws + ((int64_t)s * A.M + m) * A.N + n);
+      acc0 += v.x;
+      acc1 += v.y;
+    }
+    if (A.double_round) acc0 = round_bf16(acc0), acc1 = round_bf16(acc1);
+    const float s0 = A.s_bf16 ? bf16_bits_to_f32(((const uint16_t *)A.s)[n]) : ((const float *)A.s)[n];
+    const float s1 = A.s_bf16 ? bf16_bits_to_f32(((const uint16_t *)A.s)[n + 1]) : ((const float *)A.s)[n + 1];
+    *(uint32_t *)(A.y + m * A.ldy + n) = (uint32_t)f32_to_bf16_bits(acc0 * s0) | ((uint32_t)f32_to_bf16_bits(acc1 * s1) << 16);
+  }
+}
+
+// k ranges per tile so that the work units fill about one wave of the GPU, each range at least 4 k blocks.
+inline int choose_ksplit(int64_t M, int64_t N, int64_t K, int sms) {
+  const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+  const int64_t nkb = K / kBK;
+  int64_t s = (sms + tiles - 1) / tiles;
+  s = std::min<int64_t>(s, std::max<int64_t>(1, nkb / 4));
+  return (int)std::max<int64_t>(1, std::min<int64_t>(s, 16));
+}
+
 }  // namespace gtc
 }  // namespace egpt
 
 using namespace egpt;
 
+extern "C" size_t egpt_gemm_i8_tc_ws_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M < 1 || N < 1 || K < gtc::kBK) return 0;
+  const int S = gtc::choose_ksplit(M, N, K, num_sms());
+  return S > 1 ? (size_t)S * M * N * 4 : 0;
+}
+
 extern "C" int egpt_gemm_i8_tc(void *y, int64_t ldy, const void *x, int64_t ldx, int64_t M, const int8_t *q,
-                               const void *s, int s_dtype, int64_t N, int64_t K, unsigned flags, void *stream) {
+                               const void *s, int s_dtype, int64_t N, int64_t K, unsigned flags, void *ws,
+                               size_t ws_bytes, void *stream) {
   clear_error();
   if (!y || !x || !q || !s) return set_error(EGPT_ERR_ARG, "gemm_i8_tc: null pointer");
   if (s_dtype != EGPT_BF16 && s_dtype != EGPT_F32) return set_error(EGPT_ERR_DTYPE, "gemm_i8_tc: scale dtype");
@@ -384,6 +436,12 @@ extern "C" int egpt_gemm_i8_tc(void *y, int64_t ldy, const void *x, int64_t ldx,
     return set_error(EGPT_ERR_ALIGN, "gemm_i8_tc: tensor map of q rejected");
   A.q = q, A.s = s, A.s_bf16 = s_dtype == EGPT_BF16, A.y = (uint16_t *)y;
   A.M = M, A.N = N, A.K = K, A.ldy = ldy, A.double_round = (flags & EGPT_FLAG_DOUBLE_ROUND) ? 1 : 0;
+  // split K over several CTAs per output tile when the tiles alone leave SMs idle (few rows: decode batches,
+  // short prompts), given the workspace for the fp32 partials; else one range per tile
+  A.ksplit = 1;
+  const int S = gtc::choose_ksplit(M, N, K, num_sms());
+  if (S > 1 && ws && ws_bytes >= (size_t)S * M * N * 4 && (uintptr_t)ws % 16 == 0 && N % 2 == 0)
+    A.ksplit = S, A.ws = (float *)ws;
   static bool attr = false;
   if (!attr) {
     const cudaError_t e = cudaFuncSetAttribute(gtc::gemm_i8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -391,8 +449,13 @@ extern "C" int egpt_gemm_i8_tc(void *y, int64_t ldy, const void *x, int64_t ldx,
     if (e != cudaSuccess) return check_launch(e, "gemm_i8_tc (shared memory attribute)");
     attr = true;
   }
-  const int64_t tiles = ((N + gtc::kBN - 1) / gtc::kBN) * ((M + gtc::kBM - 1) / gtc::kBM);
-  const unsigned grid = (unsigned)std::min<int64_t>(tiles, (int64_t)egpt_num_sms());  // persistent: one CTA per SM
+  const int64_t units = ((N + gtc::kBN - 1) / gtc::kBN) * ((M + gtc::kBM - 1) / gtc::kBM) * A.ksplit;
+  const unsigned grid = (unsigned)std::min<int64_t>(units, (int64_t)num_sms());  // persistent: one CTA per SM
   gtc::gemm_i8_tc_kernel<<<grid, gtc::kThreads, gtc::kSmem, (cudaStream_t)stream>>>(A);
-  return check_launch(cudaGetLastError(), "gemm_i8_tc_kernel");
+  int rc = check_launch(cudaGetLastError(), "gemm_i8_tc_kernel");
+  if (rc != EGPT_OK || A.ksplit == 1) return rc;
+  const int64_t pairs = M * (N / 2);
+  const unsigned rgrid = (unsigned)std::min<int64_t>((pairs + 255) / 256, (int64_t)num_sms() * 8);
+  gtc::gemm_reduce_kernel<<<rgrid, 256, 0, (cudaStream_t)stream>>>(A);
+  return check_launch(cudaGetLastError(), "gemm_reduce_kernel");
 }

@@ -208,9 +208,10 @@ def argmax_rows(logits):
     return out.reshape(logits.shape[:-1])
 
 
-def gemm_i8_tc(x, w, s, *, double_round=True, out=None):
+def gemm_i8_tc(x, w, s, *, double_round=True, out=None, ws=None):
     """bf16 [M, K] x int8 [N, K]^T on the tcgen05 tensor cores -> bf16 [M, N]: bf16(bf16(acc) * s) (the reference's
-    >16-row arithmetic) or, with double_round=False, bf16(acc * s). K a multiple of 64."""
+    >16-row arithmetic) or, with double_round=False, bf16(acc * s). K a multiple of 64. Few rows split K over
+    several CTAs per tile with an fp32 workspace (allocated here unless `ws` is given)."""
     _cuda(x, w, s)
     if x.dtype != torch.bfloat16 or w.dtype != torch.int8 or x.dim() != 2 or w.dim() != 2:
         raise ValueError('gemm_i8_tc: x bf16 [M, K], w int8 [N, K]')
@@ -220,6 +221,10 @@ def gemm_i8_tc(x, w, s, *, double_round=True, out=None):
         raise ValueError('gemm_i8_tc: shapes or strides')
     if out is None:
         out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+    need = int(L.load().egpt_gemm_i8_tc_ws_bytes(m, n, k))
+    if ws is None and need:
+        ws = torch.empty(need, dtype=torch.uint8, device=x.device)
     L.check(L.load().egpt_gemm_i8_tc(_p(out), out.stride(0), _p(x), x.stride(0), m, _p(w), _p(s), _dt(s), n, k,
-                                     L.FLAG_DOUBLE_ROUND if double_round else 0, _stream()), 'gemm_i8_tc')
+                                     L.FLAG_DOUBLE_ROUND if double_round else 0, _p(ws),
+                                     0 if ws is None else ws.numel(), _stream()), 'gemm_i8_tc')
     return out

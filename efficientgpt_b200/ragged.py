@@ -10,8 +10,9 @@ bit-identical to the batch-1 step, which uses the exact one-row kernel).
 Per step, on the device (one CUDA graph per step in RaggedGraphDecoder): the B token embeddings, per layer RMSNorm
 over the B rows, the q|k|v, o, gate|up (SiLU·up) and down (residual) projections over all B rows at once, so the
 weights stream once per step for the whole batch (the point of small-batch decode, int8_linear.py:18
-MAX_DECODE_ROWS): for 8..16 rows on the tcgen05 GEMM (egpt_gemm_i8_tc with one rounding, bf16(acc * s), then the
-epilogue at the reference's rounding points), for fewer on the GEMV kernel; one attention launch for the B
+MAX_DECODE_ROWS): for 4..16 rows on the tcgen05 GEMM (egpt_gemm_i8_tc with one rounding, bf16(acc * s), K split
+over several CTAs per weight tile, then the epilogue at the reference's rounding points), for fewer on the GEMV
+kernel; one attention launch for the B
 sequences (egpt_attn_decode with
 EGPT_FLAG_RAGGED | EGPT_FLAG_APPEND: row b's q/k RMSNorm, RoPE at position[b] and K/V append into its own cache
 heads, then its own causal range); the final norm, the lm_head projection over the B rows and a row-wise argmax.
@@ -57,23 +58,31 @@ class RaggedEngine:
         self.max_split = attn_max_split
         self.attn_ws = ops.attn_ws(batch, b.nq, b.nkv, b.d, attn_max_split, b.device)
         self.logits = torch.empty(batch, b.vocab, dtype=torch.bfloat16, device=b.device)
-        # 8..16 rows: the projections on the tcgen05 GEMM (one 128-row tile holds the batch); fewer rows: the GEMV
-        # kernel (measured on the config-2 model: B = 4 3.22 ms per step on the GEMV against 5.42 on the GEMM,
-        # B = 16 10.43 ms against 5.42: the GEMM's cost is its few weight-tile CTAs, nearly flat in B)
+        # 4..16 rows: the projections on the tcgen05 GEMM (one 128-row tile holds the batch, K split over several
+        # CTAs per weight tile); fewer rows: the GEMV kernel. Measured on the config-2 model: B = 16 2.93 ms per
+        # step on the GEMM against 10.43 on the GEMV; B = 4 3.22 ms on the GEMV; B = 1 1.83 ms on the GEMV
         dims = (b.hidden, b.inter, b.nq * b.d)
-        self.use_gemm = batch >= 8 and all(k % 64 == 0 for k in dims)
+        self.use_gemm = batch >= 4 and all(k % 64 == 0 for k in dims)
+        self.gemm_ws = {}  # fp32 split-K workspaces per (N, K), reused by every step (and by the captured graph)
 
     def _proj(self, x, w, s, epilogue=L.EPI_NONE, residual=None):
         """bf16(acc * s) over the batch rows, then the epilogue at the reference's rounding points."""
         if not self.use_gemm:
             return ops.gemv_i8(x, w, s, epilogue=epilogue, residual=residual)
-        y = ops.gemm_i8_tc(x, w, s, double_round=False)
+        y = ops.gemm_i8_tc(x, w, s, double_round=False, ws=self._ws(w))
         if epilogue == L.EPI_RESIDUAL:
             return residual + y
         if epilogue == L.EPI_SILU_MUL:
             half = y.shape[1] // 2
             return torch.nn.functional.silu(y[:, :half]) * y[:, half:]
         return y
+
+    def _ws(self, w):
+        n, k = w.shape
+        if (n, k) not in self.gemm_ws:
+            need = int(L.load().egpt_gemm_i8_tc_ws_bytes(self.batch, n, k))
+            self.gemm_ws[(n, k)] = torch.empty(max(need, 16), dtype=torch.uint8, device=self.device)
+        return self.gemm_ws[(n, k)]
 
     def _row_kv(self, row):
         b = self.base
@@ -124,7 +133,7 @@ class RaggedEngine:
             h = self._proj(act, lay['w_down'], lay['s_down'], epilogue=L.EPI_RESIDUAL, residual=h)
         x = ops.rmsnorm(h, b.final_norm, b.eps)
         if self.use_gemm:
-            ops.gemm_i8_tc(x, b.w_lm, b.s_lm, double_round=False, out=self.logits)
+            ops.gemm_i8_tc(x, b.w_lm, b.s_lm, double_round=False, out=self.logits, ws=self._ws(b.w_lm))
         else:
             ops.gemv_i8(x, b.w_lm, b.s_lm, out=self.logits)
         self.tokens.copy_(ops.argmax_rows(self.logits))

@@ -177,9 +177,13 @@ EGPT_API int egpt_argmax_rows(int64_t *out, const void *logits, int64_t rows, in
  * (with EGPT_FLAG_DOUBLE_ROUND; without it bf16(fp32 sum * s)). x bf16 [M, K] (leading dimension ldx),
  * q int8 [N, K] row-major, s [N] bf16 or fp32, y bf16 [M, N] (leading dimension ldy). fp32 accumulation on
  * tcgen05.mma (128 x 256 tiles, int8 widened to bf16 in shared memory). K a multiple of 64; x, y, q 16-byte
- * aligned, ldx and ldy multiples of 8. */
+ * aligned, ldx and ldy multiples of 8. When the tiles alone leave SMs idle (few rows) K is split over several
+ * CTAs per tile if ws holds egpt_gemm_i8_tc_ws_bytes(M, N, K) bytes (16-byte aligned; fp32 partials, no
+ * zero-fill needed), followed by a reduce launch; with a smaller (or NULL) ws one CTA takes each tile. */
+EGPT_API size_t egpt_gemm_i8_tc_ws_bytes(int64_t M, int64_t N, int64_t K);
 EGPT_API int egpt_gemm_i8_tc(void *y, int64_t ldy, const void *x, int64_t ldx, int64_t M, const int8_t *q,
-                             const void *s, int s_dtype, int64_t N, int64_t K, unsigned flags, void *stream);
+                             const void *s, int s_dtype, int64_t N, int64_t K, unsigned flags, void *ws,
+                             size_t ws_bytes, void *stream);
 
 /* ---- stochastic sampling: temperature -> top-k -> top-p -> inverse CDF -------------------------------
  * replaces: filtered_probs + sample_from (research/phase5/sampling.py:39-71; the Triton families

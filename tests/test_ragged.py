@@ -71,16 +71,16 @@ def test_ragged_graph_equals_eager_and_pads_unread(cuda):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize('rows', [4, 8])
+@pytest.mark.parametrize('rows', [2, 8])
 def test_ragged_equal_rows(cuda, golden, rows):
-    """Equal prompts give equal rows, on the GEMV (4 rows) and on the tcgen05 GEMM (8 rows) projections, and the
+    """Equal prompts give equal rows, on the GEMV (2 rows) and on the tcgen05 GEMM (8 rows) projections, and the
     row matches the reference's greedy tokens under the near-tie rule."""
     from efficientgpt_b200.ragged import RaggedGraphDecoder
     model = _model()
     p = gi.tiny_prompts()[5]
     x = p.repeat(rows, 1)
     dec = RaggedGraphDecoder(model, rows, 5 + 16)
-    assert dec.engine.use_gemm == (rows >= 8)
+    assert dec.engine.use_gemm == (rows >= 4)
     out = dec.generate(x.cuda(), torch.full((rows,), 5, dtype=torch.long).cuda(), 16)
     assert all(torch.equal(out[0], out[r]) for r in range(1, rows))
     run = golden['tiny_qwen3']['runs']['bf16']['5']
