@@ -239,7 +239,7 @@ class Qwen3Engine:
             h_last = fill_kv(ids, self.layers, self.embed, self.kv, self.rope_cos, self.rope_sin, self.nq, self.nkv,
                              self.d, self.eps, last_hidden=True)
             ops.lm_head_argmax(h_last[0], self.w_lm, self.s_lm, self.lm_ws, norm_w=self.final_norm, eps=self.eps,
-                               logits=self.logits, token=self.token)
+                               logits=self.logits, token=self.token, exact=True)
             self.position.fill_(p)
             return self.token
         self.position.zero_()
@@ -258,7 +258,7 @@ class Qwen3Engine:
             act = self._linear(x, lay['w_gu'], lay['s_gu'], epilogue=L.EPI_SILU_MUL)
             h = self._linear(act, lay['w_down'], lay['s_down'], epilogue=L.EPI_RESIDUAL, residual=h)
         ops.lm_head_argmax(h[p - 1], self.w_lm, self.s_lm, self.lm_ws, norm_w=self.final_norm, eps=self.eps,
-                           logits=self.logits, token=self.token)
+                           logits=self.logits, token=self.token, exact=True)
         self.position.fill_(p)
         return self.token
 
