@@ -54,6 +54,7 @@ struct Params {
   int scale_bf16;
   int rw;                           // ring slots per warp
   int kv_smem;                      // attention CTAs hold their K and V rows in shared memory
+  int cph;                          // attention CTAs per kv head (2: each takes half of the group's q heads)
   const int8_t *w_lm;
   const egpt_qwen3_layer *layers;  // device array
   const uint16_t *embed, *final_norm, *rope_cos, *rope_sin;
@@ -626,9 +627,8 @@ __device__ __forceinline__ int ord_enc(float f) {  // int order == float order
 }
 __device__ __forceinline__ float ord_dec(int i) { return __int_as_float(i >= 0 ? i : i ^ 0x7fffffff); }
 
-// Sums of NV partial values over the 32 lanes (NV = 16 or 32), halving the set at each butterfly step: after the
-// call lane l holds the full sum of value l >> 1 (NV = 16) or l (NV = 32) in v[0]. NV - 1 + (NV == 16) shuffles in
-// all instead of 5 NV.
+// Sums of NV partial values over the 32 lanes (NV = 8, 16 or 32), halving the set at each butterfly step: after
+// the call lane l holds the full sum of value l >> (5 - log2 NV) in v[0]. About NV shuffles in all instead of 5 NV.
 template <int NV>
 __device__ __forceinline__ void reduce_scatter(float (&v)[NV]) {
   const int lane = threadIdx.x & 31;
@@ -668,7 +668,8 @@ template <int DPL, int GRP>
 __device__ void attn_smem(const uint16_t *Ks, const uint16_t *Vs, int n, const float (*q)[DPL * 32], float scale,
                           float *sc, int capr, int *bm, float *wacc, float *wl) {
   constexpr int D = DPL * 32, NV = GRP * 8;
-  static_assert(NV == 16 || NV == 32, "heads per group: 2 or 4");
+  static_assert(NV == 8 || NV == 16 || NV == 32, "1, 2 or 4 q heads");
+  constexpr int SH = NV == 8 ? 2 : NV == 16 ? 1 : 0;  // lane l holds value l >> SH after the reduce-scatter
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float qr[GRP][DPL];
 #pragma unroll
@@ -698,14 +699,14 @@ __device__ void attn_smem(const uint16_t *Ks, const uint16_t *Vs, int n, const f
       }
     }
     reduce_scatter<NV>(v);
-    const int idx = NV == 16 ? lane >> 1 : lane;  // value held: head idx / 8, key 8 gq + idx % 8
+    const int idx = lane >> SH;  // value held: head idx / 8, key 8 gq + idx % 8
     const int j = idx >> 3, key = 8 * gq + (idx & 7);
     const float sv = v[0] * scale;
     float m = key < n ? sv : -INFINITY;
-    // maximum over the group's 8 keys of head j: lanes of one head are 16 (NV 16) or 8 (NV 32) apart in a run
+    // maximum over the group's 8 keys of head j: the 8 keys' lanes are 2^SH apart, within one head's run of lanes
 #pragma unroll
-    for (int o = NV == 16 ? 2 : 1; o < (NV == 16 ? 16 : 8); o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const bool writer = NV == 16 ? (lane & 1) == 0 : true;
+    for (int o = 1 << SH; o < (8 << SH); o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const bool writer = (lane & ((1 << SH) - 1)) == 0;
     if (writer && key < n) sc[j * capr + key] = sv;
     if (writer && (idx & 7) == 0) atomicMax(&bm[j * kMaxBlk + key / kRefBlock], ord_enc(m));
   }
@@ -771,13 +772,14 @@ __device__ void attn_smem(const uint16_t *Ks, const uint16_t *Vs, int n, const f
   csync();
 }
 
-// Attention of kv head g for this step (one CTA): the q heads of the group and the new k row from the q|k|v words
+// Attention of kv head g for this step, q heads [head0, head0 + GRP) of its group (one CTA; with two CTAs per kv
+// head each takes half of the group): those q heads and the new k row from the q|k|v words
 // (normalised and rotated by one warp each), the new k and v rows appended to the cache (and to the shared-memory
 // copies Ks / Vs when those hold the cache), then attention over keys [0, pos] (attn_smem on the shared-memory
 // copies, else the attention core of attention.cu: both the reference GPU kernel's 128-key block walk), and the
 // group's output published as LL words.
 template <int DPL, int GRP, bool TRACE>
-__device__ void attention_ll(const Params &P, const egpt_qwen3_layer &Ly, int g, int64_t pos,
+__device__ void attention_ll(const Params &P, const egpt_qwen3_layer &Ly, int g, int head0, int64_t pos,
                              const unsigned long long *qkv_w, uint32_t qkv_tag, unsigned long long *out_w,
                              uint32_t out_tag, float *u, uint16_t *Ks, uint16_t *Vs, int tslot) {
   constexpr int D = DPL * 32;
@@ -786,7 +788,7 @@ __device__ void attention_ll(const Params &P, const egpt_qwen3_layer &Ly, int g,
   uint16_t *kc = (uint16_t *)Ly.k_cache, *vc = (uint16_t *)Ly.v_cache;
   const int64_t kv_base = (int64_t)g * P.cap * D;
   if (warp <= GRP + 1) {
-    const int head = warp < GRP ? g * GRP + warp : warp == GRP ? P.NQ + g : P.NQ + P.NKV + g;
+    const int head = warp < GRP ? head0 + warp : warp == GRP ? P.NQ + g : P.NQ + P.NKV + g;
     const int64_t e0 = (int64_t)head * D + lane * DPL;  // first element of this lane
     float v[DPL];
     if (DPL >= 2) {
@@ -870,7 +872,7 @@ __device__ void attention_ll(const Params &P, const egpt_qwen3_layer &Ly, int g,
         num0 += wacc[(w * GRP + j) * D + dd];
         num1 += wacc[(w * GRP + j) * D + dd + 1];
       }
-      ll_put(out_w + ((int64_t)g * GRP * D) / 2 + idx, pack2(num0 / den, num1 / den), out_tag);
+      ll_put(out_w + ((int64_t)head0 * D) / 2 + idx, pack2(num0 / den, num1 / den), out_tag);
     }
     if (TRACE && tslot >= 0 && P.trace) {
       csync();
@@ -902,7 +904,7 @@ __device__ void attention_ll(const Params &P, const egpt_qwen3_layer &Ly, int g,
       a0 += S.w_acc[w][j][dd] * f;
       a1 += S.w_acc[w][j][dd + 1] * f;
     }
-    ll_put(out_w + ((int64_t)g * GRP * D) / 2 + idx, pack2(a0 / lsum, a1 / lsum), out_tag);
+    ll_put(out_w + ((int64_t)head0 * D) / 2 + idx, pack2(a0 / lsum, a1 / lsum), out_tag);
   }
   if (TRACE && tslot >= 0 && P.trace) {
     csync();
@@ -934,8 +936,10 @@ __global__ void __launch_bounds__(kCT, 1) dataflow_step_kernel(const __grid_cons
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int D = DPL * 32;
   const int nstages = 4 * P.L + 1;
-  const int W = (int)gridDim.x - P.NKV;                 // GEMV CTAs
-  const int attn_g = (int)blockIdx.x - W;               // >= 0: this CTA runs kv head attn_g's attention
+  const int W = (int)gridDim.x - P.NKV * P.cph;        // GEMV CTAs
+  const int attn_a = (int)blockIdx.x - W;               // >= 0: this CTA runs attention
+  const int attn_g = attn_a >= 0 ? attn_a / P.cph : -1;  // its kv head
+  const int attn_part = attn_a >= 0 ? attn_a % P.cph : 0;  // and which part of the group's q heads
   // layout: scratch 512 B | stage table | barriers | part | union(digit planes, attention scratch) | rings / K, V
   float *redf = (float *)smem;
   double *redd = (double *)smem;  // first 16 doubles overlap redf[0..31]
@@ -1023,13 +1027,19 @@ __global__ void __launch_bounds__(kCT, 1) dataflow_step_kernel(const __grid_cons
           ok = false;
       }
       if (ok) {
-        attention_ll<DPL, GRP, TRACE>(P, Ly, attn_g, pos, lw + M.o_qkv, tag_of(P, epoch, l, 0), lw + M.o_attn,
-                                      tag_of(P, epoch, l, 1), u, Ks, Vs,
-                                      (TRACE && attn_g == 0) ? 3 + 5 * P.L + 10 * l + 2 : -1);
-        if (TRACE && attn_g == 0) stamp<TRACE>(P, 2 + 5 * l);
+        const int tslot = (TRACE && attn_a == 0) ? 3 + 5 * P.L + 10 * l + 2 : -1;
+        if (GRP >= 2 && P.cph == 2)
+          attention_ll<DPL, (GRP >= 2 ? GRP / 2 : 1), TRACE>(P, Ly, attn_g, attn_g * GRP + attn_part * (GRP / 2), pos,
+                                                         lw + M.o_qkv, tag_of(P, epoch, l, 0), lw + M.o_attn,
+                                                         tag_of(P, epoch, l, 1), u, Ks, Vs, tslot);
+        else
+          attention_ll<DPL, GRP, TRACE>(P, Ly, attn_g, attn_g * GRP, pos, lw + M.o_qkv, tag_of(P, epoch, l, 0),
+                                        lw + M.o_attn, tag_of(P, epoch, l, 1), u, Ks, Vs, tslot);
+        if (TRACE && attn_a == 0) stamp<TRACE>(P, 2 + 5 * l);
       } else {  // bad position or a failed copy: publish zeros so that no consumer waits for this head
-        for (int idx = threadIdx.x; idx < GRP * D / 2; idx += kCT)
-          ll_put(lw + M.o_attn + ((int64_t)attn_g * GRP * D) / 2 + idx, 0u, tag_of(P, epoch, l, 1));
+        const int gh = GRP / P.cph;  // this CTA's q heads
+        for (int idx = threadIdx.x; idx < gh * D / 2; idx += kCT)
+          ll_put(lw + M.o_attn + ((int64_t)(attn_g * GRP + attn_part * gh) * D) / 2 + idx, 0u, tag_of(P, epoch, l, 1));
       }
       csync();  // the copies' rows and the attention scratch are free again
       if (ok && Ks && l + 1 < P.L) {
@@ -1288,11 +1298,12 @@ static size_t attn_bytes() {
 
 struct Layout {
   size_t smem;
-  int rw, part, ubytes, kv_smem;
+  int rw, part, ubytes, kv_smem, cph;
 };
 
 static bool layout(const egpt_qwen3_plan *Pl, Layout &lo) {
-  const int G = num_sms(), W = G - Pl->n_kv_heads;
+  // the stage shares are sized for the smaller GEMV grid (two attention CTAs per kv head), enough for either
+  const int G = num_sms(), W = G - 2 * Pl->n_kv_heads;
   const int L = Pl->n_layers, D = Pl->head_dim, grp = Pl->n_q_heads / Pl->n_kv_heads;
   const int64_t kmax = std::max<int64_t>({(int64_t)Pl->hidden, (int64_t)Pl->intermediate, (int64_t)Pl->n_q_heads * D});
   const size_t ab = D == 32 ? attn_bytes<1, 2>() : grp == 2 ? attn_bytes<4, 2>() : attn_bytes<4, 4>();
@@ -1316,6 +1327,10 @@ static bool layout(const egpt_qwen3_plan *Pl, Layout &lo) {
   const size_t sa = 4 * (size_t)smem_attn_floats(Pl->cap, grp, D);
   // attention CTAs: K and V rows of the whole cache, then the attention scratch
   lo.kv_smem = ((size_t)Pl->cap * D * 2 * 2 + sa <= big && Pl->cap <= kMaxBlk * kRefBlock) ? 1 : 0;
+  // two attention CTAs per kv head (half of the group's q heads each) when the rows sit in shared memory: the
+  // attention stage is issue-bound on one CTA, and the GEMV stages are bound by their latency chain, not by the
+  // 8 CTAs they give up
+  lo.cph = (lo.kv_smem && grp >= 2) ? 2 : 1;
   return true;
 }
 
@@ -1336,7 +1351,7 @@ static int validate(const egpt_qwen3_plan *Pl, Layout *lo_out) {
     return set_error(EGPT_ERR_SHAPE, "dataflow step: hidden, intermediate and nq*d must be multiples of 64 and at most "
                      "%d, vocab a multiple of 16", kMaxK);
   const int G = num_sms();
-  if (G > kArgmaxMaxCtas || G < 2 * NKV) return set_error(EGPT_ERR_SHAPE, "dataflow step: SM count %d unusable", G);
+  if (G > kArgmaxMaxCtas || G <= 2 * NKV) return set_error(EGPT_ERR_SHAPE, "dataflow step: SM count %d unusable", G);
   if (Pl->vocab > 0x7fffffffLL) return set_error(EGPT_ERR_SHAPE, "dataflow step: vocabulary too large");
   if (!maps_ok()) return set_error(EGPT_ERR_LAUNCH, "dataflow step: this driver does not encode the weights' tensor maps");
   bool aligned = (uintptr_t)Pl->w_lm % 16 == 0;
@@ -1416,7 +1431,7 @@ extern "C" int egpt_decode_step_dataflow(const egpt_qwen3_plan *Pl, void *stream
   P.L = Pl->n_layers, P.H = Pl->hidden, P.NQ = Pl->n_q_heads, P.NKV = Pl->n_kv_heads, P.D = D;
   P.I = Pl->intermediate, P.V = Pl->vocab, P.cap = Pl->cap, P.eps = Pl->eps, P.scale = Pl->attn_scale;
   P.scale_bf16 = Pl->scale_dtype == EGPT_BF16;
-  P.rw = lo.rw, P.kv_smem = lo.kv_smem;
+  P.rw = lo.rw, P.kv_smem = lo.kv_smem, P.cph = lo.cph;
   P.w_lm = Pl->w_lm;
   P.layers = Pl->layers_dev;
   P.embed = (const uint16_t *)Pl->embed, P.final_norm = (const uint16_t *)Pl->final_norm;
