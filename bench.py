@@ -637,6 +637,28 @@ def run_gemm_prefill(a):
                           'peak_tflops': peak, 'frac_tcgen05': round(tf(t_tc) / peak, 4) if peak else None,
                           'peak_source': src}), flush=True)
         del x, q, out
+    # causal attention over the prompt: egpt_attn_prefill (tcgen05) against PyTorch's SDPA (the reference's call);
+    # useful flops 2 nq d p (p + 1) (QK^T and P.V over the causal triangle)
+    for what, p, nq, nkv in (('8B', 4096, 32, 8), ('1.7B', 4096, 16, 8), ('8B', 1024, 32, 8)):
+        if a.only not in f'prefill attention {what} p={p}':
+            continue
+        d = 128
+        g = torch.Generator(device='cuda').manual_seed(p + nq)
+        q = torch.randn(p, nq * d, device='cuda', generator=g).to(torch.bfloat16)
+        kc = torch.randn(nkv, p, d, device='cuda', generator=g).to(torch.bfloat16)
+        vc = torch.randn(nkv, p, d, device='cuda', generator=g).to(torch.bfloat16)
+        out = torch.empty(p, nq * d, dtype=torch.bfloat16, device='cuda')
+        t_tc = _time_graph(lambda i: ops.attn_prefill(q, kc, vc, 0, nq, nkv, d, scale=d ** -0.5, out=out), a.reps)
+        qh = q.view(p, nq, d).transpose(0, 1).unsqueeze(0)
+        t_ref = _time_graph(lambda i: torch.nn.functional.scaled_dot_product_attention(
+            qh, kc.unsqueeze(0), vc.unsqueeze(0), is_causal=True, scale=d ** -0.5, enable_gqa=True), a.reps)
+        tf = lambda t: 2.0 * nq * d * p * (p + 1) / (t * 1e-6) / 1e12
+        print(json.dumps({'kernel': 'attn_prefill_kernel', 'case': f'prefill attention {what} p={p} nq={nq} nkv={nkv}',
+                          'us_tcgen05': round(t_tc, 2), 'tflops_tcgen05': round(tf(t_tc), 1),
+                          'us_reference_sdpa': round(t_ref, 2), 'tflops_reference_sdpa': round(tf(t_ref), 1),
+                          'peak_tflops': peak, 'frac_tcgen05': round(tf(t_tc) / peak, 4) if peak else None,
+                          'peak_source': src}), flush=True)
+        del q, kc, vc, out
 
 
 def run_ragged(a):

@@ -72,6 +72,7 @@ SIGNATURES = {
                                        I32, U32, P]),
     'egpt_argmax_rows': (I32, [P, P, I64, I64, I64, I32, P]),
     'egpt_sample_ws_bytes': (SZ, [I64]),
+    'egpt_attn_prefill': (I32, [P, I64, P, I64, P, P, I64, I64, I64, I32, I32, I32, F32, P]),
     'egpt_gemm_i8_tc_ws_bytes': (SZ, [I64, I64, I64]),
     'egpt_gemm_i8_tc': (I32, [P, I64, P, I64, I64, P, P, I32, I64, I64, U32, P, SZ, P]),
     'egpt_sample': (I32, [P, I32, I64, I64, I64, F32, I64, F32, P, I64, P, P, I64, P, SZ, P]),

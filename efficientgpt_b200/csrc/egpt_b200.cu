@@ -9,3 +9,4 @@
 #include "gemv_tc.cu"
 #include "sampling.cu"
 #include "gemm_tc.cu"
+#include "attn_prefill.cu"

@@ -228,7 +228,7 @@ class Qwen3Engine:
         """Run the prompt (int64 [p] or [1, p] on the device) from position 0; leaves token = first generated id
         and position = p. Returns the token tensor (device). Prompts longer than PREFILL_GEMM_MIN tokens (the
         reference op's >16-row branch) run the GEMM prefill (efficientgpt_b200.prefill: tcgen05 projections with
-        the >16-row rounding, SDPA over the prompt) up to the last row's hidden state, then the final norm and the
+        the >16-row rounding, the tcgen05 causal attention kernel over the prompt) up to the last row's hidden state, then the final norm and the
         lm_head argmax on that row; shorter ones run the per-stage kernels on one block of rows."""
         ids = input_ids.reshape(-1).to(device=self.device, dtype=torch.int64).contiguous()
         p = ids.numel()

@@ -198,6 +198,25 @@ def attn_decode(q, k_cache, v_cache, position, nq, nkv, d, *, scale, max_split=1
     return out
 
 
+def attn_prefill(q, k_cache, v_cache, pos0, nq, nkv, d, *, scale, out=None):
+    """Causal attention of the prompt rows q bf16 [m, nq * d] (row i at position pos0 + i, normed and rotated) over
+    the cached keys 0 .. pos0 + i of caches [nkv, cap, d] -> bf16 [m, nq * d], on the tcgen05 tensor cores."""
+    _cuda(q, k_cache, v_cache, out)
+    _contig_rows(q, 'q')
+    if q.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16:
+        raise ValueError('attn_prefill: bf16 q and caches')
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()) or k_cache.shape != v_cache.shape:
+        raise ValueError('attn_prefill: caches must be contiguous [nkv, cap, d]')
+    m = q.shape[0]
+    cap = k_cache.shape[-2]
+    if out is None:
+        out = torch.empty((m, nq * d), dtype=q.dtype, device=q.device)
+    _contig_rows(out, 'out')
+    L.check(L.load().egpt_attn_prefill(_p(out), out.stride(0), _p(q), q.stride(0), _p(k_cache), _p(v_cache), cap,
+                                       int(pos0), m, nq, nkv, d, float(scale), _stream()), 'attn_prefill')
+    return out
+
+
 def argmax_rows(logits):
     _cuda(logits)
     x2 = logits.reshape(-1, logits.shape[-1])

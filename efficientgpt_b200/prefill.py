@@ -7,11 +7,13 @@ the HF Qwen3 forward over the prompt (modeling_qwen3.py:258-335), as GraphGreedy
 Prompts of more than 16 tokens are GEMMs, not GEMVs: the projections run on `egpt_gemm_i8_tc` (the int8 weights are
 widened to bf16 in shared memory on their way to the tensor cores, where the reference materialises `bf16(q)` in HBM
 on every call), RMSNorm and the q/k-norm + RoPE + KV-cache write run on this library's kernels, and causal attention
-over the prompt runs through PyTorch's SDPA (the reference's own prefill attention). The one-GPU engine takes the
+over the prompt runs on this library's tcgen05 flash-attention kernel (egpt_attn_prefill; head_dim 128) in place of
+the reference's SDPA call. The one-GPU engine takes the
 last prompt row's hidden state (`last_hidden`) to its final norm and lm_head; the tensor-parallel engine fills the
 cache of all but the last token and runs that one through its decode step, which exchanges the lm_head keys. With
-`allreduce` (tensor parallelism) o_proj and down_proj give per-rank unscaled fp32 partial products (a cuBLAS GEMM of
-the dequantised shard) that are summed across ranks before the scale.
+`allreduce` (tensor parallelism) o_proj and down_proj give per-rank unscaled partial products (the tcgen05 GEMM
+with unit scales, bf16(x_r @ bf16(q_r).T)) that are summed across ranks in fp32 (torch.distributed) before the
+scale.
 """
 import torch
 import torch.nn.functional as F
@@ -28,10 +30,30 @@ def _proj(x, q, s):
     return (y.float() * s.float()).to(torch.bfloat16)
 
 
+def _attend(q, k_cache, v_cache, pos0, nq, nkv, d):
+    """Causal attention of the rows q [m, nq * d] at positions pos0 .. pos0 + m - 1 over the cached keys: this
+    library's tcgen05 kernel (egpt_attn_prefill) for head_dim 128, the head size of every Qwen3 model; other head
+    sizes (small test models) take PyTorch's SDPA, the reference's own prefill attention."""
+    m = q.shape[0]
+    if d == 128:
+        return ops.attn_prefill(q.contiguous(), k_cache, v_cache, pos0, nq, nkv, d, scale=d ** -0.5)
+    n = pos0 + m
+    qh = q.view(m, nq, d).transpose(0, 1).unsqueeze(0)
+    kh, vh = k_cache[:, :n].unsqueeze(0), v_cache[:, :n].unsqueeze(0)
+    mask = None if pos0 == 0 else torch.ones(m, n, dtype=torch.bool, device=q.device).tril(diagonal=pos0)
+    a = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=mask, is_causal=mask is None and m > 1,
+                                       scale=d ** -0.5, enable_gqa=nq != nkv)
+    return a[0].transpose(0, 1).reshape(m, nq * d)
+
+
 def _proj_partial(x, q, s, allreduce):
     """Row-sharded projection: every rank's bf16(x_r @ bf16(q_r).T), summed over the ranks in fp32, then scaled
     and rounded once more (the one-GPU rounding points with the sum split across ranks)."""
-    y = torch.matmul(x, q.to(torch.bfloat16).t()).float()
+    if x.shape[-1] % 64 == 0:  # bf16(bf16(acc) * 1) = bf16(acc) on the tcgen05 GEMM
+        ones = torch.ones(q.shape[0], dtype=torch.bfloat16, device=x.device)
+        y = ops.gemm_i8_tc(x.contiguous(), q, ones, double_round=True).float()
+    else:
+        y = torch.matmul(x, q.to(torch.bfloat16).t()).float()
     allreduce(y)
     return (y.to(torch.bfloat16).float() * s.float()).to(torch.bfloat16)
 
@@ -61,18 +83,12 @@ def fill_kv(ids, layers, embed, kv, rope_cos, rope_sin, nq, nkv, d, eps, allredu
                 break
             # the last layer only matters for the last row: its attention over the prompt, then o_proj and the MLP
             # on that row (the per-element arithmetic of the >16-row branch does not depend on the row count)
-            qh = q[p - 1:p].view(1, nq, d).transpose(0, 1).unsqueeze(0)
-            kh, vh = kv[i, 0, :, :p].unsqueeze(0), kv[i, 1, :, :p].unsqueeze(0)
-            a = F.scaled_dot_product_attention(qh, kh, vh, scale=d ** -0.5, enable_gqa=nq != nkv)
-            a = a[0].transpose(0, 1).reshape(1, nq * d)
+            a = _attend(q[p - 1:p], kv[i, 0], kv[i, 1], p - 1, nq, nkv, d)
             hl = h[p - 1:p] + _proj(a, lay['w_o'], lay['s_o'])
             x = ops.rmsnorm(hl, lay['ln_post'], eps)
             gu = _proj(x, lay['w_gu'], lay['s_gu'])
             return hl + _proj(F.silu(gu[:, :inter]) * gu[:, inter:], lay['w_down'], lay['s_down'])
-        qh = q.view(p, nq, d).transpose(0, 1).unsqueeze(0)
-        kh, vh = kv[i, 0, :, :p].unsqueeze(0), kv[i, 1, :, :p].unsqueeze(0)
-        a = F.scaled_dot_product_attention(qh, kh, vh, is_causal=True, scale=d ** -0.5, enable_gqa=nq != nkv)
-        a = a[0].transpose(0, 1).reshape(p, nq * d)
+        a = _attend(q, kv[i, 0], kv[i, 1], 0, nq, nkv, d)
         o = _proj(a, lay['w_o'], lay['s_o']) if allreduce is None else _proj_partial(a, lay['w_o'], lay['s_o'], allreduce)
         h = h + o
         x = ops.rmsnorm(h, lay['ln_post'], eps)

@@ -168,6 +168,19 @@ EGPT_API int egpt_attn_decode_noalloc(void *out, int64_t ldo, const void *q, int
                                       const void *rope_cos, const void *rope_sin, float scale, int max_split,
                                       int dtype, unsigned flags, void *stream);
 
+/* ---- causal attention over a prompt (prefill) on the tcgen05 tensor cores ----------------------------
+ * replaces: the SDPA call of the HF Qwen3 attention over the prompt (modeling_qwen3.py:258-291 with
+ *           is_causal), as GraphGreedyDecoder's prefill runs it (research/realmodel/fast_decode.py:77-85).
+ * out[i, h] = softmax(scale * q[i, h] . K[0 .. pos0 + i]) V[0 .. pos0 + i] for rows i < m; q bf16 [m][ldq]
+ * (head h at columns h*d, already normed and rotated), caches bf16 [nkv][cap][d] holding keys 0 .. pos0 + m - 1,
+ * out bf16 [m][ldo]; GQA head h reads kv head h / (nq / nkv). d = 128. fp32 scores and sums, probabilities
+ * rounded to bf16 relative to the running row maximum before P.V, one bf16 rounding of the output. pos0 > 0
+ * continues a prompt whose first pos0 keys are already cached (chunked prefill; m = 1 is one decode row).
+ * Pointers 16-byte aligned, ldq and ldo multiples of 8. No workspace. */
+EGPT_API int egpt_attn_prefill(void *out, int64_t ldo, const void *q, int64_t ldq, const void *k_cache,
+                               const void *v_cache, int64_t cap, int64_t pos0, int64_t m, int nq, int nkv, int d,
+                               float scale, void *stream);
+
 /* ---- argmax over rows of bf16/fp32 logits -----------------------------------------------------------
  * replaces: logits[:, -1].argmax(-1) (research/realmodel/fast_decode.py:48,84): first index on ties. */
 EGPT_API int egpt_argmax_rows(int64_t *out, const void *logits, int64_t rows, int64_t n, int64_t ld, int dtype, void *stream);
