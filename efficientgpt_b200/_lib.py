@@ -21,6 +21,7 @@ FLAG_REF_SOFTMAX = 128
 FLAG_X_F32 = 256
 FLAG_EXACT = 512
 FLAG_RAGGED = 1024
+FLAG_ADD_OUT = 2048
 
 _VALUE_ERRORS = {EGPT_ERR_SHAPE, EGPT_ERR_DTYPE, EGPT_ERR_ALIGN, EGPT_ERR_ARG, EGPT_ERR_WORKSPACE}
 
@@ -73,6 +74,7 @@ SIGNATURES = {
     'egpt_argmax_rows': (I32, [P, P, I64, I64, I64, I32, P]),
     'egpt_sample_ws_bytes': (SZ, [I64]),
     'egpt_attn_prefill': (I32, [P, I64, P, I64, P, P, I64, I64, I64, I32, I32, I32, F32, P]),
+    'egpt_silu_mul': (I32, [P, I64, P, I64, I64, I64, P]),
     'egpt_gemm_i8_tc_ws_bytes': (SZ, [I64, I64, I64]),
     'egpt_gemm_i8_tc': (I32, [P, I64, P, I64, I64, P, P, I32, I64, I64, U32, P, SZ, P]),
     'egpt_sample': (I32, [P, I32, I64, I64, I64, F32, I64, F32, P, I64, P, P, I64, P, SZ, P]),

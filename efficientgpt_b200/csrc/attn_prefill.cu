@@ -7,18 +7,21 @@
 //
 // One CTA per (q head, 128 query rows), the longest query blocks first, 576 threads:
 //   warp 0   lane 0 issues TMA loads (this GPU's memory, no multicast): the Q tile once (two 64-column halves,
-//            128-byte swizzle), then K and V blocks of 128 keys into a 2-slot ring; the K/V tensor maps end at
+//            128-byte swizzle), then K blocks of 128 keys into a 3-slot ring and V blocks into a 2-slot ring (a K
+//            slot frees once its scores are computed, a V slot once its P.V has run); the K/V tensor maps end at
 //            key pos0 + m, so rows past the prompt arrive as zeros (stale cache rows are never read);
-//   warp 1   allocates TMEM (two 128-column score buffers S and the 128-column output accumulator O; lane = query
-//            row) and, lane 0, issues tcgen05.mma.kind::f16: S_j = Q K_j^T (both K-major) one block ahead, and
-//            O += P_j V_j (P K-major from shared memory, V MN-major straight from the TMA tile);
+//   warp 1   allocates TMEM (two 128-column score buffers S, the 128-column output accumulator O, two 64-column
+//            buffers P; lane = query row) and, lane 0, issues tcgen05.mma.kind::f16: S_j = Q K_j^T (both K-major
+//            in shared memory) two blocks ahead, and O += P_j V_j with P_j read from TMEM as the A operand and V
+//            MN-major straight from its TMA tile;
 //   warps 2-17 run the softmax: four warps per TMEM lane quarter (the rows they may read), each taking 32 of a
 //            row's 128 columns. Per block: load the thread's 32 scores of S_j, mask keys past the row's position,
-//            exchange the partial row maxima within the quarter (shared memory, named barrier), write
-//            P_j = bf16(2^(scale log2(e) s - m)) in the operand's swizzled layout and keep a partial sum. The
+//            exchange the partial row maxima within the quarter (shared memory, named barrier), store
+//            P_j = bf16(2^(scale log2(e) s - m)) into TMEM (two values per column) and keep a partial sum. The
 //            running maximum m moves only when a block's maximum exceeds it by more than 2^8 (then O's columns
-//            are rescaled in TMEM): probabilities stay below 2^8, and O and the sum use the same m, so the result
-//            is the same softmax with fewer rescales. After the last block: bf16(O / sum of the partial sums).
+//            are rescaled in TMEM, the one step that waits for the previous P.V): probabilities stay below 2^8, and
+//            O and the sum use the same m, so the result is the same softmax with fewer rescales. After the last
+//            block: bf16(O / sum of the partial sums).
 // Rounding: probabilities enter P.V as bf16 (relative to the maximum in use), fp32 accumulation, one bf16 rounding
 // of the normalised output (the flash-attention scheme of the SDPA kernels the reference's prefill runs on).
 // Every mbarrier wait is bounded (EGPT_ERR_TIMEOUT through egpt_device_error); before the CTA exits the issued TMA
@@ -34,17 +37,19 @@ constexpr int kBQ = 128;               // query rows per CTA (TMEM lanes)
 constexpr int kBK = 128;               // keys per block
 constexpr int kHalf = 128 * 128;       // bytes: 128 rows x 64 bf16, one 128-byte swizzle column of a tile
 constexpr int kTile = 2 * kHalf;       // 32 KB: 128 rows x 128 bf16
-constexpr int kStages = 2;             // K/V ring
+constexpr int kKStages = 3;            // K ring (a slot frees once its scores are computed)
+constexpr int kVStages = 2;            // V ring (a slot frees once its P.V has run)
 constexpr int kSplit = 4;              // softmax warps per TMEM lane quarter
 constexpr int kCols = kBK / kSplit;    // 32 columns of S (and of O) per softmax thread
 constexpr int kSmThreads = 128 * kSplit;
 constexpr int kThreads = 64 + kSmThreads;  // TMA warp, MMA warp, 16 softmax warps
 constexpr float kStale = 8.f;          // the running maximum moves when a block's exceeds it by more (log2 units)
-constexpr uint32_t kTmemCols = 512;    // S0 | S1 | O (384 used; allocations are powers of two)
+constexpr uint32_t kTmemCols = 512;    // S0 | S1 | O | P0 | P1 (128 + 128 + 128 + 64 + 64 columns)
 constexpr uint32_t kOCol = 2 * kBK;
+constexpr uint32_t kPCol = 3 * kBK;    // P_j: 128 bf16 per row packed two per column, buffer j % 2
 constexpr size_t kRedBytes = 2 * kSplit * kBQ * 4;  // partial row maxima (and sums), two blocks in flight
-constexpr size_t kSmem = 1024 /* alignment slack */ + (size_t)kTile /* Q */ + (size_t)kStages * 2 * kTile /* K, V */ +
-                         (size_t)kTile /* P */ + kRedBytes + 128 /* barriers, TMEM address */;
+constexpr size_t kSmem = 1024 /* alignment slack */ + (size_t)kTile /* Q */ +
+                         (size_t)(kKStages + kVStages) * kTile /* K, V */ + kRedBytes + 256 /* barriers, TMEM address */;
 
 struct Args {
   CUtensorMap qmap;  // q bf16 [m][ldq], box {64, 128}, 128-byte swizzle
@@ -75,6 +80,14 @@ __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t b
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
       : "memory");
 }
+// D (TMEM) += A (TMEM: row i in lane i, K elements packed two per 32-bit column) x B (shared-memory descriptor).
+__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
@@ -102,6 +115,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t *v) {
       "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
 }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -114,21 +135,47 @@ __device__ __forceinline__ void quarter_sync(int quarter) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Bounded wait by every lane of a warp; true only if all of them saw the phase complete (the tcgen05.ld/st that
-// follow are warp-collective, so the warp stays together).
+// Bounded wait by lane 0 of a warp, then a warp barrier that orders the other lanes after it; the result is the
+// warp's (the tcgen05.ld/st that follow are warp-collective, so the warp stays together). One polling lane per
+// warp keeps the softmax warps' polls from crowding the shared-memory pipe.
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, unsigned parity) {
-  return __all_sync(0xffffffffu, gtc::mbar_wait(bar, parity));
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = gtc::mbar_wait(bar, parity);
+  __syncwarp();
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+// Two fp32 lanes at once (packed f32x2 instructions of sm_100).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
 }
 
 __global__ void __launch_bounds__(kThreads, 1) attn_prefill_kernel(const __grid_constant__ Args A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);  // 1024-aligned operand tiles
   uint8_t *sq = smem;                                 // Q: two [128 rows][128 B] halves
-  uint8_t *skv = sq + kTile;                          // slot s: K at skv + 2 s kTile, V right after it
-  uint8_t *sp = skv + (size_t)kStages * 2 * kTile;    // P: two [128 rows][128 B] halves (keys 0-63, 64-127)
-  float *red = (float *)(sp + kTile);                 // [2][kSplit][128] partial row maxima / sums
+  uint8_t *sk = sq + kTile;                           // K slots, each two [128 keys][128 B] halves
+  uint8_t *sv = sk + (size_t)kKStages * kTile;        // V slots, the same layout
+  float *red = (float *)(sv + (size_t)kVStages * kTile);  // [2][kSplit][128] partial row maxima / sums
   uint64_t *bars = (uint64_t *)((uint8_t *)red + kRedBytes);
-  uint64_t *q_full = bars, *kv_full = bars + 1, *kv_empty = kv_full + kStages, *s_full = kv_empty + kStages;
+  uint64_t *q_full = bars, *k_full = bars + 1, *k_empty = k_full + kKStages, *v_full = k_empty + kKStages;
+  uint64_t *v_empty = v_full + kVStages, *s_full = v_empty + kVStages;
   uint64_t *p_full = s_full + 2, *o_done = p_full + 1, *mma_done = o_done + 1;
   uint32_t *tmem_slot = (uint32_t *)(mma_done + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -142,9 +189,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_prefill_kernel(const __grid_
 
   if (threadIdx.x == 0) {
     gtc::mbar_init(q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
-      gtc::mbar_init(kv_full + s, 1);
-      gtc::mbar_init(kv_empty + s, 1);
+    for (int s = 0; s < kKStages; ++s) {
+      gtc::mbar_init(k_full + s, 1);
+      gtc::mbar_init(k_empty + s, 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      gtc::mbar_init(v_full + s, 1);
+      gtc::mbar_init(v_empty + s, 1);
     }
     gtc::mbar_init(s_full, 1);
     gtc::mbar_init(s_full + 1, 1);
@@ -170,32 +221,43 @@ __global__ void __launch_bounds__(kThreads, 1) attn_prefill_kernel(const __grid_
       gtc::mbar_arrive_tx(q_full, kTile);
       gtc::tma_load_2d(sq, &A.qmap, h * kD, (int)r0, q_full);
       gtc::tma_load_2d(sq + kHalf, &A.qmap, h * kD + 64, (int)r0, q_full);
-      int issued = 0;
-      for (int j = 0; j < nkb; ++j) {
-        const int s = j % kStages;
-        if (j >= kStages && !gtc::mbar_wait(kv_empty + s, (unsigned)((j / kStages) - 1) & 1u)) break;
-        uint8_t *k = skv + (size_t)s * 2 * kTile, *v = k + kTile;
-        gtc::mbar_arrive_tx(kv_full + s, 2 * kTile);
-        tma_load_3d(k, &A.kmap, 0, j * kBK, kvh, kv_full + s);
-        tma_load_3d(k + kHalf, &A.kmap, 64, j * kBK, kvh, kv_full + s);
-        tma_load_3d(v, &A.vmap, 0, j * kBK, kvh, kv_full + s);
-        tma_load_3d(v + kHalf, &A.vmap, 64, j * kBK, kvh, kv_full + s);
-        ++issued;
+      int nk = 0, nv = 0;  // K and V blocks issued; K runs one block ahead of V (scores come first)
+      auto load_k = [&](int b) -> bool {
+        const int ks = b % kKStages;
+        if (b >= kKStages && !gtc::mbar_wait(k_empty + ks, (unsigned)((b / kKStages) - 1) & 1u)) return false;
+        uint8_t *k = sk + (size_t)ks * kTile;
+        gtc::mbar_arrive_tx(k_full + ks, kTile);
+        tma_load_3d(k, &A.kmap, 0, b * kBK, kvh, k_full + ks);
+        tma_load_3d(k + kHalf, &A.kmap, 64, b * kBK, kvh, k_full + ks);
+        ++nk;
+        return true;
+      };
+      bool ok = load_k(0);
+      for (int j = 0; j < nkb && ok; ++j) {
+        if (j + 1 < nkb && !load_k(j + 1)) break;
+        const int vs = j % kVStages;
+        if (j >= kVStages && !gtc::mbar_wait(v_empty + vs, (unsigned)((j / kVStages) - 1) & 1u)) break;
+        uint8_t *v = sv + (size_t)vs * kTile;
+        gtc::mbar_arrive_tx(v_full + vs, kTile);
+        tma_load_3d(v, &A.vmap, 0, j * kBK, kvh, v_full + vs);
+        tma_load_3d(v + kHalf, &A.vmap, 64, j * kBK, kvh, v_full + vs);
+        ++nv;
       }
       // none of this CTA's copies may still be landing when it exits
       gtc::mbar_drain(q_full, 0);
-      for (int j = max(0, issued - kStages); j < issued; ++j)
-        gtc::mbar_drain(kv_full + j % kStages, (unsigned)(j / kStages) & 1u);
+      for (int b = max(0, nk - kKStages); b < nk; ++b) gtc::mbar_drain(k_full + b % kKStages, (unsigned)(b / kKStages) & 1u);
+      for (int b = max(0, nv - kVStages); b < nv; ++b) gtc::mbar_drain(v_full + b % kVStages, (unsigned)(b / kVStages) & 1u);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      // S_j = Q K_j^T into score buffer j % 2: eight K = 16 steps, 32 bytes apart inside a 128-byte swizzled row
+      // S_j = Q K_j^T into score buffer j % 2: eight K = 16 steps, 32 bytes apart inside a 128-byte swizzled row.
+      // Its commit also completes once every MMA issued before it has (P.V of block j - 2 included).
       auto issue_scores = [&](int j) -> bool {
-        const int s = j % kStages;
-        if (!gtc::mbar_wait(kv_full + s, (unsigned)(j / kStages) & 1u)) return false;
+        const int s = j % kKStages;
+        if (!gtc::mbar_wait(k_full + s, (unsigned)(j / kKStages) & 1u)) return false;
         gtc::tc_fence_after();
-        const uint8_t *k = skv + (size_t)s * 2 * kTile;
+        const uint8_t *k = sk + (size_t)s * kTile;
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           const int half = kk >> 2;
@@ -203,23 +265,25 @@ __global__ void __launch_bounds__(kThreads, 1) attn_prefill_kernel(const __grid_
           umma(tmem + (uint32_t)((j & 1) * kBK), gtc::sw128_desc(sq + half * kHalf) + off,
                gtc::sw128_desc(k + half * kHalf) + off, kIdescS, kk > 0 ? 1u : 0u);
         }
+        gtc::umma_commit(k_empty + s);  // the K slot is free once these MMAs have read it
         gtc::umma_commit(s_full + (j & 1));
         return true;
       };
-      bool ok = gtc::mbar_wait(q_full, 0) && issue_scores(0);
+      bool ok = gtc::mbar_wait(q_full, 0) && issue_scores(0) && (nkb < 2 || issue_scores(1));
       for (int j = 0; j < nkb && ok; ++j) {
-        if (j + 1 < nkb && !issue_scores(j + 1)) break;  // the next block's scores overlap this block's softmax
-        if (!gtc::mbar_wait(p_full, (unsigned)j & 1u)) break;
+        const int vs = j % kVStages;
+        if (!gtc::mbar_wait(p_full, (unsigned)j & 1u) || !gtc::mbar_wait(v_full + vs, (unsigned)(j / kVStages) & 1u))
+          break;
         gtc::tc_fence_after();
-        const uint8_t *v = skv + (size_t)(j % kStages) * 2 * kTile + kTile;
+        const uint8_t *v = sv + (size_t)vs * kTile;
+        const uint32_t pa = tmem + kPCol + (uint32_t)((j & 1) * 64);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {  // 16 keys per step: 16 rows of 128 bytes of V
-          const int half = kk >> 2;
-          umma(tmem + kOCol, gtc::sw128_desc(sp + half * kHalf) + (uint64_t)(2 * (kk & 3)),
-               sw128_mn_desc(v + (size_t)kk * 16 * 128), kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kBK / 16; ++kk)  // 16 keys per step: 8 columns of P, 16 rows of 128 bytes of V
+          umma_ts(tmem + kOCol, pa + (uint32_t)(8 * kk), sw128_mn_desc(v + (size_t)kk * 16 * 128), kIdescO,
+                  (j > 0 || kk > 0) ? 1u : 0u);
+        gtc::umma_commit(v_empty + vs);  // the V slot is free once these MMAs have read it
         gtc::umma_commit(o_done);
-        gtc::umma_commit(kv_empty + j % kStages);  // the K/V slot is free once these MMAs have read it
+        if (j + 2 < nkb && !issue_scores(j + 2)) break;  // block j + 2's scores overlap the softmax of j + 1
       }
       gtc::umma_commit(mma_done);  // completes once every MMA issued above has finished
       gtc::mbar_drain(mma_done, 0);
@@ -240,11 +304,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_prefill_kernel(const __grid_
     bool ok = true;
     for (int j = 0; j < nkb; ++j) {
       ok = ok && warp_wait(s_full + (j & 1), (unsigned)(j >> 1) & 1u);
-      uint32_t sv[kCols];
+      uint32_t sc[kCols];
       float mx = -INFINITY;
       if (ok) {
         gtc::tc_fence_after();
-        tmem_ld32(taddr + (uint32_t)((j & 1) * kBK + c0), sv);
+        tmem_ld32(taddr + (uint32_t)((j & 1) * kBK + c0), sc);
         tmem_wait_ld();
         // columns past `lim` are keys after the row's position (lim >= kCols - 1: none)
         const int lim = (int64_t)j * kBK + kBK - 1 > mask_from
@@ -252,9 +316,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_prefill_kernel(const __grid_
                             : kCols;
 #pragma unroll
         for (int c = 0; c < kCols; ++c) {
-          float x = __uint_as_float(sv[c]);
+          float x = __uint_as_float(sc[c]);
           if (c > lim) x = -INFINITY;
-          sv[c] = __float_as_uint(x);
+          sc[c] = __float_as_uint(x);
           mx = fmaxf(mx, x);
         }
       }
@@ -270,40 +334,38 @@ __global__ void __launch_bounds__(kThreads, 1) attn_prefill_kernel(const __grid_
         alpha = ex2(m_run - bm);  // 0 on the first block (m_run = -inf)
         m_run = bm;
       }
-      float sum = 0.f;
+      // p = 2^(s scale log2(e) - m): the exponent argument two at a time, sums in two fp32 lanes
+      const uint64_t sc2 = f2_pack(A.scale_log2, A.scale_log2), nm2 = f2_pack(-m_run, -m_run);
+      uint64_t sum2 = f2_pack(0.f, 0.f);
       uint32_t pk[kCols / 2];
 #pragma unroll
       for (int c = 0; c < kCols; c += 2) {
-        const float p0 = ex2(fmaf(__uint_as_float(sv[c]), A.scale_log2, -m_run));
-        const float p1 = ex2(fmaf(__uint_as_float(sv[c + 1]), A.scale_log2, -m_run));
-        sum += p0 + p1;
+        const float2 e = f2_unpack(f2_fma(f2_pack(__uint_as_float(sc[c]), __uint_as_float(sc[c + 1])), sc2, nm2));
+        const float p0 = ex2(e.x), p1 = ex2(e.y);
+        sum2 = f2_add(sum2, f2_pack(p0, p1));
         pk[c / 2] = gtc::pack_bf16x2(p0, p1);
       }
-      l_part = l_part * alpha + sum;
-      if (ok && j > 0) {
-        // the previous P.V has finished: the P buffer is free and O holds every block before this one
+      const float2 sum = f2_unpack(sum2);
+      l_part = l_part * alpha + (sum.x + sum.y);
+      if (ok && j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // rescale O once the previous P.V has finished (O then holds every block before this one)
         ok = warp_wait(o_done, (unsigned)(j - 1) & 1u);
         if (ok) {
           gtc::tc_fence_after();
-          if (__any_sync(0xffffffffu, alpha != 1.f)) {
-            uint32_t o[kCols];
-            tmem_ld32(taddr + kOCol + (uint32_t)c0, o);
-            tmem_wait_ld();
+          uint32_t o[kCols];
+          tmem_ld32(taddr + kOCol + (uint32_t)c0, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < kCols; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(taddr + kOCol + (uint32_t)c0, o);
-            tmem_wait_st();
-          }
+          for (int e = 0; e < kCols; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(taddr + kOCol + (uint32_t)c0, o);
+          tmem_wait_st();
         }
       }
       if (ok) {
-        // keys c0 .. c0 + 31 of the P row: half c0 / 64, 16-byte chunks (c0 % 64) / 8 .. + 3 at (chunk ^ (row & 7)) * 16
-        uint8_t *prow = sp + (size_t)(c0 >> 6) * kHalf + (size_t)row * 128;
-        const int cb = (c0 & 63) >> 3;
-#pragma unroll
-        for (int c = 0; c < kCols / 8; ++c)
-          *(uint4 *)(prow + (((cb + c) ^ (row & 7)) << 4)) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> the tensor cores' reads
+        // P_j, keys c0 .. c0 + 31 of the row as 16 packed columns, into TMEM buffer j % 2: the P.V of block j - 2
+        // has finished reading it (S_j's commit completes after that MMA)
+        tmem_st16(taddr + kPCol + (uint32_t)((j & 1) * 64 + c0 / 2), pk);
+        tmem_wait_st();
         gtc::tc_fence_before();
         gtc::mbar_arrive(p_full);
       }

@@ -157,6 +157,21 @@ __global__ void __launch_bounds__(kRowThreads) argmax_rows_kernel(int64_t *out, 
 
 using namespace egpt;
 
+// out[r, i] = bf16(bf16(silu(g)) * u) with g = gu[r, i], u = gu[r, inter + i]: the HF MLP's act_fn(gate) * up in
+// eager bf16 (SiLU evaluated in fp32 and rounded, the product rounded), two columns per thread.
+__global__ void silu_mul_kernel(uint16_t *out, int64_t ldo, const uint16_t *gu, int64_t ldg, int64_t rows,
+                                int64_t inter) {
+  const int64_t half = inter / 2, pairs = rows * half;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < pairs; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / half, c = 2 * (i - r * half);
+    const uint32_t g2 = *(const uint32_t *)(gu + r * ldg + c), u2 = *(const uint32_t *)(gu + r * ldg + inter + c);
+    const float g0 = bf16_lo(g2), g1 = bf16_hi(g2);
+    const float a0 = round_bf16(g0 / (1.0f + expf(-g0))) * bf16_lo(u2);
+    const float a1 = round_bf16(g1 / (1.0f + expf(-g1))) * bf16_hi(u2);
+    *(uint32_t *)(out + r * ldo + c) = (uint32_t)f32_to_bf16_bits(a0) | ((uint32_t)f32_to_bf16_bits(a1) << 16);
+  }
+}
+
 extern "C" int egpt_quantize_rows(int8_t *q, void *scale, int scale_dtype, const void *w, int w_dtype, int64_t n,
                                   int64_t k, void *stream) {
   clear_error();
@@ -211,4 +226,19 @@ extern "C" int egpt_argmax_rows(int64_t *out, const void *logits, int64_t rows, 
   return check_launch(launch_kernel((const void *)argmax_rows_kernel, dim3((unsigned)rows), dim3(kRowThreads), 0,
                                     (cudaStream_t)stream, false, out, logits, n, ld, (int)(dtype == EGPT_BF16)),
                       "argmax_rows_kernel");
+}
+
+extern "C" int egpt_silu_mul(void *out, int64_t ldo, const void *gu, int64_t ldg, int64_t rows, int64_t inter,
+                             void *stream) {
+  clear_error();
+  if (!out || !gu) return set_error(EGPT_ERR_ARG, "silu_mul: null pointer");
+  if (rows < 1 || inter < 2 || inter % 2 || ldo < inter || ldg < 2 * inter)
+    return set_error(EGPT_ERR_SHAPE, "silu_mul: bad shape (inter even, ldo >= inter, ldg >= 2 inter)");
+  if ((uintptr_t)out % 4 || (uintptr_t)gu % 4 || ldo % 2 || ldg % 2)
+    return set_error(EGPT_ERR_ALIGN, "silu_mul: 4-byte aligned rows");
+  const int64_t pairs = rows * (inter / 2);
+  const unsigned grid = (unsigned)std::min<int64_t>((pairs + kRowThreads - 1) / kRowThreads, (int64_t)num_sms() * 16);
+  silu_mul_kernel<<<grid, kRowThreads, 0, (cudaStream_t)stream>>>((uint16_t *)out, ldo, (const uint16_t *)gu, ldg,
+                                                                  rows, inter);
+  return check_launch(cudaGetLastError(), "silu_mul_kernel");
 }

@@ -52,6 +52,7 @@ struct Args {
   uint16_t *y;
   int64_t M, N, K, ldy;
   int double_round;
+  int add_out;    // y holds the residual on entry: y = bf16(y + result)
   int ksplit;     // k ranges per output tile (work unit = tile x range); > 1: fp32 partials into ws, then reduce
   float *ws;      // [ksplit][M][N] fp32 partial sums (ksplit > 1)
 };
@@ -340,6 +341,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_i8_tc_kernel(const __grid_co
             packed[j / 2] = (uint32_t)f32_to_bf16_bits(y2[0]) | ((uint32_t)f32_to_bf16_bits(y2[1]) << 16);
           }
           uint16_t *dst = A.y + m * A.ldy + n0 + c0;
+          if (A.add_out) {  // y = bf16(residual + bf16(result)), the residual read from y itself
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int64_t n = n0 + c0 + 2 * j;
+              const uint32_t r = n + 1 < A.N ? *(const uint32_t *)(dst + 2 * j) : (n < A.N ? (uint32_t)dst[2 * j] : 0u);
+              packed[j] = (uint32_t)f32_to_bf16_bits(bf16_lo(r) + bf16_lo(packed[j])) |
+                          ((uint32_t)f32_to_bf16_bits(bf16_hi(r) + bf16_hi(packed[j])) << 16);
+            }
+          }
           if (n0 + c0 + 32 <= A.N) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) ((uint4 *)dst)[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
@@ -382,7 +392,13 @@ __global__ void __launch_bounds__(256) gemm_reduce_kernel(const __grid_constant_
     if (A.double_round) acc0 = round_bf16(acc0), acc1 = round_bf16(acc1);
     const float s0 = A.s_bf16 ? bf16_bits_to_f32(((const uint16_t *)A.s)[n]) : ((const float *)A.s)[n];
     const float s1 = A.s_bf16 ? bf16_bits_to_f32(((const uint16_t *)A.s)[n + 1]) : ((const float *)A.s)[n + 1];
-    *(uint32_t *)(A.y + m * A.ldy + n) = (uint32_t)f32_to_bf16_bits(acc0 * s0) | ((uint32_t)f32_to_bf16_bits(acc1 * s1) << 16);
+    uint32_t *dst = (uint32_t *)(A.y + m * A.ldy + n);
+    float y0 = acc0 * s0, y1 = acc1 * s1;
+    if (A.add_out) {  // y = bf16(residual + bf16(result)), the residual read from y itself
+      const uint32_t r = *dst;
+      y0 = bf16_lo(r) + round_bf16(y0), y1 = bf16_hi(r) + round_bf16(y1);
+    }
+    *dst = (uint32_t)f32_to_bf16_bits(y0) | ((uint32_t)f32_to_bf16_bits(y1) << 16);
   }
 }
 
@@ -436,6 +452,7 @@ extern "C" int egpt_gemm_i8_tc(void *y, int64_t ldy, const void *x, int64_t ldx,
     return set_error(EGPT_ERR_ALIGN, "gemm_i8_tc: tensor map of q rejected");
   A.q = q, A.s = s, A.s_bf16 = s_dtype == EGPT_BF16, A.y = (uint16_t *)y;
   A.M = M, A.N = N, A.K = K, A.ldy = ldy, A.double_round = (flags & EGPT_FLAG_DOUBLE_ROUND) ? 1 : 0;
+  A.add_out = (flags & EGPT_FLAG_ADD_OUT) ? 1 : 0;
   // split K over several CTAs per output tile when the tiles alone leave SMs idle (few rows: decode batches,
   // short prompts), given the workspace for the fp32 partials; else one range per tile
   A.ksplit = 1;

@@ -227,10 +227,13 @@ def argmax_rows(logits):
     return out.reshape(logits.shape[:-1])
 
 
-def gemm_i8_tc(x, w, s, *, double_round=True, out=None, ws=None):
+def gemm_i8_tc(x, w, s, *, double_round=True, out=None, ws=None, add_out=False):
     """bf16 [M, K] x int8 [N, K]^T on the tcgen05 tensor cores -> bf16 [M, N]: bf16(bf16(acc) * s) (the reference's
     >16-row arithmetic) or, with double_round=False, bf16(acc * s). K a multiple of 64. Few rows split K over
-    several CTAs per tile with an fp32 workspace (allocated here unless `ws` is given)."""
+    several CTAs per tile with an fp32 workspace (allocated here unless `ws` is given). add_out: `out` holds the
+    residual and becomes bf16(out + result) (the HF residual add, fused)."""
+    if add_out and out is None:
+        raise ValueError('gemm_i8_tc: add_out needs out (the residual)')
     _cuda(x, w, s)
     if x.dtype != torch.bfloat16 or w.dtype != torch.int8 or x.dim() != 2 or w.dim() != 2:
         raise ValueError('gemm_i8_tc: x bf16 [M, K], w int8 [N, K]')
@@ -244,6 +247,21 @@ def gemm_i8_tc(x, w, s, *, double_round=True, out=None, ws=None):
     if ws is None and need:
         ws = torch.empty(need, dtype=torch.uint8, device=x.device)
     L.check(L.load().egpt_gemm_i8_tc(_p(out), out.stride(0), _p(x), x.stride(0), m, _p(w), _p(s), _dt(s), n, k,
-                                     L.FLAG_DOUBLE_ROUND if double_round else 0, _p(ws),
+                                     (L.FLAG_DOUBLE_ROUND if double_round else 0) | (L.FLAG_ADD_OUT if add_out else 0),
+                                     _p(ws),
                                      0 if ws is None else ws.numel(), _stream()), 'gemm_i8_tc')
+    return out
+
+
+def silu_mul(gu, inter, out=None):
+    """bf16(bf16(silu(gate)) * up) over rows of the gate|up output gu bf16 [M, >= 2 inter] (gate columns first)."""
+    _cuda(gu, out)
+    _contig_rows(gu, 'gu')
+    if gu.dtype != torch.bfloat16:
+        raise ValueError('silu_mul: bf16 rows')
+    m = gu.shape[0]
+    if out is None:
+        out = torch.empty(m, inter, dtype=torch.bfloat16, device=gu.device)
+    _contig_rows(out, 'out')
+    L.check(L.load().egpt_silu_mul(_p(out), out.stride(0), _p(gu), gu.stride(0), m, int(inter), _stream()), 'silu_mul')
     return out

@@ -21,13 +21,17 @@ import torch.nn.functional as F
 from . import ops
 
 
-def _proj(x, q, s):
+def _proj(x, q, s, residual=None):
     """bf16(bf16(x @ bf16(q).T) * s): the op's >16-row arithmetic (int8_linear.py:96-97), on this library's tcgen05
-    GEMM (int8 rows widened to bf16 in shared memory, fp32 accumulation in TMEM)."""
+    GEMM (int8 rows widened to bf16 in shared memory, fp32 accumulation in TMEM). With `residual` the result is
+    bf16(residual + y), the HF residual add, done in the GEMM's epilogue into `residual` itself."""
     if x.shape[-1] % 64 == 0:
+        if residual is not None:
+            return ops.gemm_i8_tc(x.contiguous(), q, s, double_round=True, out=residual, add_out=True)
         return ops.gemm_i8_tc(x.contiguous(), q, s, double_round=True)
     y = torch.matmul(x, q.to(torch.bfloat16).t())  # widths the tcgen05 tiles do not take
-    return (y.float() * s.float()).to(torch.bfloat16)
+    y = (y.float() * s.float()).to(torch.bfloat16)
+    return y if residual is None else residual + y
 
 
 def _attend(q, k_cache, v_cache, pos0, nq, nkv, d):
@@ -84,17 +88,20 @@ def fill_kv(ids, layers, embed, kv, rope_cos, rope_sin, nq, nkv, d, eps, allredu
             # the last layer only matters for the last row: its attention over the prompt, then o_proj and the MLP
             # on that row (the per-element arithmetic of the >16-row branch does not depend on the row count)
             a = _attend(q[p - 1:p], kv[i, 0], kv[i, 1], p - 1, nq, nkv, d)
-            hl = h[p - 1:p] + _proj(a, lay['w_o'], lay['s_o'])
+            hl = _proj(a, lay['w_o'], lay['s_o'], residual=h[p - 1:p])
             x = ops.rmsnorm(hl, lay['ln_post'], eps)
             gu = _proj(x, lay['w_gu'], lay['s_gu'])
-            return hl + _proj(F.silu(gu[:, :inter]) * gu[:, inter:], lay['w_down'], lay['s_down'])
+            return _proj(ops.silu_mul(gu, inter), lay['w_down'], lay['s_down'], residual=hl)
         a = _attend(q, kv[i, 0], kv[i, 1], 0, nq, nkv, d)
-        o = _proj(a, lay['w_o'], lay['s_o']) if allreduce is None else _proj_partial(a, lay['w_o'], lay['s_o'], allreduce)
-        h = h + o
+        if allreduce is None:
+            h = _proj(a, lay['w_o'], lay['s_o'], residual=h)
+        else:
+            h = h + _proj_partial(a, lay['w_o'], lay['s_o'], allreduce)
         x = ops.rmsnorm(h, lay['ln_post'], eps)
         gu = _proj(x, lay['w_gu'], lay['s_gu'])
-        act = F.silu(gu[:, :inter]) * gu[:, inter:]
-        dn = (_proj(act, lay['w_down'], lay['s_down']) if allreduce is None
-              else _proj_partial(act, lay['w_down'], lay['s_down'], allreduce))
-        h = h + dn
+        act = ops.silu_mul(gu, inter)
+        if allreduce is None:
+            h = _proj(act, lay['w_down'], lay['s_down'], residual=h)
+        else:
+            h = h + _proj_partial(act, lay['w_down'], lay['s_down'], allreduce)
     return p

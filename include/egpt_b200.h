@@ -60,6 +60,7 @@ extern "C" {
 #define EGPT_FLAG_EXACT 512u      /* GEMV, one bf16 row: exact int8 tensor-core sums, one rounding per row    */
 #define EGPT_FLAG_RAGGED 1024u    /* attention: the m rows are m sequences, row i at position[i] with its own
                                      cache (kv heads [i nkv, (i + 1) nkv) of caches laid out [m nkv][cap][d]) */
+#define EGPT_FLAG_ADD_OUT 2048u   /* GEMM: y holds the residual on entry and becomes bf16(y + result)         */
 
 /* ---- library ---------------------------------------------------------------------------------------- */
 EGPT_API const char *egpt_version(void);
@@ -194,9 +195,18 @@ EGPT_API int egpt_argmax_rows(int64_t *out, const void *logits, int64_t rows, in
  * CTAs per tile if ws holds egpt_gemm_i8_tc_ws_bytes(M, N, K) bytes (16-byte aligned; fp32 partials, no
  * zero-fill needed), followed by a reduce launch; with a smaller (or NULL) ws one CTA takes each tile. */
 EGPT_API size_t egpt_gemm_i8_tc_ws_bytes(int64_t M, int64_t N, int64_t K);
+/* With EGPT_FLAG_ADD_OUT y is also the residual: y = bf16(y + bf16(result)), the HF residual add of o_proj and
+ * down_proj fused into the epilogue. */
 EGPT_API int egpt_gemm_i8_tc(void *y, int64_t ldy, const void *x, int64_t ldx, int64_t M, const int8_t *q,
                              const void *s, int s_dtype, int64_t N, int64_t K, unsigned flags, void *ws,
                              size_t ws_bytes, void *stream);
+
+/* ---- SwiGLU activation over prefill rows ----------------------------------------------------------------
+ * replaces: act_fn(gate_proj(x)) * up_proj(x) of the HF Qwen3 MLP (modeling_qwen3.py:81-82) on the prompt rows:
+ * out[r, i] = bf16(bf16(silu(g)) * u), g = gu[r, i], u = gu[r, inter + i] for the gate|up GEMM output gu [rows][ldg]
+ * (gate columns, then up columns), out [rows][ldo], bf16, inter even. */
+EGPT_API int egpt_silu_mul(void *out, int64_t ldo, const void *gu, int64_t ldg, int64_t rows, int64_t inter,
+                           void *stream);
 
 /* ---- stochastic sampling: temperature -> top-k -> top-p -> inverse CDF -------------------------------
  * replaces: filtered_probs + sample_from (research/phase5/sampling.py:39-71; the Triton families

@@ -60,3 +60,37 @@ def test_gemm_i8_tc_guards(cuda):
         ops.gemm_i8_tc(x, q, s)
     with pytest.raises(ValueError):
         ops.gemm_i8_tc(x.float(), q, s)
+
+
+@pytest.mark.parametrize('m,n,k', [(300, 2048, 2048), (5, 4096, 6144), (4096, 768, 4096)])
+def test_gemm_i8_tc_residual_add_in_epilogue(cuda, m, n, k):
+    """EGPT_FLAG_ADD_OUT: out = bf16(residual + bf16(result)), the HF residual add of o_proj/down_proj over the
+    prompt rows, equal bit for bit to the GEMM followed by PyTorch's bf16 add (split-K rows included)."""
+    from efficientgpt_b200 import ops
+    g = torch.Generator(device='cuda').manual_seed(m + n)
+    x = torch.randn(m, k, generator=g, device='cuda').to(torch.bfloat16)
+    q = torch.randint(-127, 128, (n, k), generator=g, device='cuda', dtype=torch.int8)
+    s = (torch.rand(n, generator=g, device='cuda') * 0.02 + 0.001).to(torch.bfloat16)
+    h = torch.randn(m, n, generator=g, device='cuda').to(torch.bfloat16)
+    want = h + ops.gemm_i8_tc(x, q, s)
+    got = h.clone()
+    out = ops.gemm_i8_tc(x, q, s, out=got, add_out=True)
+    assert out.data_ptr() == got.data_ptr()
+    assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize('m,inter', [(1, 6144), (300, 6144), (33, 12288), (7, 2)])
+def test_silu_mul_matches_eager_bf16(cuda, m, inter):
+    """egpt_silu_mul: bf16(bf16(silu(gate)) * up) as the HF MLP evaluates it in eager bf16 (modeling_qwen3.py:81-82);
+    within one bf16 ulp of PyTorch's F.silu(gate) * up (CUDA's expf and PyTorch's may differ in the last fp32 bit,
+    which can move a bf16 rounding), and identical for at least 99.9% of the values."""
+    import torch.nn.functional as F
+    from efficientgpt_b200 import ops
+    g = torch.Generator(device='cuda').manual_seed(m + inter)
+    gu = (torch.randn(m, 2 * inter, generator=g, device='cuda') * 3).to(torch.bfloat16)
+    got = ops.silu_mul(gu, inter)
+    want = F.silu(gu[:, :inter]) * gu[:, inter:]
+    assert got.shape == want.shape
+    diff = (got.float() - want.float()).abs()
+    assert bool((diff <= _ulp(want.float())).all())
+    assert float((got == want).float().mean()) >= 0.999
