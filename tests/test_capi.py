@@ -54,6 +54,15 @@ def test_argument_validation_without_launch():
     assert rc == L.EGPT_ERR_WORKSPACE
     with pytest.raises(ValueError, match='workspace'):
         L.check(rc, 'lm_head_argmax')
+    # prefill attention and SwiGLU: shape checks before any tensor map or launch
+    rc = lib.egpt_attn_prefill(dummy, 2048, dummy, 2048, dummy, dummy, 64, 0, 16, 16, 8, 64, 0.1, null)
+    assert rc == L.EGPT_ERR_SHAPE and 'head_dim' in L.last_error()
+    rc = lib.egpt_attn_prefill(dummy, 2048, dummy, 2048, dummy, dummy, 64, 60, 16, 16, 8, 128, 0.1, null)
+    assert rc == L.EGPT_ERR_SHAPE  # pos0 + m > cap
+    rc = lib.egpt_attn_prefill(null, 2048, dummy, 2048, dummy, dummy, 64, 0, 16, 16, 8, 128, 0.1, null)
+    assert rc == L.EGPT_ERR_ARG
+    rc = lib.egpt_silu_mul(dummy, 8, dummy, 16, 4, 7, null)
+    assert rc == L.EGPT_ERR_SHAPE  # odd width
 
 
 def test_ops_reject_cpu_tensors():
@@ -65,6 +74,11 @@ def test_ops_reject_cpu_tensors():
         quantize_weight(torch.randn(4, 4))
     with pytest.raises(ValueError, match='bf16'):
         int8_linear(torch.zeros(2, 32), torch.zeros(8, 32, dtype=torch.int8), torch.ones(8))
+    with pytest.raises(ValueError, match='CUDA'):
+        ops.silu_mul(torch.zeros(2, 16, dtype=torch.bfloat16), 8)
+    with pytest.raises(ValueError, match='CUDA'):
+        ops.attn_prefill(torch.zeros(4, 256, dtype=torch.bfloat16), torch.zeros(1, 8, 128, dtype=torch.bfloat16),
+                         torch.zeros(1, 8, 128, dtype=torch.bfloat16), 0, 2, 1, 128, scale=0.1)
 
 
 def test_plan_struct_layout_matches_the_header(tmp_path):
