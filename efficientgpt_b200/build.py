@@ -15,7 +15,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / 'csrc'
 LIB_DIR = PKG / '_lib'
 LIB = LIB_DIR / 'libegpt_b200.so'
-SOURCES = ['egpt_b200.cu', 'capi.cu', 'elementwise.cu', 'gemv_i8.cu', 'attention.cu', 'decode_step.cu', 'decode_dataflow.cu', 'gemv_tc.cu', 'sampling.cu', 'gemm_tc.cu', 'attn_prefill.cu', 'common.cuh',
+SOURCES = ['egpt_b200.cu', 'capi.cu', 'elementwise.cu', 'gemv_i8.cu', 'attention.cu', 'decode_step.cu', 'decode_dataflow.cu', 'gemv_tc.cu', 'sampling.cu', 'gemm_tc.cu', 'attn_prefill.cu', 'attn_stream.cu', 'common.cuh',
            'internal.h']
 HEADER = PKG.parent / 'include' / 'egpt_b200.h'
 

@@ -10,3 +10,4 @@
 #include "sampling.cu"
 #include "gemm_tc.cu"
 #include "attn_prefill.cu"
+#include "attn_stream.cu"
