@@ -6,13 +6,13 @@
 //
 // Grid (nkv, ranges): a CTA owns one kv head, its GRP q heads and one range of whole 128-key blocks (ranges sized
 // from L on the device, so a captured graph follows the position). A kv head's K rows (and V rows) are one
-// contiguous stream, so a block of 128 keys is one 32 KB bulk copy (cp.async.bulk, this GPU's memory, no
-// multicast): warp 8 keeps K and V blocks in flight through a 3-stage ring (192 KB), completion by transaction
-// count on the stage's mbarrier; two stages load while the eight compute warps work on the third. Warp w takes
-// keys 16 w .. 16 w + 15 of every block: lanes l and l + 16 score key l over the two halves of the row for every q
-// head (16-byte pieces rotated by the key so that a shared-memory phase reads different bank groups; q from
-// shared memory), the warp keeps its own running maximum, sum and P.V accumulator per q head (lane l: dims
-// 4l .. 4l + 3; probabilities enter P.V rounded to bf16, the sums use the fp32 values), and releases the stage.
+// contiguous stream, so a block of 128 keys is 32 KB of consecutive bytes, copied as eight 4 KB bulk copies
+// (cp.async.bulk, this GPU's memory, no multicast): warp 8 keeps K and V blocks in flight through a 3-stage
+// ring (192 KB), completion by transaction count on the stage's mbarrier; two stages load while the eight compute
+// warps work on the third. Warp w takes keys 16 w .. 16 w + 15 of every block: lane l reads dims 4l .. 4l + 3 of
+// each key row (q's same dims in registers) and one reduce-scatter of the partial dot products leaves every
+// score in one lane; the warp keeps a running maximum, sum and P.V accumulator per q head (lane l: dims
+// 4l .. 4l + 3; probabilities enter P.V rounded to bf16, the sums use the fp32 values) and releases the stage.
 // The warps merge in a fixed order; one range writes the output, several write partials (maximum, sum,
 // unnormalised output, base-2 exponents) and the last range of the kv head to arrive combines them. Every wait
 // is bounded (EGPT_ERR_TIMEOUT); the producer drains its copies before the CTA exits.
@@ -23,10 +23,11 @@ namespace egpt {
 namespace ast {
 
 constexpr int kD = 128;
-constexpr int kBlock = 128;                 // keys per bulk copy (one softmax block of the reference kernel)
+constexpr int kBlock = 128;                 // keys per ring stage
 constexpr int kStages = 3;
 constexpr int kRowBytes = kD * 2;           // bf16 row: 256 bytes
 constexpr int kBlockBytes = kBlock * kRowBytes;
+constexpr unsigned kPiece = 16 * kRowBytes; // bytes per bulk copy: 4 KB
 constexpr int kWarps = 8;                   // compute warps, 16 keys of every block each
 constexpr int kThreads = (kWarps + 1) * 32; // + the copy warp
 
@@ -100,8 +101,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_stream_kernel(AttnParams p) 
         if (b >= kStages && !gtc::mbar_wait(S.empty + s, (unsigned)((b / kStages) - 1) & 1u)) break;
         const unsigned bytes = (unsigned)(min((int64_t)kBlock, k1 - k0 - (int64_t)b * kBlock) * kRowBytes);
         gtc::mbar_arrive_tx(S.full + s, 2 * bytes);
-        df::bulk_copy(S.ring[s][0], Kg + (int64_t)b * kBlockBytes, bytes, S.full + s);
-        df::bulk_copy(S.ring[s][1], Vg + (int64_t)b * kBlockBytes, bytes, S.full + s);
+        for (unsigned o = 0; o < bytes; o += kPiece) {  // pieces of 16 rows: more copies in flight at once
+          const unsigned n = min(kPiece, bytes - o);
+          df::bulk_copy(S.ring[s][0] + o, Kg + (int64_t)b * kBlockBytes + o, n, S.full + s);
+          df::bulk_copy(S.ring[s][1] + o, Vg + (int64_t)b * kBlockBytes + o, n, S.full + s);
+        }
         ++issued;
       }
       for (int b = max(0, issued - kStages); b < issued; ++b)  // nothing may still be landing at exit
@@ -109,15 +113,25 @@ __global__ void __launch_bounds__(kThreads, 1) attn_stream_kernel(AttnParams p) 
     }
   } else {
     // ---------------------------------------------------------------- compute warps
-    // every block: warp w takes keys 16 w .. 16 w + 15; lane l scores key l % 16 over dims 64 (l / 16) .. + 63
-    const int slice = 16 * warp, kl = lane & 15, half = lane >> 4;
-    float m_run[GRP], l_run[GRP], acc[GRP][4];
+    // every block: warp w takes keys 16 w .. 16 w + 15. Lane l holds q's dims 4l .. 4l + 3 of every head and forms
+    // the partial dot products of those dims with each key (index 16 j + k for head j, key k); one reduce-scatter
+    // leaves every total in one lane (GRP 1: key l / 2 in lanes l, two copies; GRP 2: index l; GRP 4: indices 2l,
+    // 2l + 1).
+    constexpr int NV = 16 * GRP, NS = NV > 32 ? NV / 32 : 1;  // values held per lane after the reduce-scatter
+    constexpr int HL = 32 / GRP;                              // lanes per head after it
+    const int slice = 16 * warp;
+    float qr[GRP][4];
 #pragma unroll
     for (int j = 0; j < GRP; ++j) {
-      m_run[j] = -INFINITY;
-      l_run[j] = 0.f;
-      acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+      const float4 t = *(const float4 *)&S.q[j][4 * lane];
+      qr[j][0] = t.x, qr[j][1] = t.y, qr[j][2] = t.z, qr[j][3] = t.w;
     }
+    const int head = lane / HL;  // the head of this lane's totals
+    float m_run = -INFINITY;     // running maximum of that head (the same in all its lanes)
+    float l_lane = 0.f;          // this lane's share of that head's sum
+    float acc[GRP][4];
+#pragma unroll
+    for (int j = 0; j < GRP; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
     for (int b = 0; b < nblk; ++b) {
       const int s = b % kStages;
       if (!__all_sync(0xffffffffu, gtc::mbar_wait(S.full + s, (unsigned)(b / kStages) & 1u))) break;
@@ -125,57 +139,77 @@ __global__ void __launch_bounds__(kThreads, 1) attn_stream_kernel(AttnParams p) 
       if (nvalid > 0) {
         const uint8_t *Ks = S.ring[s][0] + (size_t)slice * kRowBytes;
         const uint8_t *Vs = S.ring[s][1] + (size_t)slice * kRowBytes;
-        // scores (base-2 exponent units): half a row per lane, 16-byte pieces rotated by the key so that the
-        // lanes of a shared-memory phase read different bank groups
-        float a[GRP][2];
+        float v[NV];
 #pragma unroll
-        for (int j = 0; j < GRP; ++j) a[j][0] = a[j][1] = 0.f;
-        if (kl < nvalid) {
-          const uint4 *row = (const uint4 *)(Ks + (size_t)kl * kRowBytes);
-          const int rot = kl & 7;
-#pragma unroll 4
-          for (int u = 0; u < 8; ++u) {
-            const int pc = 8 * half + ((u + rot) & 7);
-            const uint4 w = row[pc];
-            const float kv[8] = {bf16_lo(w.x), bf16_hi(w.x), bf16_lo(w.y), bf16_hi(w.y),
-                                 bf16_lo(w.z), bf16_hi(w.z), bf16_lo(w.w), bf16_hi(w.w)};
+        for (int k = 0; k < 16; ++k) {  // rows past nvalid give totals that are masked below
+          const uint2 w = *(const uint2 *)(Ks + (size_t)k * kRowBytes + 8 * lane);
+          const float k0v = bf16_lo(w.x), k1v = bf16_hi(w.x), k2v = bf16_lo(w.y), k3v = bf16_hi(w.y);
 #pragma unroll
-            for (int j = 0; j < GRP; ++j) {
-              const float4 q0 = *(const float4 *)&S.q[j][8 * pc], q1 = *(const float4 *)&S.q[j][8 * pc + 4];
-              a[j][0] = fmaf(q0.x, kv[0], a[j][0]);
-              a[j][1] = fmaf(q0.y, kv[1], a[j][1]);
-              a[j][0] = fmaf(q0.z, kv[2], a[j][0]);
-              a[j][1] = fmaf(q0.w, kv[3], a[j][1]);
-              a[j][0] = fmaf(q1.x, kv[4], a[j][0]);
-              a[j][1] = fmaf(q1.y, kv[5], a[j][1]);
-              a[j][0] = fmaf(q1.z, kv[6], a[j][0]);
-              a[j][1] = fmaf(q1.w, kv[7], a[j][1]);
+          for (int j = 0; j < GRP; ++j)
+            v[16 * j + k] = fmaf(qr[j][0], k0v, qr[j][1] * k1v) + fmaf(qr[j][2], k2v, qr[j][3] * k3v);
+        }
+        // reduce-scatter: at offset o the lane keeps the upper half of its values if (lane & o), else the lower
+        int cnt = NV;
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+          if (cnt > 1) {
+            const int hv = cnt / 2;
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < NV / 2; ++i) {
+              if (i < hv) {
+                const float send = up ? v[i] : v[i + hv];
+                const float keep = up ? v[i + hv] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+              }
             }
+            cnt = hv;
+          } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
           }
         }
-        float pr[GRP];
+        // this lane's keys and the block maximum of its head (scores are in base-2 exponent units)
+        float x[NS];
+        float bm = -INFINITY;
+#pragma unroll
+        for (int t = 0; t < NS; ++t) {
+          const int key = GRP == 1 ? lane >> 1 : (GRP == 2 ? lane & 15 : ((2 * lane + t) & 15));
+          x[t] = key < nvalid ? v[t] : -INFINITY;
+          bm = fmaxf(bm, x[t]);
+        }
+#pragma unroll
+        for (int o = HL / 2; o >= 1; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+        const float m_new = fmaxf(m_run, bm);  // finite: the slice has a valid key
+        const float alpha = ex2(m_run - m_new);  // 0 while m_run = -inf
+        m_run = m_new;
+        float pr[NS];
+        float psum = 0.f;
+#pragma unroll
+        for (int t = 0; t < NS; ++t) {
+          const float pv = x[t] == -INFINITY ? 0.f : ex2(x[t] - m_new);
+          psum += pv;
+          pr[t] = round_bf16(pv);  // P.V takes the bf16 probability
+        }
+        if (GRP == 1 && (lane & 1)) psum = 0.f;  // the odd lane of a pair holds a second copy
+        l_lane = l_lane * alpha + psum;
+        // P.V: lane l accumulates dims 4l .. 4l + 3; head j's alpha and probabilities come from the lanes that hold
+        // them
 #pragma unroll
         for (int j = 0; j < GRP; ++j) {
-          const float part = a[j][0] + a[j][1];
-          const float sc = part + __shfl_xor_sync(0xffffffffu, part, 16);  // both halves of the row
-          const float x = kl < nvalid ? sc : -INFINITY;
-          const float m_new = fmaxf(m_run[j], warp_max(x));  // finite: the slice has a valid key
-          const float alpha = ex2(m_run[j] - m_new);         // 0 while m_run = -inf
-          const float pv = kl < nvalid ? ex2(x - m_new) : 0.f;
-          l_run[j] = l_run[j] * alpha + warp_sum(half == 0 ? pv : 0.f);  // each key once
+          const float aj = __shfl_sync(0xffffffffu, alpha, j * HL);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) acc[j][e] *= alpha;
-          m_run[j] = m_new;
-          pr[j] = round_bf16(pv);  // P.V takes the bf16 probability
+          for (int e = 0; e < 4; ++e) acc[j][e] *= aj;
         }
-        // P.V: lane l accumulates dims 4l .. 4l + 3 over the slice's valid keys (key k's p sits in lane k)
 #pragma unroll 4
         for (int k = 0; k < nvalid; ++k) {
-          const uint2 v = *(const uint2 *)(Vs + (size_t)k * kRowBytes + 8 * lane);
-          const float v0 = bf16_lo(v.x), v1 = bf16_hi(v.x), v2 = bf16_lo(v.y), v3 = bf16_hi(v.y);
+          const uint2 w = *(const uint2 *)(Vs + (size_t)k * kRowBytes + 8 * lane);
+          const float v0 = bf16_lo(w.x), v1 = bf16_hi(w.x), v2 = bf16_lo(w.y), v3 = bf16_hi(w.y);
 #pragma unroll
           for (int j = 0; j < GRP; ++j) {
-            const float pk = __shfl_sync(0xffffffffu, pr[j], k);
+            float pk;
+            if (GRP == 1) pk = __shfl_sync(0xffffffffu, pr[0], 2 * k);
+            else if (GRP == 2) pk = __shfl_sync(0xffffffffu, pr[0], 16 * j + k);
+            else pk = __shfl_sync(0xffffffffu, (k & 1) ? pr[NS - 1] : pr[0], (16 * j + k) >> 1);
             acc[j][0] = fmaf(pk, v0, acc[j][0]);
             acc[j][1] = fmaf(pk, v1, acc[j][1]);
             acc[j][2] = fmaf(pk, v2, acc[j][2]);
@@ -186,9 +220,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_stream_kernel(AttnParams p) 
       __syncwarp();
       if (lane == 0) gtc::mbar_arrive(S.empty + s);  // this warp is done with the stage
     }
+    // each head's sum over its lanes
+    float l_head = l_lane;
+#pragma unroll
+    for (int o = HL / 2; o >= 1; o >>= 1) l_head += __shfl_xor_sync(0xffffffffu, l_head, o);
 #pragma unroll
     for (int j = 0; j < GRP; ++j) {
-      if (lane == 0) S.w_m[warp][j] = m_run[j], S.w_l[warp][j] = l_run[j];
+      const float mj = __shfl_sync(0xffffffffu, m_run, j * HL), lj = __shfl_sync(0xffffffffu, l_head, j * HL);
+      if (lane == 0) S.w_m[warp][j] = mj, S.w_l[warp][j] = lj;
       *(float4 *)&S.w_acc[warp][j][4 * lane] = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
     }
   }
