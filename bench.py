@@ -3,8 +3,8 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload ...]
 
-A step is one decode token: one replay of the CUDA graph that holds the native decode step (one persistent
-cooperative kernel per token). Workload = BASELINE config 2: random-init weights (seed 0), int8 per-row weights
+A step is one decode token: one replay of the CUDA graph that holds the native decode step (one cooperative kernel
+per token, the dataflow step). Workload = BASELINE config 2: random-init weights (seed 0), int8 per-row weights
 with bf16 scales, a 32-token uniform prompt, then 256 greedy tokens (contexts 33..288). Before the timed region the
 whole 256-token window runs once (every KV row of the window written); the K timed steps are then spread evenly
 over the window's positions (K >= 256: whole windows in order; K < 256: position 32 + floor(256 i / K) for step i,

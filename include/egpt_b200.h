@@ -139,7 +139,9 @@ EGPT_API int egpt_embed(void *out, const int64_t *ids, int64_t rows, const void 
  *   egpt_attn_ws_bytes(m, nq, nkv, d, max_split) bytes, zero-filled once before first use.
  *   bf16: probabilities enter P.V rounded to bf16. With EGPT_FLAG_REF_SOFTMAX they are rounded relative to
  *   the running maximum of the 128-key block walk of the reference's GPU SDPA kernel (a range then rescores
- *   the keys before it); without it each range starts its own walk (same accuracy, less work).
+ *   the keys before it); without it each range starts its own walk (same accuracy, less work). One bf16 row
+ *   (m = 1) with d = 128 and none of APPEND / RAGGED / REF_SOFTMAX streams the cache through shared memory with
+ *   bulk copies (one CTA per SM over the grid; the same workspace).
  *   dtype: bf16 (Qwen) or fp32 (nanoGPT, no norm/RoPE). */
 EGPT_API int egpt_qk_norm_rope_kv_append(void *q_out, const void *qkv, int64_t ldqkv, void *k_cache, void *v_cache,
                                 int64_t cap, const int64_t *position, int64_t m, int nq, int nkv, int d,
