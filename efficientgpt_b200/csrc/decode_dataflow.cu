@@ -333,21 +333,24 @@ __device__ int stage_input(const unsigned long long *words, const uint16_t *plai
 
 // ------------------------------------------------------------------------------------------------ weight stream
 // A warp's item stream: its items of every GEMV stage in order. Layer stage s: CTA items i = w, w + 16, ... of
-// the stage's ntl * nk (tile-major: tile-local tl = i / nk, chunk c = i % nk); lm_head: the warp's tiles w, w + 16,
-// ... whole, chunk by chunk.
+// the stage's ntl * nk (tile-major: tile-local tl = i / nk, chunk c = i % nk); lm_head: the contiguous range
+// [lm_lo(w), lm_lo(w + 1)) of those items, so every warp streams the same number of items to within one (whole
+// tiles per warp left a quarter of the warps one tile, eight items, behind the rest).
 struct Cursor {
   int s;   // stage (4 L + 1 = end)
   int i;   // layer stage: CTA item index; lm_head: tl * nk + c
 };
 __device__ __forceinline__ int stage_items(const DStage &sd) { return (int)sd.ntl * (int)sd.nk; }
+// First lm_head item of warp w (w = kW: the end).
+__device__ __forceinline__ int lm_lo(const DStage &sd, int w) { return (int)((int64_t)w * stage_items(sd) / kW); }
 
 __device__ __forceinline__ void cur_seek(const DStage *stab, int nstages, Cursor &cu) {
   const int w = threadIdx.x >> 5;
   while (cu.s < nstages) {
     const DStage &sd = stab[cu.s];
     if (sd.kind == LMHEAD) {
-      if (w < sd.ntl) {
-        cu.i = w * sd.nk;
+      if (lm_lo(sd, w) < lm_lo(sd, w + 1)) {
+        cu.i = lm_lo(sd, w);
         return;
       }
     } else if (w < stage_items(sd)) {
@@ -361,8 +364,7 @@ __device__ __forceinline__ void cur_next(const DStage *stab, int nstages, Cursor
   const DStage &sd = stab[cu.s];
   if (sd.kind == LMHEAD) {
     ++cu.i;
-    if (cu.i % sd.nk == 0) cu.i += (kW - 1) * sd.nk;  // the warp's next tile
-    if (cu.i < stage_items(sd)) return;
+    if (cu.i < lm_lo(sd, (threadIdx.x >> 5) + 1)) return;
   } else {
     cu.i += kW;
     if (cu.i < stage_items(sd)) return;
@@ -563,39 +565,83 @@ __device__ void gemv_stage(const Params &P, const DStage *stab, int nstages, int
   }
 }
 
-// lm_head stage: the warp's whole tiles (all chunks accumulate in the MMA registers), bf16 logits, argmax.
+// lm_head stage: the warp's range of items; a tile it covers whole is finished in the warp (bf16 logits, argmax),
+// the row sums of a tile it covers in part go to shared memory (slot 2w: the range's first tile, 2w + 1: its last),
+// and after a CTA barrier warp 0 adds the partial sums of each such tile (integers: exact in any order) and
+// finishes it. lm_part: kLmSlots x 16 row sums, then kLmSlots tile ids (-1: unused).
+constexpr int kLmSlots = 2 * kW;
+constexpr size_t kLmPartBytes = (size_t)kLmSlots * 16 * 8 + (size_t)kLmSlots * 8;
 struct Best {
   float v;
   int i;
 };
+__device__ __forceinline__ void lm_finish(const Params &P, const DStage &sd, int W, int tl, int r, long long T, int E,
+                                          float sc, Best &best) {
+  const int64_t row = ((int64_t)blockIdx.x + (int64_t)W * tl) * 16 + r;
+  const float l = round_bf16(ps::mul_pow2(__ll2float_rn(T), E) * sc);
+  if (P.logits) P.logits[row] = f32_to_bf16_bits(l);
+  if (argmax_better(l, (int)row, best.v, best.i)) best.v = l, best.i = (int)row;
+}
 __device__ void lm_stage(const Params &P, const DStage *stab, int nstages, int W, int s, Ring &R, Cursor &cur,
-                         const int8_t *xd, int E, Best &best) {
+                         const int8_t *xd, int E, Best &best, long long *lm_part) {
   const DStage &sd = stab[s];
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int xs = x_stride(sd.k);
+  const int lo = lm_lo(sd, warp);
+  long long *slot_tile = lm_part + kLmSlots * 16;
+  if (lane < 2) slot_tile[2 * warp + lane] = -1;
+  int c4[4] = {0, 0, 0, 0};
+  float s0 = 0.f, s1 = 0.f;
   while (cur.s == s) {
-    const int tl = cur.i / sd.nk;
-    const int64_t tile = blockIdx.x + (int64_t)W * tl;
-    const int64_t r0 = tile * 16 + g, r1 = r0 + 8;
-    float s0 = 0.f, s1 = 0.f;
-    if (t == 0) s0 = scale_of(P, raw_scale(P, sd.s, r0)), s1 = scale_of(P, raw_scale(P, sd.s, r1));
-    int c4[4] = {0, 0, 0, 0};
-    for (int c = 0; c < sd.nk; ++c) {
-      consume(P, stab, nstages, W, R, xd, c, xs, c4);
-      refill(P, stab, nstages, W, R);
-      cur_next(stab, nstages, cur);
+    const int i = cur.i;
+    const int tl = i / sd.nk, c = i - tl * sd.nk;
+    if ((c == 0 || i == lo) && t == 0) {  // the tile's scales, requested before its items
+      const int64_t tile = blockIdx.x + (int64_t)W * tl;
+      s0 = scale_of(P, raw_scale(P, sd.s, tile * 16 + g)), s1 = scale_of(P, raw_scale(P, sd.s, tile * 16 + g + 8));
     }
+    consume(P, stab, nstages, W, R, xd, c, xs, c4);
+    refill(P, stab, nstages, W, R);
+    cur_next(stab, nstages, cur);
+    const bool range_end = cur.s != s;
+    if (c != sd.nk - 1 && !range_end) continue;
     long long T0, T1;
     fold_planes(c4, T0, T1);
-    if (t != 0) continue;
-    const float l0 = round_bf16(ps::mul_pow2(__ll2float_rn(T0), E) * s0);
-    const float l1 = round_bf16(ps::mul_pow2(__ll2float_rn(T1), E) * s1);
-    if (P.logits) {
-      P.logits[r0] = f32_to_bf16_bits(l0);
-      P.logits[r1] = f32_to_bf16_bits(l1);
+    c4[0] = c4[1] = c4[2] = c4[3] = 0;
+    const bool whole = tl * sd.nk >= lo && c == sd.nk - 1;
+    if (whole) {
+      if (t == 0) {
+        lm_finish(P, sd, W, tl, g, T0, E, s0, best);
+        lm_finish(P, sd, W, tl, g + 8, T1, E, s1, best);
+      }
+    } else {
+      const int slot = tl * sd.nk < lo ? 2 * warp : 2 * warp + 1;
+      if (t == 0) lm_part[slot * 16 + g] = T0, lm_part[slot * 16 + g + 8] = T1;
+      if (lane == 0) slot_tile[slot] = tl;
     }
-    if (argmax_better(l0, (int)r0, best.v, best.i)) best.v = l0, best.i = (int)r0;
-    if (argmax_better(l1, (int)r1, best.v, best.i)) best.v = l1, best.i = (int)r1;
+  }
+  csync();  // every partial row sum is in shared memory
+  if (warp == 0) {
+    // the slots in order hold the partial tiles in item order, so the parts of one tile are consecutive
+    const int r = lane & 15;
+    long long acc = 0;
+    int cur_tile = -1;
+    for (int sl = 0; sl < kLmSlots; ++sl) {
+      const int tile_id = (int)slot_tile[sl];
+      if (tile_id < 0) continue;
+      if (tile_id != cur_tile) {
+        if (cur_tile >= 0 && lane < 16) {
+          const int64_t tile = blockIdx.x + (int64_t)W * cur_tile;
+          lm_finish(P, sd, W, cur_tile, r, acc, E, scale_of(P, raw_scale(P, sd.s, tile * 16 + r)), best);
+        }
+        cur_tile = tile_id;
+        acc = 0;
+      }
+      acc += lm_part[sl * 16 + r];
+    }
+    if (cur_tile >= 0 && lane < 16) {
+      const int64_t tile = blockIdx.x + (int64_t)W * cur_tile;
+      lm_finish(P, sd, W, cur_tile, r, acc, E, scale_of(P, raw_scale(P, sd.s, tile * 16 + r)), best);
+    }
   }
 }
 
@@ -1119,7 +1165,7 @@ __global__ void __launch_bounds__(kCT, 1) dataflow_step_kernel(const __grid_cons
       const int E = stage_input(P.ll + (int64_t)P.L * M.LW, nullptr, P.H, tag_of(P, epoch, P.L - 1, 4), &nw, P.eps,
                                 xd, redd, redf);
       if (TRACE && blockIdx.x == 0) stamp<TRACE>(P, 1 + 5 * P.L);
-      lm_stage(P, stab, nstages, W, 4 * P.L, R, cur, xd, E, best);
+      lm_stage(P, stab, nstages, W, 4 * P.L, R, cur, xd, E, best, part);
     }
     // every issued copy has landed before the CTA exits (normally the warp consumed all of them)
     if (lane == 0) {
@@ -1307,7 +1353,7 @@ static bool layout(const egpt_qwen3_plan *Pl, Layout &lo) {
   const int L = Pl->n_layers, D = Pl->head_dim, grp = Pl->n_q_heads / Pl->n_kv_heads;
   const int64_t kmax = std::max<int64_t>({(int64_t)Pl->hidden, (int64_t)Pl->intermediate, (int64_t)Pl->n_q_heads * D});
   const size_t ab = D == 32 ? attn_bytes<1, 2>() : grp == 2 ? attn_bytes<4, 2>() : attn_bytes<4, 4>();
-  lo.part = (int)part_bytes(Pl, W);
+  lo.part = (int)std::max(part_bytes(Pl, W), (kLmPartBytes + 127) / 128 * 128);  // also the lm_head's partial tiles
   lo.ubytes = (int)std::max<size_t>((4 * (size_t)x_stride(kmax) + 127) / 128 * 128, ab);
   const size_t limit = smem_limit();  // the kernel has no static shared memory
   const size_t fixed0 = 512 + ((size_t)(4 * L + 1) * sizeof(DStage) + 127) / 128 * 128 + (size_t)lo.part +
