@@ -719,7 +719,7 @@ def run_attn_sweep(a):
                                                        ref_softmax=ref), a.reps)
             nbytes = 4096 * length + 8192
             gbs = nbytes / (us * 1e-6) / 1e9
-            print(json.dumps({'kernel': 'attn_split_kernel' if ref else 'attn_stream_kernel',
+            print(json.dumps({'kernel': 'attn_block_max_kernel + attn_stream_kernel' if ref else 'attn_stream_kernel',
                               'case': f'config 4 L={length}' + (' ref_softmax' if ref else ''),
                               'us': round(us, 3), 'bytes': nbytes, 'achieved_gbs': round(gbs, 1), 'peak_gbs': peak,
                               'frac': round(gbs / peak, 4), 'peak_source': src,

@@ -706,7 +706,7 @@ extern "C" size_t egpt_attn_ws_bytes(int64_t m, int nq, int nkv, int d, int max_
 
 namespace egpt {
 // The streamed single-row kernel (attn_stream.cu): which calls it takes, and its launch.
-bool attn_stream_applies(int64_t m, int d, int dtype, unsigned flags, int grp);
+bool attn_stream_applies(const AttnParams &p, int64_t m, int d, int dtype, unsigned flags);
 cudaError_t attn_stream_launch(AttnParams p, cudaStream_t st, bool pdl);
 }  // namespace egpt
 
@@ -760,7 +760,7 @@ extern "C" int egpt_attn_decode(void *out, int64_t ldo, const void *q, int64_t l
   p.flags = flags;
   const dim3 grid(nkv, p.split_cap, (unsigned)m);
   const bool pdl = (flags & EGPT_FLAG_PDL) != 0;
-  if (attn_stream_applies(m, d, dtype, flags, p.group))  // one bf16 row, head_dim 128: K/V streamed by bulk copies
+  if (attn_stream_applies(p, m, d, dtype, flags))  // one bf16 row, head_dim 128: K/V streamed by bulk copies
     return check_launch(attn_stream_launch(p, (cudaStream_t)stream, pdl), "attn_stream_kernel");
   cudaError_t e;
   const bool bf = dtype == EGPT_BF16;

@@ -140,8 +140,10 @@ EGPT_API int egpt_embed(void *out, const int64_t *ids, int64_t rows, const void 
  *   bf16: probabilities enter P.V rounded to bf16. With EGPT_FLAG_REF_SOFTMAX they are rounded relative to
  *   the running maximum of the 128-key block walk of the reference's GPU SDPA kernel (a range then rescores
  *   the keys before it); without it each range starts its own walk (same accuracy, less work). One bf16 row
- *   (m = 1) with d = 128 and none of APPEND / RAGGED / REF_SOFTMAX streams the cache through shared memory with
- *   bulk copies (one CTA per SM over the grid; the same workspace).
+ *   (m = 1) with d = 128 and neither APPEND nor RAGGED streams the cache through shared memory with bulk copies
+ *   (one CTA per SM over the grid; the same workspace; with REF_SOFTMAX a first pass over K writes the 128-key
+ *   block maxima into the workspace's unused partial slots, and calls whose workspace lacks the room for the
+ *   maxima of cap keys run the split kernel).
  *   dtype: bf16 (Qwen) or fp32 (nanoGPT, no norm/RoPE). */
 EGPT_API int egpt_qk_norm_rope_kv_append(void *q_out, const void *qkv, int64_t ldqkv, void *k_cache, void *v_cache,
                                 int64_t cap, const int64_t *position, int64_t m, int nq, int nkv, int d,

@@ -101,9 +101,9 @@ def test_never_reads_past_position(cuda):
 
 def test_multi_row_causal_matches_rowwise(cuda):
     """Prefill rows: row i attends to [0, pos0 + i]; equals one decode call per row. The one-row calls take the
-    streamed kernel and the multi-row call the split kernel (fp32 sums and bf16 probabilities against other
-    running maxima): within the tolerance that split counts are held to; with the reference-rounding flag (which
-    keeps single rows on the split kernel) bit-identical."""
+    streamed kernels and the multi-row call the split kernel (fp32 sums in other orders, and without the
+    reference-rounding flag bf16 probabilities against other running maxima): within the tolerance that split
+    counts are held to, with and without the flag."""
     L, ops = _ops()
     cap, m = 96, 9
     g = torch.Generator(device='cuda').manual_seed(4)
@@ -118,7 +118,7 @@ def test_multi_row_causal_matches_rowwise(cuda):
         torch.testing.assert_close(out[i:i + 1].float(), one.float(), atol=4e-3, rtol=1e-2)
         one_ref = ops.attn_decode(q[i:i + 1].contiguous(), k, v, pos0 + i, NQ, NKV, D, scale=SCALE, max_split=4,
                                   ref_softmax=True)
-        assert torch.equal(ref[i:i + 1], one_ref), i
+        torch.testing.assert_close(ref[i:i + 1].float(), one_ref.float(), atol=4e-3, rtol=1e-2)
 
 
 def _norm_rope_setup(cuda, cap=64):
@@ -156,9 +156,9 @@ def test_qk_norm_rope_append_vs_oracle(cuda):
 
 
 def test_fused_append_equals_separate_kernels(cuda):
-    """The in-kernel q/k-norm + RoPE + append (EGPT_FLAG_APPEND) writes the same cache rows as the separate kernel and
-    gives the same output: bit for bit with the reference rounding (both on the split kernel), within the split-count
-    tolerance without it (the separate one-row call then takes the streamed kernel)."""
+    """The in-kernel q/k-norm + RoPE + append (EGPT_FLAG_APPEND) writes the same cache rows as the separate kernel,
+    bit for bit, and gives the same output within the split-count tolerance (the separate one-row call takes the
+    streamed kernels, the fused one the split kernel), with and without the reference rounding."""
     L, ops = _ops()
     cap = 200
     qkv, qn, kn, cos, sin = _norm_rope_setup(cuda, cap)
@@ -178,7 +178,7 @@ def test_fused_append_equals_separate_kernels(cuda):
         sep = ops.attn_decode(q, kb, vb, pos, NQ, NKV, D, scale=SCALE, max_split=ms)
         sep_ref = ops.attn_decode(q, kb, vb, pos, NQ, NKV, D, scale=SCALE, max_split=ms, ref_softmax=True)
         assert torch.equal(ka, kb) and torch.equal(va, vb), p
-        assert torch.equal(fused_ref, sep_ref), (p, ms)
+        torch.testing.assert_close(fused_ref.float(), sep_ref.float(), atol=4e-3, rtol=1e-2)
         torch.testing.assert_close(fused.float(), sep.float(), atol=4e-3, rtol=1e-2)
 
 
