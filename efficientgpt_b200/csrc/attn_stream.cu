@@ -19,8 +19,9 @@
 // score in one lane; the warp keeps a running maximum, sum and P.V accumulator per q head (lane l: dims
 // 4l .. 4l + 3; probabilities enter P.V rounded to bf16, the sums use the fp32 values) and releases the stage.
 // The warps merge in a fixed order; one range writes the output, several write partials (maximum, sum,
-// unnormalised output, base-2 exponents) and the last range of the kv head to arrive combines them. Every wait
-// is bounded (EGPT_ERR_TIMEOUT); the producer drains its copies before the CTA exits.
+// unnormalised output; base-2 exponents, or natural ones with the reference rounding) and the last range of the kv
+// head to arrive combines them. Every wait is bounded (EGPT_ERR_TIMEOUT); the copy warp drains its copies before
+// the CTA exits, and the block-maximum pass's compute warps take every named barrier whatever their waits returned.
 #include "internal.h"
 #include "common.cuh"
 
@@ -39,9 +40,9 @@ constexpr int kThreads = (kWarps + 1) * 32; // + the copy warp
 template <int GRP>
 struct Smem {
   uint8_t ring[kStages][2][kBlockBytes];  // [stage][K | V][128 rows of 256 bytes]
-  float q[GRP][kD];                       // q heads, pre-scaled by scale log2(e)
+  float q[GRP][kD];                       // q heads (pre-scaled by scale log2(e) without the reference rounding)
   float w_m[kWarps][GRP], w_l[kWarps][GRP];
-  float w_acc[kWarps][GRP][kD];
+  float w_acc[kWarps][GRP][kD];           // (the block-maximum pass keeps its per-warp maxima here)
   uint64_t full[kStages], empty[kStages];
   int flag;
 };
