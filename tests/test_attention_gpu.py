@@ -220,3 +220,31 @@ def test_single_row_group_sizes_vs_fp64(cuda, nq, nkv, length):
     err = float((out.double() - truth).abs().max())
     assert err <= 2e-3 or length < 512, (nq, length, err)  # short contexts: O(1) outputs, bf16 output rounding
     assert err <= max(2 * float((sdpa.double() - truth).abs().max()), 1e-3), (nq, length, err)
+
+
+@pytest.mark.parametrize('nq,nkv', [(8, 8), (32, 8)])
+@pytest.mark.parametrize('length', [130, 3000])
+def test_single_row_ref_softmax_group_sizes_vs_oracle(cuda, nq, nkv, length):
+    """The reference rounding on the one-row streamed kernels (block-maximum pass, then the attention pass) with 1
+    and 4 q heads per kv head: the oracle's 128-key block walk to one bf16 ulp plus the fp32-noise allowance of
+    test_ref_softmax_matches_oracle_block_walk, nearly all outputs identical."""
+    L, ops = _ops()
+    g = torch.Generator(device='cuda').manual_seed(3 * length + nq)
+    cap = 3072
+    q = torch.randn(1, nq * D, device=cuda, generator=g).to(torch.bfloat16)
+    k = torch.randn(nkv, cap, D, device=cuda, generator=g).to(torch.bfloat16)
+    v = torch.randn(nkv, cap, D, device=cuda, generator=g).to(torch.bfloat16)
+    pos = torch.tensor([length - 1], device=cuda)
+    out = from_torch(ops.attn_decode(q, k, v, pos, nq, nkv, D, scale=SCALE, max_split=64,
+                                     ref_softmax=True)).reshape(nq, D)
+    qn, kn, vn = from_torch(q).reshape(nq, D), from_torch(k), from_torch(v)
+    want = round_bf16(attn_ref.decode_attention_fp32(qn, kn, vn, length, SCALE, p_bf16=True,
+                                                     block=attn_ref.REF_KEY_BLOCK))
+    grp = nq // nkv
+    tol = np.empty((nq, 1))
+    for h in range(nq):
+        sc = (kn[h // grp, :length].astype(np.float64) @ qn[h]) * SCALE
+        tol[h] = 4 * 2.0 ** -8 * np.abs(vn[h // grp, :length]).max() / np.exp(sc - sc.max()).sum()
+    diff = np.abs(out - want)
+    assert (diff <= np.abs(want) * 2.0 ** -7 + tol).all(), (nq, length)
+    assert (diff == 0).mean() > 0.98, (nq, length, float((diff == 0).mean()))
