@@ -444,12 +444,14 @@ extern "C" int egpt_attn_prefill(void *out, int64_t ldo, const void *q, int64_t 
   A.out = (uint16_t *)out, A.ldo = ldo, A.m = m, A.pos0 = pos0, A.nq = nq, A.nkv = nkv;
   A.nqb = (int)((m + apf::kBQ - 1) / apf::kBQ);
   A.scale_log2 = scale * 1.4426950408889634f;
-  static bool attr = false;
-  if (!attr) {
+  static int configured[64] = {0};  // the shared-memory opt-in, per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
     const cudaError_t e = cudaFuncSetAttribute(apf::attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                (int)apf::kSmem);
     if (e != cudaSuccess) return check_launch(e, "attn_prefill (shared memory attribute)");
-    attr = true;
+    configured[dev] = 1;
   }
   const unsigned grid = (unsigned)((int64_t)nq * A.nqb);
   apf::attn_prefill_kernel<<<grid, apf::kThreads, apf::kSmem, (cudaStream_t)stream>>>(A);

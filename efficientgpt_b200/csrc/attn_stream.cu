@@ -410,15 +410,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_stream_kernel(AttnParams p) 
 
 template <int GRP, bool REF>
 cudaError_t launch_grp(const AttnParams &p, cudaStream_t st, bool pdl) {
-  static bool attr = false;
+  static int configured[64] = {0};  // the shared-memory opt-in, per device
   const size_t smem = sizeof(Smem<GRP>) + 128;
-  if (!attr) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(attn_stream_kernel<GRP, REF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e == cudaSuccess && REF)
       e = cudaFuncSetAttribute(attn_block_max_kernel<GRP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    attr = true;
+    configured[dev] = 1;
   }
   const dim3 grid(p.nkv, p.split_cap);
   if (REF) {  // block maxima first; the attention pass follows in stream order

@@ -459,12 +459,14 @@ extern "C" int egpt_gemm_i8_tc(void *y, int64_t ldy, const void *x, int64_t ldx,
   const int S = gtc::choose_ksplit(M, N, K, num_sms());
   if (S > 1 && ws && ws_bytes >= (size_t)S * M * N * 4 && (uintptr_t)ws % 16 == 0 && N % 2 == 0)
     A.ksplit = S, A.ws = (float *)ws;
-  static bool attr = false;
-  if (!attr) {
+  static int configured[64] = {0};  // the shared-memory opt-in, per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
     const cudaError_t e = cudaFuncSetAttribute(gtc::gemm_i8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                (int)gtc::kSmem);
     if (e != cudaSuccess) return check_launch(e, "gemm_i8_tc (shared memory attribute)");
-    attr = true;
+    configured[dev] = 1;
   }
   const int64_t units = ((N + gtc::kBN - 1) / gtc::kBN) * ((M + gtc::kBM - 1) / gtc::kBM) * A.ksplit;
   const unsigned grid = (unsigned)std::min<int64_t>(units, (int64_t)num_sms());  // persistent: one CTA per SM
